@@ -1,0 +1,395 @@
+#!/usr/bin/env python
+"""bench.py -- IQ4_XS decode GEMV sweep on B200 (BASELINE.json metric: IQ4_XS GEMV HBM GB/s).
+
+Workload (one GPU): one step = the decode GEMV of every 27B-class layer
+shape -- q_proj 8192x5120, k_proj 1024x5120, v_proj 1024x5120, o_proj 5120x8192, gate|up fused
+34816x5120, down 5120x17408 (out x in) -- at batch 1, 2, 4 and 8 (24 GEMVs, each a Q8_1 quantize
+plus the GEMV kernel).  Weights: fp32 N(0, 0.02) from fixed seeds quantised to IQ4_XS on the device;
+activations fp32 N(0, 1).  Two copies of the layer weights (384 MB, > 3x the 126 MB L2) alternate
+between steps and the 24 GEMVs of a step stream 768 MB, so every weight byte comes from HBM.
+
+value  = algorithmic bytes (sum over GEMVs of N*K*17/32 + 4*B*K + 4*B*N) / device time, all ranks
+         (each rank runs the full step on its own weights: weak scaling), inputs resident in HBM,
+         the step replayed as a CUDA graph.
+e2e    = same metric through the reference-facing ggml hook (custom_gemv_iq4xs_dispatch_batched)
+         called from a C++ host loop, with the step's activations copied from pinned host memory
+         and every output copied back, per GEMV, inside the timed region.
+roofline = the GEMV kernel alone (quantizer excluded), timed per launch with CUDA events on its
+         stream, against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+--impl reference: the reference's own CPU path (kernels/matmul_iq4xs/ref_cpu.cpp, compiled unchanged
+         into oracle/_ref/) on the host cores, same metric on a bounded row sample.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+
+SHAPES = [  # (name, N out, K in)
+    ("q_proj", 8192, 5120),
+    ("k_proj", 1024, 5120),
+    ("v_proj", 1024, 5120),
+    ("o_proj", 5120, 8192),
+    ("gate_up", 34816, 5120),
+    ("down", 5120, 17408),
+]
+BATCHES = [1, 2, 4, 8]
+FALLBACK_HBM_GBS = 6650.0
+
+
+def gemv_bytes(N: int, K: int, B: int) -> int:
+    return N * K * 17 // 32 + 4 * B * K + 4 * B * N
+
+
+def step_bytes() -> int:
+    return sum(gemv_bytes(N, K, B) for B in BATCHES for _, N, K in SHAPES)
+
+
+def load_pkg():
+    spec = importlib.util.spec_from_file_location("_iq4xs_loader", ROOT / "qwen_3.8_27b_optimizations_b200" / "loader.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.load()
+
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "gemv_ncu_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return None
+    return None
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- reference arm (CPU)
+def cpu_sample_plan(rows_per_shape: int):
+    return [(name, min(N, rows_per_shape), K) for name, N, K in SHAPES]
+
+
+def run_cpu_reference(threads: int, rows_per_shape: int, steps: int, warmup: int):
+    """The reference's gemv_iq4xs_cpu_ref (FP64, unquantised x) over a row sample of every shape,
+    every batch size (one call per token, as the reference's CPU path has no batch), row slices
+    spread over `threads` host threads.  Returns (GB/s, seconds per step, sample text)."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+
+    plan = cpu_sample_plan(rows_per_shape)
+    rng = np.random.default_rng(0)
+    mats = {}
+    for name, n, K in plan:
+        W = O.random_blocks(K, n, 1000 + [s[0] for s in SHAPES].index(name))
+        xs = [rng.standard_normal(K).astype(np.float32) for _ in range(max(BATCHES))]
+        mats[name] = (W, xs, n, K)
+
+    def one_step():
+        for B in BATCHES:
+            for name, n, K in plan:
+                W, xs, _, _ = mats[name]
+                for b in range(B):
+                    O.ref_gemv_threaded(W, xs[b], K, n, threads)
+
+    for _ in range(warmup):
+        one_step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_step()
+    dt = (time.perf_counter() - t0) / max(steps, 1)
+    nbytes = sum(gemv_bytes(n, K, B) for B in BATCHES for _, n, K in plan)
+    sample = (f"first {rows_per_shape} rows of each of the 6 shapes (all rows of k/v), batch 1/2/4/8 "
+              f"(one FP64 gemv_iq4xs_cpu_ref call per token), rows split over {threads} threads")
+    return nbytes / dt / 1e9, dt, sample
+
+
+def reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    if not O.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_cpu.so not built"}))
+        return 0
+    threads = O.host_threads()
+    gbs, dt, sample = run_cpu_reference(threads, args.cpu_rows, args.steps, args.warmup)
+    line = {
+        "impl": "reference",
+        "metric": "IQ4_XS decode GEMV sweep HBM GB/s", "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (reference random-byte IQ4_XS blocks, N(0,1) activations)",
+        "config": {"workload": "decode_gemv_sweep_27b_layers", "shapes": {n: [N, K] for n, N, K in SHAPES},
+                   "batches": BATCHES, "path": "kernels/matmul_iq4xs/ref_cpu.cpp gemv_iq4xs_cpu_ref (unchanged)"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-rows", type=int, default=256, help="rows per shape in the CPU samples")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=0, help="default: same as --steps")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local_rank))
+    P = load_pkg()
+    L = P.lib()
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device=dev)
+
+    # ---- data (2 weight copies alternate between steps)
+    weights = [[P.random_weights(N, K, seed=1000 + 97 * c + i + 7919 * rank) for i, (_, N, K) in enumerate(SHAPES)]
+               for c in range(2)]
+    X = {(B, i): P.fill_normal(B * K, seed=42 + B + 31 * i + 7919 * rank).view(B, K)
+         for B in BATCHES for i, (_, N, K) in enumerate(SHAPES)}
+    Y = {(B, i): torch.empty((B, N), dtype=torch.float32, device=dev) for B in BATCHES for i, (_, N, K) in enumerate(SHAPES)}
+    maxK = max(K for _, _, K in SHAPES)
+    ws = torch.empty(P.gemv_workspace_bytes(maxK, max(BATCHES)), dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    def step(c: int, s):
+        for B in BATCHES:
+            for i, (_, N, K) in enumerate(SHAPES):
+                P.gemv(weights[c][i], X[(B, i)], N, workspace=ws, out=Y[(B, i)], stream=s)
+
+    # capture one graph per weight copy
+    graphs = []
+    with torch.cuda.stream(stream):
+        step(0, stream)
+        step(1, stream)
+        stream.synchronize()
+        for c in range(2):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(c, stream)
+            graphs.append(g)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    # ---- warmup
+    with torch.cuda.stream(stream):
+        for w in range(args.warmup):
+            graphs[w % 2].replay()
+    stream.synchronize()
+
+    # ---- timed region (value)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for k in range(args.steps):
+                graphs[k % 2].replay()
+            e1.record(stream)
+        stream.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    sb = step_bytes()
+    value_gbs = world * sb * args.steps / (ms_max * 1e-3) / 1e9
+    clocks = clk.summary()
+
+    # ---- roofline: the GEMV kernel alone, per launch, on its stream
+    per = []
+    q8s = {(B, i): P.q8_1_quantize(X[(B, i)], stream=stream) for B in BATCHES for i in range(len(SHAPES))}
+    stream.synchronize()
+    reps = 20
+    tot_bytes, tot_ms = 0, 0.0
+    with torch.cuda.stream(stream):
+        for B in BATCHES:
+            for i, (name, N, K) in enumerate(SHAPES):
+                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+                for r in range(reps):
+                    a, b = evs[r]
+                    a.record(stream)
+                    P.gemv_q8(weights[r % 2][i], q8s[(B, i)], K, N, B, out=Y[(B, i)], stream=stream)
+                    b.record(stream)
+                stream.synchronize()
+                d = statistics.median([a.elapsed_time(b) for a, b in evs[2:]])
+                nb = gemv_bytes(N, K, B)
+                per.append({"shape": name, "B": B, "us": round(d * 1e3, 2), "gbs": round(nb / (d * 1e-3) / 1e9, 1)})
+                tot_bytes += nb
+                tot_ms += d
+    achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
+    peak, peak_kind = hbm_peak()
+    traffic = ncu_traffic()
+
+    # ---- e2e through the ggml hook from the C++ host loop, pinned host buffers
+    e2e_steps = args.e2e_steps or args.steps
+    wptrs = (C.c_void_p * len(SHAPES))(*[w.data_ptr() for w in weights[0]])
+    Ks = (C.c_int64 * len(SHAPES))(*[K for _, _, K in SHAPES])
+    Ns = (C.c_int64 * len(SHAPES))(*[N for _, N, _ in SHAPES])
+    Bs = (C.c_int64 * len(BATCHES))(*BATCHES)
+    maxN = max(N for _, N, _ in SHAPES)
+    hx = torch.empty(max(BATCHES) * maxK, dtype=torch.float32).pin_memory()
+    hx.normal_()
+    hy = torch.empty(max(BATCHES) * maxN, dtype=torch.float32).pin_memory()
+    dx = torch.empty(max(BATCHES) * maxK, dtype=torch.float32, device=dev)
+    dy = torch.empty(max(BATCHES) * maxN, dtype=torch.float32, device=dev)
+    ems = C.c_float(0.0)
+    rc = L.iq4xs_bench_e2e_gemv(wptrs, Ks, Ns, len(SHAPES), Bs, len(BATCHES), hx.data_ptr(), hy.data_ptr(),
+                                dx.data_ptr(), dy.data_ptr(), max(args.warmup, 3), stream.cuda_stream, C.byref(ems))
+    if rc != 0:
+        raise RuntimeError(f"e2e warmup failed: cudaError {rc}")
+    barrier()
+    rc = L.iq4xs_bench_e2e_gemv(wptrs, Ks, Ns, len(SHAPES), Bs, len(BATCHES), hx.data_ptr(), hy.data_ptr(),
+                                dx.data_ptr(), dy.data_ptr(), e2e_steps, stream.cuda_stream, C.byref(ems))
+    if rc != 0:
+        raise RuntimeError(f"e2e failed: cudaError {rc}")
+    t = torch.tensor([float(ems.value)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_gbs = world * sb * e2e_steps / (float(t.item()) * 1e-3) / 1e9
+    h2d = sum(4 * B * K for B in BATCHES for _, _, K in SHAPES)
+    d2h = sum(4 * B * N for B in BATCHES for _, N, _ in SHAPES)
+
+    torch.cuda.synchronize()
+    err = P.device_error()
+    if err:
+        raise RuntimeError(f"device error word {err}")
+
+    # ---- CPU baseline (rank 0, one GPU only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT))
+        from oracle import oracle as O
+        if O.ref_available():
+            threads = O.host_threads()
+            gbs, _, sample = run_cpu_reference(threads, args.cpu_rows, 2, 1)
+            cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference", "sample": sample}
+
+    for g in graphs:
+        del g
+    graphs.clear()
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+    if rank == 0:
+        line = {
+            "metric": "IQ4_XS decode GEMV sweep HBM GB/s", "value": round(value_gbs, 1), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic: fp32 N(0,0.02) weights quantised to IQ4_XS on device, fp32 N(0,1) activations",
+            "config": {"workload": "decode_gemv_sweep_27b_layers", "shapes": {n: [N, K] for n, N, K in SHAPES},
+                       "batches": BATCHES, "gemvs_per_step": len(SHAPES) * len(BATCHES),
+                       "bytes_per_step": sb, "l2": "inputs larger than L2: 2 x 192 MB weight sets alternate, 768 MB streamed per step",
+                       "timing": "CUDA graph replay of the step, CUDA events on the launch stream, max over ranks"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic.get("bytes_per_launch_weighted") if traffic else None,
+                         "kernel": "gemv_iq4xs_q8_kernel", "per_launch": per},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "custom_gemv_iq4xs_dispatch_batched from a C++ host loop, pinned host x/y"},
+            "gpu_launches": args.steps * len(SHAPES) * len(BATCHES) * 2,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

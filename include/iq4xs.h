@@ -1,0 +1,146 @@
+/*
+ * iq4xs.h -- C ABI of the B200 (sm_100a) IQ4_XS x Q8_1 matmul library (libiq4xs_b200.so).
+ *
+ * Drop-in boundary for the reference's matmul_iq4xs harness and its ggml MUL_MAT hook.  Every
+ * entry point takes plain device pointers, sizes and a CUDA stream; nothing allocates on the
+ * hot path (the caller passes the workspace), nothing synchronises, nothing aborts.  Status
+ * codes instead of exceptions.  Citations are file:line in the reference project.
+ *
+ * Formats (bit-compatible with the reference / ggml):
+ *   IQ4_XS  weight row n of a K-column matrix: K/256 super-blocks of 136 bytes
+ *           {fp16 d, u16 scales_h, u8 scales_l[4], u8 qs[128]}   (kernels/common/block_iq4_xs.h:10-19)
+ *   Q8_1    activation block of 32 values: 36 bytes {fp16 d, fp16 sum, int8 q[32]}
+ *           (kernels/matmul_iq4xs/real_stock_dp4a_comparator.hip:22-26), fp16 by truncation.
+ *   Activations X are token-major fp32 [M][K] (ggml src1), outputs Y are [M][N] (ggml dst),
+ *   except where an entry point says it keeps the reference playground's [K][M] / [N][M].
+ *
+ * Constraints: K > 0, K % 256 == 0; N > 0; 1 <= B <= 8 for the GEMV entry points; pointers to
+ * device memory (W 8-byte aligned; 16-byte alignment and K % 512 == 0 select the bulk-copy path).
+ */
+#ifndef IQ4XS_H
+#define IQ4XS_H
+
+#include <cuda_runtime_api.h>
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------------------------ */
+/* Status codes (0 = success).  Argument checks mirror impl_gemv_dp4a_gfx1100.hip:299-300
+ * (null pointers, K % 256, non-positive sizes -> invalid value) and :305 (grid overflow). */
+typedef enum {
+    IQ4XS_OK = 0,
+    IQ4XS_ERR_INVALID_ARGUMENT = 1,   /* null pointer or non-positive size */
+    IQ4XS_ERR_UNSUPPORTED_SHAPE = 2,  /* K % 256 != 0, batch outside 1..8, ... */
+    IQ4XS_ERR_MISALIGNED = 3,         /* pointer alignment below what the format needs */
+    IQ4XS_ERR_WORKSPACE_TOO_SMALL = 4,
+    IQ4XS_ERR_CUDA = 5,               /* launch or runtime error (cudaGetLastError) */
+    IQ4XS_ERR_DEVICE_TIMEOUT = 6,     /* a bounded device-side wait gave up (see iq4xs_device_error) */
+    IQ4XS_ERR_NOT_SUPPORTED = 7       /* operation unavailable in this configuration */
+} iq4xs_status;
+
+#define IQ4XS_QK_K 256
+#define IQ4XS_QK8_1 32
+#define IQ4XS_BLOCK_BYTES 136
+#define IQ4XS_Q8_1_BYTES 36
+#define IQ4XS_MAX_GEMV_BATCH 8
+#define IQ4XS_GGML_TYPE_IQ4_XS 23 /* ggml_type value of GGML_TYPE_IQ4_XS */
+
+const char* iq4xs_status_string(int status);
+int iq4xs_version(void); /* major*10000 + minor*100 + patch */
+
+/* Reads the current device's error word set by bounded device waits and clears it.
+ * *code = 0 when no kernel gave up since the last call. */
+int iq4xs_device_error(uint32_t* code);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Q8_1 activation quantizer.
+ * Replaces quantize_row_q8_1_gpu (real_stock_dp4a_comparator.hip:266-273; kernel :230-264) and the
+ * coop quantizer (impl_gemv_dp4a_gfx1100.hip:138-168).  X fp32 [M][K] -> q8 [M][K/32] blocks.
+ * d = amax/127 (IEEE), q = roundf(x/d), ds = {trunc16(d), trunc16(sum)}; bit-exact. */
+int iq4xs_q8_1_quantize(const float* X, void* q8, int64_t K, int64_t M, cudaStream_t stream);
+
+/* Bytes of Q8_1 blocks for M tokens of K values. */
+size_t iq4xs_q8_1_bytes(int64_t K, int64_t M);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Decode GEMV on pre-quantised activations, batch B = 1..8:
+ *   Y[b][n] = sum_k W[n][k] * x_b[k]  with the reference's per-sub-block integer pipeline.
+ * Replaces gemv_iq4xs_dp4a_gfx1100_prequantized_gpu (impl_gemv_dp4a_gfx1100.hip:291-308) and the
+ * patch's gemv_prequantized_cuh (patches/0001-gfx1100-mul-mat-custom.patch:261-266), both batch 1;
+ * batch 2..8 is new (the reference routes it to stock MMVQ, patch:275).
+ * q8: [B][K/32] Q8_1 blocks (iq4xs_q8_1_quantize output).  Y: fp32 [B][N]. */
+int iq4xs_gemv_q8(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B,
+                  cudaStream_t stream);
+
+/* Decode GEMV on fp32 activations X [B][K]: quantise into `workspace`, then GEMV (the GEMV is
+ * launched with programmatic dependent launch so its weight stream overlaps the quantizer).
+ * Replaces gemv_iq4xs_dp4a_gfx1100_gpu (impl_gemv_dp4a_gfx1100.hip:310-329) and
+ * gemv_iq4xs_stock_dp4a_gpu (real_stock_dp4a_comparator.hip:480-503) without their per-call
+ * hipMalloc/hipFree: workspace >= iq4xs_gemv_workspace_bytes(K, B) bytes, 16-byte aligned. */
+int iq4xs_gemv_f32(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B,
+                   void* workspace, size_t workspace_bytes, cudaStream_t stream);
+size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t B);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Raw int32 sub-block dot products sum_j kvalues[q_j]*q8_j (before the (ls-32) factor) through
+ * the production GEMV kernel's own inner loop: S [B][N][K/32].  Debug / parity entry point for
+ * the bit-exact contract of vec_dot_iq4_xs_q8_1 (real_stock_dp4a_comparator.hip:145-160). */
+int iq4xs_debug_subblock_dots(const void* W, const void* q8, int32_t* S, int64_t K, int64_t N,
+                              int64_t B, cudaStream_t stream);
+
+/* Same as iq4xs_gemv_q8 but forcing the direct-load (non bulk-copy) kernel; for tests. */
+int iq4xs_gemv_q8_generic(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B,
+                          cudaStream_t stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Weight-side helpers (data generation, format tools).
+ * iq4xs_fill_normal: dst[i] = mean + std * N(0,1) from a counter-based generator (seeded).
+ * iq4xs_quantize_weights: fp32 [N][K] -> IQ4_XS rows; the upstream ggml quantize_row_iq4_xs
+ *   algorithm without importance matrix (the reference calls it from llama.cpp; not vendored).
+ * iq4xs_dequantize: IQ4_XS -> fp32 [N][K] (dequant_mat_iq4xs_cpu semantics, ref_cpu.cpp:115-139). */
+int iq4xs_fill_normal(float* dst, int64_t n, uint64_t seed, float mean, float stddev, cudaStream_t stream);
+int iq4xs_quantize_weights(const float* src, void* W, int64_t N, int64_t K, cudaStream_t stream);
+int iq4xs_dequantize(const void* W, float* out, int64_t K, int64_t N, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Reference-named entry points, same argument meaning, returning cudaError_t like the HIP
+ * originals return hipError_t.  The ones without a workspace argument use a library-owned
+ * per-(device, stream) workspace that is allocated on the first call of a given size outside
+ * stream capture; under capture with no cached workspace they return cudaErrorNotSupported
+ * (the reference refuses capture outright, patch:269). */
+
+/* impl_gemv_dp4a_gfx1100.hip:332-341 (the reference's extern "C" symbol), batch 1. */
+cudaError_t gemv_iq4xs_dp4a_coop_gpu(const void* W, const float* x, float* y, int64_t K, int64_t N,
+                                     cudaStream_t stream);
+/* real_stock_dp4a_comparator.hip:480-503, batch 1. */
+cudaError_t gemv_iq4xs_stock_dp4a_gpu(const void* W, const float* x, float* y, int64_t K, int64_t N,
+                                      cudaStream_t stream);
+/* real_stock_dp4a_comparator.hip:266-273: one token, x fp32 [K] -> y [K/32] Q8_1 blocks. */
+cudaError_t quantize_row_q8_1_gpu(const float* x, void* y, int64_t K, cudaStream_t stream);
+/* real_stock_dp4a_comparator.hip:308-315: playground layout X [K][M] (X[k*M+m]) -> Y [M][K/32]. */
+cudaError_t quantize_row_q8_1_batched_gpu(const float* X, void* Y, int64_t K, int64_t M, cudaStream_t stream);
+
+/* ggml MUL_MAT hook (patches/0001-gfx1100-mul-mat-custom.patch).  ggml layouts: W = src0 data
+ * (ne00 = K, ne01 = N), x/X = src1 fp32 [M][K], y/Y = dst fp32 [M][N].
+ * can_handle: patch:274-277 (GEMV) and :148-151 (GEMM); dispatch: :278-280 and :152-154.
+ * GEMV handles M = 1..8 (the patch: M == 1 and three fixed shapes); the batched dispatch is the
+ * M > 1 form of the same call.  Any non-success status lets the caller fall back to stock. */
+bool custom_gemv_iq4xs_can_handle(int64_t K, int64_t N, int64_t M, int type);
+cudaError_t custom_gemv_iq4xs_dispatch(const void* W, const float* x, float* y, int64_t K, int64_t N,
+                                       cudaStream_t stream);
+cudaError_t custom_gemv_iq4xs_dispatch_batched(const void* W, const float* x, float* y, int64_t K,
+                                               int64_t N, int64_t M, cudaStream_t stream);
+bool custom_gemm_iq4xs_can_handle(int64_t K, int64_t N, int64_t M, int type);
+cudaError_t custom_gemm_iq4xs_dispatch(const void* W, const float* X, float* Y, int64_t K, int64_t N,
+                                       int64_t M, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IQ4XS_H */

@@ -1,0 +1,33 @@
+/*
+ * iq4xs_bench.h -- host-side measurement driver exported by libiq4xs_b200.so.
+ *
+ * Not part of the matmul path: it is the C++ caller a ggml-style host would be, used by bench.py
+ * to time the reference-facing entry point end to end (pinned host inputs in, results back to
+ * the host, every step).  It has no counterpart in the reference, whose harness does the same
+ * from bench_gemv_dp4a.cpp with device-resident inputs.
+ */
+#ifndef IQ4XS_BENCH_H
+#define IQ4XS_BENCH_H
+
+#include <cuda_runtime_api.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Runs `steps` passes; one pass = for every batch size b in batches[0..nbatch) and every matrix i:
+ *   cudaMemcpyAsync(dev_x <- host_x, b*K[i] floats), custom_gemv_iq4xs_dispatch_batched(W[i], dev_x,
+ *   dev_y, K[i], N[i], b), cudaMemcpyAsync(host_y <- dev_y, b*N[i] floats).
+ * host_x / host_y must be pinned and large enough for the largest b*K / b*N.  *ms = elapsed
+ * device time between events recorded on `stream` before the first and after the last pass,
+ * with the stream synchronised at the end.  Returns 0 or the first failing cudaError_t. */
+int iq4xs_bench_e2e_gemv(const void* const* W, const int64_t* K, const int64_t* N, int nmat,
+                         const int64_t* batches, int nbatch, const float* host_x, float* host_y,
+                         float* dev_x, float* dev_y, int steps, cudaStream_t stream, float* ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,231 @@
+"""Python host side of the C ABI in include/iq4xs.h (ctypes over libiq4xs_b200.so).
+
+The names and argument meanings follow the reference harness (kernels/matmul_iq4xs) and its ggml
+hook; torch tensors are only the device-memory / stream plumbing.  There is no CPU fallback:
+loading fails loudly when the CUDA library is missing, and every non-zero status raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libiq4xs_b200.so"
+
+QK_K = 256
+QK8_1 = 32
+BLOCK_BYTES = 136
+Q8_1_BYTES = 36
+MAX_GEMV_BATCH = 8
+GGML_TYPE_IQ4_XS = 23
+
+STATUS = {
+    0: "ok", 1: "invalid argument", 2: "unsupported shape", 3: "misaligned pointer",
+    4: "workspace too small", 5: "CUDA error", 6: "device wait timed out", 7: "not supported",
+}
+
+# Every exported symbol of include/iq4xs.h with (restype, argtypes).
+_i64, _vp, _sz, _u64, _f, _i = C.c_int64, C.c_void_p, C.c_size_t, C.c_uint64, C.c_float, C.c_int
+SIGNATURES = {
+    "iq4xs_status_string": (C.c_char_p, [_i]),
+    "iq4xs_version": (_i, []),
+    "iq4xs_device_error": (_i, [C.POINTER(C.c_uint32)]),
+    "iq4xs_q8_1_quantize": (_i, [_vp, _vp, _i64, _i64, _vp]),
+    "iq4xs_q8_1_bytes": (_sz, [_i64, _i64]),
+    "iq4xs_gemv_q8": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "iq4xs_gemv_f32": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "iq4xs_gemv_workspace_bytes": (_sz, [_i64, _i64]),
+    "iq4xs_debug_subblock_dots": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "iq4xs_gemv_q8_generic": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "iq4xs_fill_normal": (_i, [_vp, _i64, _u64, _f, _f, _vp]),
+    "iq4xs_quantize_weights": (_i, [_vp, _vp, _i64, _i64, _vp]),
+    "iq4xs_dequantize": (_i, [_vp, _vp, _i64, _i64, _vp]),
+    "gemv_iq4xs_dp4a_coop_gpu": (_i, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "gemv_iq4xs_stock_dp4a_gpu": (_i, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "quantize_row_q8_1_gpu": (_i, [_vp, _vp, _i64, _vp]),
+    "quantize_row_q8_1_batched_gpu": (_i, [_vp, _vp, _i64, _i64, _vp]),
+    "custom_gemv_iq4xs_can_handle": (C.c_bool, [_i64, _i64, _i64, _i]),
+    "custom_gemv_iq4xs_dispatch": (_i, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "custom_gemv_iq4xs_dispatch_batched": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "custom_gemm_iq4xs_can_handle": (C.c_bool, [_i64, _i64, _i64, _i]),
+    "custom_gemm_iq4xs_dispatch": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+}
+# include/iq4xs_bench.h (measurement driver, not the matmul path)
+BENCH_SIGNATURES = {
+    "iq4xs_bench_e2e_gemv": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i, _vp, C.POINTER(C.c_float)]),
+}
+
+_lib = None
+
+
+class IQ4XSError(RuntimeError):
+    def __init__(self, fn: str, status: int, cuda: bool = False):
+        kind = "cudaError" if cuda else STATUS.get(status, "unknown status")
+        super().__init__(f"{fn} failed: {kind} ({status})")
+        self.status = status
+
+
+def lib():
+    """Load the CUDA library (raises if it was not built: there is no fallback path)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing; build it with __graft_entry__.build()")
+        L = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in {**SIGNATURES, **BENCH_SIGNATURES}.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(fn: str, status: int, cuda: bool = False) -> None:
+    if status != 0:
+        raise IQ4XSError(fn, status, cuda)
+
+
+# ----------------------------------------------------------------------------- torch helpers
+def _torch():
+    import torch
+    return torch
+
+
+def _stream(stream=None) -> int:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _ptr(t) -> int:
+    return t.data_ptr()
+
+
+def weight_row_bytes(K: int) -> int:
+    return K // QK_K * BLOCK_BYTES
+
+
+def device_error() -> int:
+    code = C.c_uint32(0)
+    _check("iq4xs_device_error", lib().iq4xs_device_error(C.byref(code)))
+    return int(code.value)
+
+
+def q8_1_quantize(X, stream=None):
+    """fp32 [M][K] (cuda) -> uint8 [M][K/32*36] Q8_1 blocks."""
+    torch = _torch()
+    X = X.contiguous()
+    if X.dim() == 1:
+        X = X[None]
+    M, K = X.shape
+    q8 = torch.empty((M, K // QK8_1 * Q8_1_BYTES), dtype=torch.uint8, device=X.device)
+    _check("iq4xs_q8_1_quantize", lib().iq4xs_q8_1_quantize(_ptr(X), _ptr(q8), K, M, _stream(stream)))
+    return q8
+
+
+def gemv_q8(W, q8, K: int, N: int, B: int, out=None, stream=None, generic: bool = False):
+    """Y [B][N] fp32 from IQ4_XS W and pre-quantised activations q8 [B][K/32] blocks."""
+    torch = _torch()
+    Y = out if out is not None else torch.empty((B, N), dtype=torch.float32, device=W.device)
+    fn = lib().iq4xs_gemv_q8_generic if generic else lib().iq4xs_gemv_q8
+    _check("iq4xs_gemv_q8", fn(_ptr(W), _ptr(q8), _ptr(Y), K, N, B, _stream(stream)))
+    return Y
+
+
+def gemv_workspace_bytes(K: int, B: int) -> int:
+    return int(lib().iq4xs_gemv_workspace_bytes(K, B))
+
+
+def gemv(W, X, N: int, workspace=None, out=None, stream=None):
+    """Y [B][N] = W . X^T for fp32 activations X [B][K] (quantised on the fly into workspace)."""
+    torch = _torch()
+    X = X.contiguous()
+    if X.dim() == 1:
+        X = X[None]
+    B, K = X.shape
+    need = gemv_workspace_bytes(K, B)
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=X.device)
+    Y = out if out is not None else torch.empty((B, N), dtype=torch.float32, device=X.device)
+    _check("iq4xs_gemv_f32", lib().iq4xs_gemv_f32(_ptr(W), _ptr(X), _ptr(Y), K, N, B, _ptr(workspace),
+                                                  workspace.numel() * workspace.element_size(), _stream(stream)))
+    return Y
+
+
+def debug_subblock_dots(W, q8, K: int, N: int, B: int, stream=None):
+    """Raw int32 sub-block dots [B][N][K/32] from the production GEMV inner loop."""
+    torch = _torch()
+    S = torch.empty((B, N, K // QK8_1), dtype=torch.int32, device=W.device)
+    _check("iq4xs_debug_subblock_dots", lib().iq4xs_debug_subblock_dots(_ptr(W), _ptr(q8), _ptr(S), K, N, B, _stream(stream)))
+    return S
+
+
+def fill_normal(n: int, seed: int, mean: float = 0.0, std: float = 1.0, device="cuda", out=None, stream=None):
+    torch = _torch()
+    t = out if out is not None else torch.empty(n, dtype=torch.float32, device=device)
+    _check("iq4xs_fill_normal", lib().iq4xs_fill_normal(_ptr(t), n, seed, mean, std, _stream(stream)))
+    return t
+
+
+def quantize_weights(src, stream=None):
+    """fp32 [N][K] (cuda) -> IQ4_XS uint8 [N][K/256*136]."""
+    torch = _torch()
+    src = src.contiguous()
+    N, K = src.shape
+    W = torch.empty((N, weight_row_bytes(K)), dtype=torch.uint8, device=src.device)
+    _check("iq4xs_quantize_weights", lib().iq4xs_quantize_weights(_ptr(src), _ptr(W), N, K, _stream(stream)))
+    return W
+
+
+def random_weights(N: int, K: int, seed: int, std: float = 0.02, device="cuda", stream=None):
+    """fp32 N(0, std) weights drawn from `seed`, quantised to IQ4_XS on the device."""
+    torch = _torch()
+    src = fill_normal(N * K, seed, 0.0, std, device=device, stream=stream).view(N, K)
+    W = quantize_weights(src, stream=stream)
+    del src
+    return W
+
+
+def dequantize(W, K: int, N: int, stream=None):
+    torch = _torch()
+    out = torch.empty((N, K), dtype=torch.float32, device=W.device)
+    _check("iq4xs_dequantize", lib().iq4xs_dequantize(_ptr(W), _ptr(out), K, N, _stream(stream)))
+    return out
+
+
+# ----------------------------------------------------------------------------- reference-named
+def gemv_iq4xs_dp4a_coop_gpu(W, x, y, K: int, N: int, stream=None) -> None:
+    _check("gemv_iq4xs_dp4a_coop_gpu", lib().gemv_iq4xs_dp4a_coop_gpu(_ptr(W), _ptr(x), _ptr(y), K, N, _stream(stream)), True)
+
+
+def gemv_iq4xs_stock_dp4a_gpu(W, x, y, K: int, N: int, stream=None) -> None:
+    _check("gemv_iq4xs_stock_dp4a_gpu", lib().gemv_iq4xs_stock_dp4a_gpu(_ptr(W), _ptr(x), _ptr(y), K, N, _stream(stream)), True)
+
+
+def quantize_row_q8_1_gpu(x, y, K: int, stream=None) -> None:
+    _check("quantize_row_q8_1_gpu", lib().quantize_row_q8_1_gpu(_ptr(x), _ptr(y), K, _stream(stream)), True)
+
+
+def quantize_row_q8_1_batched_gpu(X_km, Y, K: int, M: int, stream=None) -> None:
+    _check("quantize_row_q8_1_batched_gpu", lib().quantize_row_q8_1_batched_gpu(_ptr(X_km), _ptr(Y), K, M, _stream(stream)), True)
+
+
+def custom_gemv_iq4xs_can_handle(K: int, N: int, M: int, type_: int = GGML_TYPE_IQ4_XS) -> bool:
+    return bool(lib().custom_gemv_iq4xs_can_handle(K, N, M, type_))
+
+
+def custom_gemv_iq4xs_dispatch(W, x, y, K: int, N: int, stream=None) -> int:
+    """Returns the cudaError_t code (0 = handled), like the ggml hook expects."""
+    return int(lib().custom_gemv_iq4xs_dispatch(_ptr(W), _ptr(x), _ptr(y), K, N, _stream(stream)))
+
+
+def custom_gemv_iq4xs_dispatch_batched(W, x, y, K: int, N: int, M: int, stream=None) -> int:
+    return int(lib().custom_gemv_iq4xs_dispatch_batched(_ptr(W), _ptr(x), _ptr(y), K, N, M, _stream(stream)))
+
+
+def custom_gemm_iq4xs_can_handle(K: int, N: int, M: int, type_: int = GGML_TYPE_IQ4_XS) -> bool:
+    return bool(lib().custom_gemm_iq4xs_can_handle(K, N, M, type_))
+
+
+def custom_gemm_iq4xs_dispatch(W, X, Y, K: int, N: int, M: int, stream=None) -> int:
+    return int(lib().custom_gemm_iq4xs_dispatch(_ptr(W), _ptr(X), _ptr(Y), K, N, M, _stream(stream)))

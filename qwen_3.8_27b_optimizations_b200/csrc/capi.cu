@@ -1,0 +1,293 @@
+// capi.cu -- the C ABI (include/iq4xs.h): argument validation, workspace handling, launches.
+//
+// Argument checks and status mapping follow the reference launchers
+// (kernels/matmul_iq4xs/impl_gemv_dp4a_gfx1100.hip:291-329, real_stock_dp4a_comparator.hip:266-315,
+// patches/0001-gfx1100-mul-mat-custom.patch:148-154,261-280): null pointers, K % 256, non-positive
+// sizes are rejected before any launch; nothing aborts; errors come back as status codes.
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "../../include/iq4xs.h"
+#include "iq4xs_device.cuh"
+#include "iq4xs_kernels.h"
+
+namespace iq4xs {
+
+namespace {
+__device__ uint32_t g_device_error;
+
+constexpr int kMaxDevices = 64;
+uint32_t* g_err_ptr[kMaxDevices];
+std::mutex g_mu;
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int status_from(cudaError_t e) { return e == cudaSuccess ? IQ4XS_OK : IQ4XS_ERR_CUDA; }
+}  // namespace
+
+uint32_t* device_error_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    if (!g_err_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+        g_err_ptr[dev] = static_cast<uint32_t*>(p);
+    }
+    return g_err_ptr[dev];
+}
+
+namespace {
+// ------------------------------------------------------------------------------ validation
+int check_matrix(const void* W, int64_t K, int64_t N) {
+    if (!W) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (K <= 0 || N <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (K % kQK != 0) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (K > (int64_t)1 << 30 || N > ((int64_t)1 << 31) - 1) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(W, 8)) return IQ4XS_ERR_MISALIGNED;
+    return IQ4XS_OK;
+}
+
+int check_batch(int64_t B) { return (B < 1 || B > IQ4XS_MAX_GEMV_BATCH) ? IQ4XS_ERR_UNSUPPORTED_SHAPE : IQ4XS_OK; }
+
+GemvArgs make_gemv_args(const void* W, const void* q8, float* Y, int64_t K, int64_t N) {
+    GemvArgs a;
+    std::memset(&a, 0, sizeof a);
+    a.W = static_cast<const uint8_t*>(W);
+    a.q8 = static_cast<const uint8_t*>(q8);
+    a.y = Y;
+    a.err = device_error_word();
+    a.N = N;
+    a.K = (int)K;
+    a.kb = (int)(K / kQK);
+    a.rb = (int64_t)a.kb * kBlockBytes;
+    return a;
+}
+
+// ------------------------------------------------------------------------------ internal workspace
+// Library-owned workspace for the reference-named entry points that have no workspace argument.
+struct Ws {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+std::map<std::pair<int, cudaStream_t>, Ws> g_ws;
+
+cudaError_t internal_workspace(cudaStream_t stream, size_t bytes, void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(g_mu);
+    Ws& w = g_ws[{dev, stream}];
+    if (w.bytes >= bytes) {
+        *out = w.ptr;
+        return cudaSuccess;
+    }
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess) return e;
+    if (cap != cudaStreamCaptureStatusNone) return cudaErrorNotSupported;  // never allocate while capturing
+    if (w.ptr) {
+        e = cudaStreamSynchronize(stream);  // the old buffer may still be read by queued work
+        if (e != cudaSuccess) return e;
+        cudaFree(w.ptr);
+        w.ptr = nullptr;
+        w.bytes = 0;
+    }
+    size_t want = 1 << 20;
+    while (want < bytes) want <<= 1;
+    e = cudaMalloc(&w.ptr, want);
+    if (e != cudaSuccess) return e;
+    w.bytes = want;
+    *out = w.ptr;
+    return cudaSuccess;
+}
+
+cudaError_t to_cuda_error(int status) {
+    switch (status) {
+        case IQ4XS_OK: return cudaSuccess;
+        case IQ4XS_ERR_CUDA: {
+            cudaError_t e = cudaGetLastError();
+            return e == cudaSuccess ? cudaErrorUnknown : e;
+        }
+        case IQ4XS_ERR_NOT_SUPPORTED: return cudaErrorNotSupported;
+        case IQ4XS_ERR_MISALIGNED: return cudaErrorMisalignedAddress;
+        default: return cudaErrorInvalidValue;
+    }
+}
+}  // namespace
+}  // namespace iq4xs
+
+using namespace iq4xs;
+
+extern "C" {
+
+const char* iq4xs_status_string(int s) {
+    switch (s) {
+        case IQ4XS_OK: return "ok";
+        case IQ4XS_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case IQ4XS_ERR_UNSUPPORTED_SHAPE: return "unsupported shape";
+        case IQ4XS_ERR_MISALIGNED: return "misaligned pointer";
+        case IQ4XS_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+        case IQ4XS_ERR_CUDA: return "CUDA error";
+        case IQ4XS_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+        case IQ4XS_ERR_NOT_SUPPORTED: return "not supported";
+        default: return "unknown status";
+    }
+}
+
+int iq4xs_version(void) { return 100; }
+
+int iq4xs_device_error(uint32_t* code) {
+    if (!code) return IQ4XS_ERR_INVALID_ARGUMENT;
+    uint32_t* p = device_error_word();
+    if (!p) return IQ4XS_ERR_CUDA;
+    uint32_t v = 0;
+    if (cudaMemcpy(&v, p, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return IQ4XS_ERR_CUDA;
+    const uint32_t zero = 0;
+    if (cudaMemcpy(p, &zero, sizeof zero, cudaMemcpyHostToDevice) != cudaSuccess) return IQ4XS_ERR_CUDA;
+    *code = v;
+    return IQ4XS_OK;
+}
+
+size_t iq4xs_q8_1_bytes(int64_t K, int64_t M) {
+    if (K <= 0 || M <= 0 || K % kQK8 != 0) return 0;
+    return (size_t)(K / kQK8) * (size_t)M * kQ8Bytes;
+}
+
+int iq4xs_q8_1_quantize(const float* X, void* q8, int64_t K, int64_t M, cudaStream_t stream) {
+    if (!X || !q8 || K <= 0 || M <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (K % kQK8 != 0) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(X, 4) || !aligned(q8, 4)) return IQ4XS_ERR_MISALIGNED;
+    return status_from(launch_q8_1_quantize(X, static_cast<uint8_t*>(q8), K, M, K, 1, stream, false));
+}
+
+size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t B) {
+    if (K <= 0 || B <= 0) return 0;
+    return iq4xs_q8_1_bytes(K, B);
+}
+
+int iq4xs_gemv_q8(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B, cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if ((s = check_batch(B))) return s;
+    if (!q8 || !Y) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (!aligned(q8, 4) || !aligned(Y, 4)) return IQ4XS_ERR_MISALIGNED;
+    return status_from(launch_gemv_q8(make_gemv_args(W, q8, Y, K, N), (int)B, stream, false));
+}
+
+int iq4xs_gemv_q8_generic(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B,
+                          cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if ((s = check_batch(B))) return s;
+    if (!q8 || !Y) return IQ4XS_ERR_INVALID_ARGUMENT;
+    GemvArgs a = make_gemv_args(W, q8, Y, K, N);
+    a.force_generic = 1;
+    return status_from(launch_gemv_q8(a, (int)B, stream, false));
+}
+
+int iq4xs_gemv_f32(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B, void* workspace,
+                   size_t workspace_bytes, cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if ((s = check_batch(B))) return s;
+    if (!X || !Y || !workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < iq4xs_gemv_workspace_bytes(K, B)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned(X, 4) || !aligned(Y, 4) || !aligned(workspace, 16)) return IQ4XS_ERR_MISALIGNED;
+    uint8_t* q8 = static_cast<uint8_t*>(workspace);
+    cudaError_t e = launch_q8_1_quantize(X, q8, K, B, K, 1, stream, true);
+    if (e != cudaSuccess) return IQ4XS_ERR_CUDA;
+    return status_from(launch_gemv_q8(make_gemv_args(W, q8, Y, K, N), (int)B, stream, true));
+}
+
+int iq4xs_debug_subblock_dots(const void* W, const void* q8, int32_t* S, int64_t K, int64_t N, int64_t B,
+                              cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if ((s = check_batch(B))) return s;
+    if (!q8 || !S) return IQ4XS_ERR_INVALID_ARGUMENT;
+    GemvArgs a = make_gemv_args(W, q8, nullptr, K, N);  // sums only, no y
+    a.sumi = S;
+    return status_from(launch_gemv_q8_debug(a, (int)B, stream));
+}
+
+int iq4xs_fill_normal(float* dst, int64_t n, uint64_t seed, float mean, float stddev, cudaStream_t stream) {
+    if (!dst || n <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    return status_from(launch_fill_normal(dst, n, seed, mean, stddev, stream));
+}
+
+int iq4xs_quantize_weights(const float* src, void* W, int64_t N, int64_t K, cudaStream_t stream) {
+    if (!src || !W || N <= 0 || K <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (K % kQK != 0) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(W, 8) || !aligned(src, 4)) return IQ4XS_ERR_MISALIGNED;
+    return status_from(launch_quantize_iq4_xs(src, static_cast<uint8_t*>(W), N, K, stream));
+}
+
+int iq4xs_dequantize(const void* W, float* out, int64_t K, int64_t N, cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if (!out) return IQ4XS_ERR_INVALID_ARGUMENT;
+    return status_from(launch_dequantize(static_cast<const uint8_t*>(W), out, K, N, stream));
+}
+
+// ------------------------------------------------------------------------------ reference-named
+static cudaError_t gemv_f32_internal_ws(const void* W, const float* x, float* y, int64_t K, int64_t N, int64_t B,
+                                        cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return to_cuda_error(s);
+    if ((s = check_batch(B))) return cudaErrorInvalidValue;
+    if (!x || !y) return cudaErrorInvalidValue;
+    const size_t need = iq4xs_gemv_workspace_bytes(K, B);
+    void* ws = nullptr;
+    cudaError_t e = internal_workspace(stream, need, &ws);
+    if (e != cudaSuccess) return e;
+    return to_cuda_error(iq4xs_gemv_f32(W, x, y, K, N, B, ws, need, stream));
+}
+
+cudaError_t gemv_iq4xs_dp4a_coop_gpu(const void* W, const float* x, float* y, int64_t K, int64_t N, cudaStream_t stream) {
+    return gemv_f32_internal_ws(W, x, y, K, N, 1, stream);
+}
+
+cudaError_t gemv_iq4xs_stock_dp4a_gpu(const void* W, const float* x, float* y, int64_t K, int64_t N, cudaStream_t stream) {
+    return gemv_f32_internal_ws(W, x, y, K, N, 1, stream);
+}
+
+cudaError_t quantize_row_q8_1_gpu(const float* x, void* y, int64_t K, cudaStream_t stream) {
+    if (!x || !y || K <= 0 || K % kQK8 != 0) return cudaErrorInvalidValue;
+    return launch_q8_1_quantize(x, static_cast<uint8_t*>(y), K, 1, K, 1, stream, false);
+}
+
+cudaError_t quantize_row_q8_1_batched_gpu(const float* X, void* Y, int64_t K, int64_t M, cudaStream_t stream) {
+    if (!X || !Y || K <= 0 || M <= 0 || K % kQK8 != 0) return cudaErrorInvalidValue;
+    return launch_q8_1_quantize(X, static_cast<uint8_t*>(Y), K, M, 1, M, stream, false);
+}
+
+bool custom_gemv_iq4xs_can_handle(int64_t K, int64_t N, int64_t M, int type) {
+    if (type != IQ4XS_GGML_TYPE_IQ4_XS) return false;
+    if (M < 1 || M > IQ4XS_MAX_GEMV_BATCH) return false;
+    if (K <= 0 || N <= 0 || K % kQK != 0) return false;
+    return true;
+}
+
+cudaError_t custom_gemv_iq4xs_dispatch(const void* W, const float* x, float* y, int64_t K, int64_t N, cudaStream_t stream) {
+    return gemv_f32_internal_ws(W, x, y, K, N, 1, stream);
+}
+
+cudaError_t custom_gemv_iq4xs_dispatch_batched(const void* W, const float* x, float* y, int64_t K, int64_t N, int64_t M,
+                                               cudaStream_t stream) {
+    return gemv_f32_internal_ws(W, x, y, K, N, M, stream);
+}
+
+bool custom_gemm_iq4xs_can_handle(int64_t K, int64_t N, int64_t M, int type) {
+    (void)K; (void)N; (void)M; (void)type;
+    return false;  // prefill GEMM not built yet: the caller keeps its stock path
+}
+
+cudaError_t custom_gemm_iq4xs_dispatch(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
+                                       cudaStream_t stream) {
+    (void)W; (void)X; (void)Y; (void)K; (void)N; (void)M; (void)stream;
+    return cudaErrorNotSupported;
+}
+
+}  // extern "C"

@@ -1,0 +1,205 @@
+// iq4xs_device.cuh -- formats and sm_100a device primitives shared by every kernel.
+//
+// IQ4_XS super-block (136 B, 256 weights; kernels/common/block_iq4_xs.h:10-19 in the reference):
+//   bytes 0-1  d         fp16 super-block scale
+//   bytes 2-3  scales_h  2 high bits of the 6-bit scale of each of the 8 sub-blocks
+//   bytes 4-7  scales_l  4 low bits of each sub-block scale (two per byte)
+//   bytes 8-135 qs       4-bit codebook indices; byte j of sub-block ib holds element j (low
+//                        nibble) and element j+16 (high nibble) of the 32-weight sub-block
+// Q8_1 activation block (36 B, 32 values; real_stock_dp4a_comparator.hip:22-26):
+//   bytes 0-1 d = trunc_fp16(amax/127), bytes 2-3 s = trunc_fp16(sum), bytes 4-35 int8 q.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace iq4xs {
+
+__host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+constexpr int kQK = 256;          // weights per super-block
+constexpr int kQK8 = 32;          // values per Q8_1 block / weights per sub-block
+constexpr int kBlockBytes = 136;  // IQ4_XS super-block
+constexpr int kQ8Bytes = 36;      // Q8_1 block
+
+// Device error word: a bounded wait that gives up records its code here (first writer wins)
+// and the kernel returns instead of hanging.  Read and cleared by iq4xs_device_error().
+enum DeviceError : uint32_t {
+    kDevErrNone = 0,
+    kDevErrFullWait = 1,    // consumer waited too long for a weight stage
+    kDevErrEmptyWait = 2,   // producer waited too long for a free stage
+    kDevErrDrainWait = 3,   // copies still in flight after an error
+    kDevErrMmaWait = 4,     // tensor-core pipeline barrier timed out
+};
+
+// Spin limit for every mbarrier wait (each try_wait already suspends for a while in hardware);
+// at ~1-2 us per expired try_wait this bounds a wait to well under a minute.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+__device__ __forceinline__ void record_error(uint32_t* err, uint32_t code) {
+    if (err) atomicCAS(err, 0u, code);
+}
+
+// ------------------------------------------------------------------------------ fp16 helpers
+// The reference's truncating fp32 -> fp16 (block_iq4_xs.h:71-86, comparator.hip:45-58).
+__device__ __forceinline__ uint16_t f32_to_f16_trunc(float v) {
+    const uint32_t x = __float_as_uint(v);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const int32_t e = (int32_t)((x >> 23) & 0xFFu) - 127 + 15;
+    uint32_t m = (x >> 13) & 0x3FFu;
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        m = (m | 0x400u) >> (1 - e);
+        return (uint16_t)(sign | m);
+    }
+    if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+    return (uint16_t)(sign | ((uint32_t)e << 10) | m);
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t h16) {
+    return __half2float(__ushort_as_half((unsigned short)(h16 & 0xFFFFu)));
+}
+
+// ------------------------------------------------------------------------------ byte permute
+// prmt.b32 default mode: bytes {b,a} numbered 0..7 (a = 0..3); selector nibble i: bits 2:0
+// pick the source byte, bit 3 replicates that byte's sign bit over the output byte.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// Codebook kvalues_iq4nl (block_iq4_xs.h:22-24) split into two 8-byte prmt tables:
+//  kNegLo: -kv[0..7]  = 127,104,83,65,49,35,22,10  (all < 128, sign bit clear)
+//  kPosHi:  kv[8..15] = 1,13,25,38,53,69,89,113    (all < 128, sign bit clear)
+// prmt(kNegLo, q) returns -kv[n] for codes n<8 and 0 for n>=8 (bit 3 selects sign replication
+// of a positive byte); prmt(kPosHi, q^0x8888) returns kv[n] for n>=8 and 0 for n<8.  So
+//   sum_j kv[n_j] x_j = dp4a(hi, x) - dp4a(lo, x)
+// with two lookups and no merge step.  Output byte order of one lookup on the low 16 bits of a
+// qs word w (bytes 4w..4w+3 of the sub-block) is [e(4w), e(4w+16), e(4w+1), e(4w+17)], on the
+// high 16 bits [e(4w+2), e(4w+18), e(4w+3), e(4w+19)]; activations are permuted to match.
+constexpr uint32_t kNegLo0 = 0x4153687Fu, kNegLo1 = 0x0A162331u;
+constexpr uint32_t kPosHi0 = 0x26190D01u, kPosHi1 = 0x71594535u;
+
+// Activation words in the lookup order: from q8 words lo = q[4w..4w+3], hi = q[16+4w..16+4w+3].
+__device__ __forceinline__ uint32_t act_perm_lo(uint32_t lo, uint32_t hi) { return prmt(lo, hi, 0x5140u); }
+__device__ __forceinline__ uint32_t act_perm_hi(uint32_t lo, uint32_t hi) { return prmt(lo, hi, 0x7362u); }
+
+// Raw sub-block dot of 4 qs words against 8 permuted activation words (exact int32).
+__device__ __forceinline__ int subblock_dot(const uint32_t q[4], const uint32_t alo[4], const uint32_t ahi[4]) {
+    int hi = 0, lo = 0;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const uint32_t x = q[w];
+        const uint32_t xf = x ^ 0x88888888u;
+        const uint32_t xh = x >> 16, xfh = xf >> 16;
+        hi = dp4a((int)prmt(kPosHi0, kPosHi1, xf), (int)alo[w], hi);
+        lo = dp4a((int)prmt(kNegLo0, kNegLo1, x), (int)alo[w], lo);
+        hi = dp4a((int)prmt(kPosHi0, kPosHi1, xfh), (int)ahi[w], hi);
+        lo = dp4a((int)prmt(kNegLo0, kNegLo1, xh), (int)ahi[w], lo);
+    }
+    return hi - lo;
+}
+
+// 6-bit scale code of sub-block ib from the two header words (h0 = d | scales_h<<16,
+// h1 = scales_l[0..3]); ref_cpu.cpp:30-33.
+__device__ __forceinline__ int subblock_scale(uint32_t h0, uint32_t h1, int ib) {
+    return (int)(((h1 >> (4 * ib)) & 0xFu) | (((h0 >> (16 + 2 * ib)) & 0x3u) << 4));
+}
+
+// ------------------------------------------------------------------------------ smem / PTX
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on one phase parity.  Returns false (and records `code`) when the limit is hit.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    record_error(err, code);
+    return false;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar` (bytes).
+// dst, src 16-byte aligned, bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Same, with an L2 eviction hint: weights are streamed once per call.
+__device__ __forceinline__ void bulk_g2s_evict_first(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                     uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Programmatic dependent launch: wait for the preceding grid's memory (no-op without PDL).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ uint2 lds_u2(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+
+}  // namespace iq4xs

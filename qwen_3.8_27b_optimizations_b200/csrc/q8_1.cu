@@ -1,0 +1,59 @@
+// q8_1.cu -- on-the-fly Q8_1 activation quantizer (sm_100a).
+//
+// Replaces quantize_row_q8_1_kernel / quantize_row_q8_1_batched_kernel
+// (kernels/matmul_iq4xs/real_stock_dp4a_comparator.hip:230-315) and the coop variant
+// (kernels/matmul_iq4xs/impl_gemv_dp4a_gfx1100.hip:138-160).  Same per-block semantics, bit for bit:
+//   amax, sum: 32-lane xor butterfly (offsets 16..1); d = amax/127 (IEEE); q = (int8)roundf(x/d),
+//   q = 0 when amax == 0; ds = {trunc_fp16(d), trunc_fp16(sum)} with the reference's truncating
+//   conversion.  Output is the reference's 36-byte block_q8_1 layout.
+// One warp per block, grid-stride; the 32 q bytes leave as eight 4-byte stores.
+#include "iq4xs_device.cuh"
+#include "iq4xs_kernels.h"
+
+namespace iq4xs {
+
+__global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restrict__ X, uint8_t* __restrict__ q8,
+                                                            int64_t K, int64_t M, int64_t stride_m,
+                                                            int64_t stride_k, int signal_dependents) {
+    if (signal_dependents) grid_launch_dependents();
+    const unsigned full = 0xFFFFFFFFu;
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = K / kQK8;
+    const int64_t total = nb * M;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t blk = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); blk < total; blk += nwarps) {
+        const int64_t m = blk / nb;
+        const int64_t ib = blk - m * nb;
+        const float x = X[m * stride_m + (ib * kQK8 + lane) * stride_k];
+        float amax = fabsf(x), sum = x;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(full, amax, off));
+            sum += __shfl_xor_sync(full, sum, off);
+        }
+        const float d = amax / 127.0f;
+        int q = 0;
+        if (amax != 0.0f) q = (int)roundf(x / d);
+        const uint32_t b0 = (uint32_t)q & 0xFFu;
+        const uint32_t b1 = __shfl_down_sync(full, b0, 1);
+        const uint32_t b2 = __shfl_down_sync(full, b0, 2);
+        const uint32_t b3 = __shfl_down_sync(full, b0, 3);
+        uint8_t* out = q8 + blk * kQ8Bytes;
+        if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(out + 4 + lane) = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        if (lane == 0)
+            *reinterpret_cast<uint32_t*>(out) = (uint32_t)f32_to_f16_trunc(d) | ((uint32_t)f32_to_f16_trunc(sum) << 16);
+    }
+}
+
+cudaError_t launch_q8_1_quantize(const float* X, uint8_t* q8, int64_t K, int64_t M, int64_t stride_m,
+                                 int64_t stride_k, cudaStream_t stream, bool signal_dependents) {
+    const int64_t total = (K / kQK8) * M;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t grid = std::min<int64_t>((total + 7) / 8, (int64_t)sms * 16);
+    q8_1_quantize_kernel<<<(unsigned)grid, 256, 0, stream>>>(X, q8, K, M, stride_m, stride_k, signal_dependents ? 1 : 0);
+    return cudaGetLastError();
+}
+
+}  // namespace iq4xs

@@ -1,0 +1,76 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol declared in
+include/iq4xs.h, and rejects bad arguments before touching the device."""
+import ctypes as C
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = ROOT / "include" / "iq4xs.h"
+BENCH_HEADER = ROOT / "include" / "iq4xs_bench.h"
+
+
+def declared_functions(header=HEADER):
+    text = header.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s+\*?([A-Za-z_][A-Za-z0-9_]*)\s*\(", text, flags=re.M)
+    return sorted(set(n for n in names if n not in ("if", "while", "return")))
+
+
+def test_header_parses():
+    names = declared_functions()
+    assert "iq4xs_gemv_f32" in names and "custom_gemv_iq4xs_dispatch" in names
+    assert len(names) >= 20
+
+
+def test_every_declared_symbol_is_exported(pkg):
+    L = pkg.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+
+
+def test_python_signatures_cover_header(pkg):
+    assert set(pkg.SIGNATURES) == set(declared_functions())
+    assert set(pkg.api.BENCH_SIGNATURES) == set(declared_functions(BENCH_HEADER))
+
+
+def test_bench_header_symbols_exported(pkg):
+    L = pkg.lib()
+    for name in declared_functions(BENCH_HEADER):
+        assert hasattr(L, name), name
+
+
+def test_status_strings(pkg):
+    L = pkg.lib()
+    assert L.iq4xs_status_string(0) == b"ok"
+    assert L.iq4xs_status_string(2) == b"unsupported shape"
+    assert L.iq4xs_version() >= 100
+
+
+FAKE = 0x10000  # never dereferenced: validation fails first
+
+
+def test_validation_before_any_launch(pkg):
+    L = pkg.lib()
+    assert L.iq4xs_gemv_q8(None, FAKE, FAKE, 512, 64, 1, None) == 1
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 500, 64, 1, None) == 2      # K % 256
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 0, 1, None) == 1       # N <= 0
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 9, None) == 2      # batch > 8
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 0, None) == 2      # batch < 1
+    assert L.iq4xs_gemv_q8(FAKE + 4, FAKE, FAKE, 512, 64, 1, None) == 3  # W not 8-byte aligned
+    need = L.iq4xs_gemv_workspace_bytes(512, 2)
+    assert need == 2 * 16 * 36
+    assert L.iq4xs_gemv_f32(FAKE, FAKE, FAKE, 512, 64, 2, FAKE, need - 1, None) == 4
+    assert L.iq4xs_q8_1_quantize(None, FAKE, 512, 1, None) == 1
+    assert L.iq4xs_q8_1_quantize(FAKE, FAKE, 100, 1, None) == 2
+    assert L.iq4xs_q8_1_bytes(5120, 3) == 3 * 160 * 36
+    assert L.iq4xs_quantize_weights(FAKE, FAKE, 4, 300, None) == 2
+
+
+def test_ggml_can_handle(pkg):
+    assert pkg.custom_gemv_iq4xs_can_handle(5120, 17408, 1)
+    assert pkg.custom_gemv_iq4xs_can_handle(4096, 4096, 8)
+    assert not pkg.custom_gemv_iq4xs_can_handle(4096, 4096, 9)
+    assert not pkg.custom_gemv_iq4xs_can_handle(4000, 4096, 1)
+    assert not pkg.custom_gemv_iq4xs_can_handle(4096, 4096, 1, 12)  # another ggml type
