@@ -237,13 +237,14 @@ def main():
          for B in BATCHES for i, (_, N, K) in enumerate(SHAPES)}
     Y = {(B, i): torch.empty((B, N), dtype=torch.float32, device=dev) for B in BATCHES for i, (_, N, K) in enumerate(SHAPES)}
     maxK = max(K for _, _, K in SHAPES)
-    ws = torch.empty(P.gemv_workspace_bytes(maxK, max(BATCHES)), dtype=torch.uint8, device=dev)
+    ws = torch.zeros(max(P.gemv_workspace_bytes(K, N, B) for B in BATCHES for _, N, K in SHAPES), dtype=torch.uint8,
+                     device=dev)
     torch.cuda.synchronize()
 
     def step(c: int, s):
         for B in BATCHES:
             for i, (_, N, K) in enumerate(SHAPES):
-                P.gemv(weights[c][i], X[(B, i)], N, workspace=ws, out=Y[(B, i)], stream=s)
+                P.gemv(weights[c][i], X[(B, i)], N, workspace=ws, out=Y[(B, i)], stream=s, flags=P.FLAG_OVERLAP_PRECEDING)
 
     # capture one graph per weight copy
     graphs = []

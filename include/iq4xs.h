@@ -68,23 +68,39 @@ int iq4xs_q8_1_quantize(const float* X, void* q8, int64_t K, int64_t M, cudaStre
 size_t iq4xs_q8_1_bytes(int64_t K, int64_t M);
 
 /* ------------------------------------------------------------------------------------------ */
+/* Workspace of the GEMV entry points: zero-filled by the caller before its first use (e.g.
+ * cudaMemset); every completed call leaves it ready for the next one, whatever the shapes.  After a
+ * call reported IQ4XS_ERR_DEVICE_TIMEOUT, zero it again.  Calls that may overlap on the GPU must use
+ * separate workspaces.  256-byte aligned. */
+
 /* Decode GEMV on pre-quantised activations, batch B = 1..8:
  *   Y[b][n] = sum_k W[n][k] * x_b[k]  with the reference's per-sub-block integer pipeline.
  * Replaces gemv_iq4xs_dp4a_gfx1100_prequantized_gpu (impl_gemv_dp4a_gfx1100.hip:291-308) and the
  * patch's gemv_prequantized_cuh (patches/0001-gfx1100-mul-mat-custom.patch:261-266), both batch 1;
  * batch 2..8 is new (the reference routes it to stock MMVQ, patch:275).
- * q8: [B][K/32] Q8_1 blocks (iq4xs_q8_1_quantize output).  Y: fp32 [B][N]. */
+ * q8: [B][K/32] Q8_1 blocks (iq4xs_q8_1_quantize output).  Y: fp32 [B][N].
+ * workspace >= iq4xs_gemv_q8_workspace_bytes(K, N, B) (cross-CTA partial sums of long rows). */
 int iq4xs_gemv_q8(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B,
-                  cudaStream_t stream);
+                  void* workspace, size_t workspace_bytes, cudaStream_t stream);
+size_t iq4xs_gemv_q8_workspace_bytes(int64_t K, int64_t N, int64_t B);
 
-/* Decode GEMV on fp32 activations X [B][K]: quantise into `workspace`, then GEMV (the GEMV is
+/* Decode GEMV on fp32 activations X [B][K]: quantise into the workspace, then GEMV (the GEMV is
  * launched with programmatic dependent launch so its weight stream overlaps the quantizer).
  * Replaces gemv_iq4xs_dp4a_gfx1100_gpu (impl_gemv_dp4a_gfx1100.hip:310-329) and
  * gemv_iq4xs_stock_dp4a_gpu (real_stock_dp4a_comparator.hip:480-503) without their per-call
- * hipMalloc/hipFree: workspace >= iq4xs_gemv_workspace_bytes(K, B) bytes, 16-byte aligned. */
+ * hipMalloc/hipFree: workspace >= iq4xs_gemv_workspace_bytes(K, N, B). */
 int iq4xs_gemv_f32(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B,
                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
-size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t B);
+size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t N, int64_t B);
+
+/* Flags of iq4xs_gemv_f32_ex. */
+#define IQ4XS_FLAG_OVERLAP_PRECEDING 1u /* W is not written by the kernel that precedes this call on
+                                          the stream: the quantizer is launched as a programmatic
+                                          dependent (it still waits for X) and the GEMV's prologue and
+                                          weight prefetch overlap the preceding kernel's tail */
+/* iq4xs_gemv_f32 with flags (iq4xs_gemv_f32 == flags 0). */
+int iq4xs_gemv_f32_ex(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B,
+                      void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Raw int32 sub-block dot products sum_j kvalues[q_j]*q8_j (before the (ls-32) factor) through
@@ -129,7 +145,8 @@ cudaError_t quantize_row_q8_1_batched_gpu(const float* X, void* Y, int64_t K, in
  * (ne00 = K, ne01 = N), x/X = src1 fp32 [M][K], y/Y = dst fp32 [M][N].
  * can_handle: patch:274-277 (GEMV) and :148-151 (GEMM); dispatch: :278-280 and :152-154.
  * GEMV handles M = 1..8 (the patch: M == 1 and three fixed shapes); the batched dispatch is the
- * M > 1 form of the same call.  Any non-success status lets the caller fall back to stock. */
+ * M > 1 form of the same call.  Any non-success status lets the caller fall back to stock.
+ * The GEMV dispatches treat W as static model weights (IQ4XS_FLAG_OVERLAP_PRECEDING). */
 bool custom_gemv_iq4xs_can_handle(int64_t K, int64_t N, int64_t M, int type);
 cudaError_t custom_gemv_iq4xs_dispatch(const void* W, const float* x, float* y, int64_t K, int64_t N,
                                        cudaStream_t stream);

@@ -32,9 +32,11 @@ SIGNATURES = {
     "iq4xs_device_error": (_i, [C.POINTER(C.c_uint32)]),
     "iq4xs_q8_1_quantize": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "iq4xs_q8_1_bytes": (_sz, [_i64, _i64]),
-    "iq4xs_gemv_q8": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "iq4xs_gemv_q8": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "iq4xs_gemv_q8_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "iq4xs_gemv_f32": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
-    "iq4xs_gemv_workspace_bytes": (_sz, [_i64, _i64]),
+    "iq4xs_gemv_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "iq4xs_gemv_f32_ex": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
     "iq4xs_debug_subblock_dots": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_gemv_q8_generic": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_fill_normal": (_i, [_vp, _i64, _u64, _f, _f, _vp]),
@@ -123,32 +125,58 @@ def q8_1_quantize(X, stream=None):
     return q8
 
 
-def gemv_q8(W, q8, K: int, N: int, B: int, out=None, stream=None, generic: bool = False):
+_ws_cache = {}
+
+
+def _workspace(nbytes: int, device):
+    """A zero-initialised workspace (the ticket region must start at zero) cached per device."""
+    torch = _torch()
+    key = (str(device),)
+    ws = _ws_cache.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _ws_cache[key] = ws
+    return ws
+
+
+def gemv_q8_workspace_bytes(K: int, N: int, B: int) -> int:
+    return int(lib().iq4xs_gemv_q8_workspace_bytes(K, N, B))
+
+
+def gemv_q8(W, q8, K: int, N: int, B: int, out=None, stream=None, generic: bool = False, workspace=None):
     """Y [B][N] fp32 from IQ4_XS W and pre-quantised activations q8 [B][K/32] blocks."""
     torch = _torch()
     Y = out if out is not None else torch.empty((B, N), dtype=torch.float32, device=W.device)
-    fn = lib().iq4xs_gemv_q8_generic if generic else lib().iq4xs_gemv_q8
-    _check("iq4xs_gemv_q8", fn(_ptr(W), _ptr(q8), _ptr(Y), K, N, B, _stream(stream)))
+    if generic:
+        _check("iq4xs_gemv_q8_generic", lib().iq4xs_gemv_q8_generic(_ptr(W), _ptr(q8), _ptr(Y), K, N, B, _stream(stream)))
+        return Y
+    ws = workspace if workspace is not None else _workspace(gemv_q8_workspace_bytes(K, N, B), W.device)
+    _check("iq4xs_gemv_q8", lib().iq4xs_gemv_q8(_ptr(W), _ptr(q8), _ptr(Y), K, N, B, _ptr(ws),
+                                                ws.numel() * ws.element_size(), _stream(stream)))
     return Y
 
 
-def gemv_workspace_bytes(K: int, B: int) -> int:
-    return int(lib().iq4xs_gemv_workspace_bytes(K, B))
+def gemv_workspace_bytes(K: int, N: int, B: int) -> int:
+    return int(lib().iq4xs_gemv_workspace_bytes(K, N, B))
 
 
-def gemv(W, X, N: int, workspace=None, out=None, stream=None):
-    """Y [B][N] = W . X^T for fp32 activations X [B][K] (quantised on the fly into workspace)."""
+FLAG_OVERLAP_PRECEDING = 1
+
+
+def gemv(W, X, N: int, workspace=None, out=None, stream=None, flags: int = 0):
+    """Y [B][N] = W . X^T for fp32 activations X [B][K] (quantised on the fly into the workspace).
+    The workspace must be zero-filled before its first use (torch.zeros).  flags=FLAG_OVERLAP_PRECEDING
+    when W is not written by the preceding kernel on the stream."""
     torch = _torch()
     X = X.contiguous()
     if X.dim() == 1:
         X = X[None]
     B, K = X.shape
-    need = gemv_workspace_bytes(K, B)
-    if workspace is None:
-        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=X.device)
+    need = gemv_workspace_bytes(K, N, B)
+    ws = workspace if workspace is not None else _workspace(need, X.device)
     Y = out if out is not None else torch.empty((B, N), dtype=torch.float32, device=X.device)
-    _check("iq4xs_gemv_f32", lib().iq4xs_gemv_f32(_ptr(W), _ptr(X), _ptr(Y), K, N, B, _ptr(workspace),
-                                                  workspace.numel() * workspace.element_size(), _stream(stream)))
+    _check("iq4xs_gemv_f32", lib().iq4xs_gemv_f32_ex(_ptr(W), _ptr(X), _ptr(Y), K, N, B, _ptr(ws),
+                                                     ws.numel() * ws.element_size(), flags, _stream(stream)))
     return Y
 
 

@@ -62,6 +62,10 @@ GemvArgs make_gemv_args(const void* W, const void* q8, float* Y, int64_t K, int6
     a.K = (int)K;
     a.kb = (int)(K / kQK);
     a.rb = (int64_t)a.kb * kBlockBytes;
+    a.lut[0] = kNegLo0;
+    a.lut[1] = kNegLo1;
+    a.lut[2] = kPosHi0;
+    a.lut[3] = kPosHi1;
     return a;
 }
 
@@ -98,9 +102,26 @@ cudaError_t internal_workspace(cudaStream_t stream, size_t bytes, void** out) {
     while (want < bytes) want <<= 1;
     e = cudaMalloc(&w.ptr, want);
     if (e != cudaSuccess) return e;
+    e = cudaMemset(w.ptr, 0, want);  // the ticket region must start at zero
+    if (e != cudaSuccess) return e;
     w.bytes = want;
     *out = w.ptr;
     return cudaSuccess;
+}
+
+// GEMV workspace: [tickets: kTicketBytes, must be zero before first use, left zero by every call]
+//                 [Q8_1 activations, f32 entry points only][cross-CTA partial sums]
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+size_t gemv_partials(int64_t K, int64_t N, int64_t B) {
+    return gemv_mma_partial_bytes(K, N, (int)B);
+}
+
+void attach_workspace(GemvArgs& a, void* ws, size_t q8_bytes, int64_t K, int64_t N, int64_t B) {
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    a.tickets = reinterpret_cast<uint32_t*>(base);
+    a.partials = reinterpret_cast<float*>(base + kTicketBytes + align256(q8_bytes));
+    a.partial_bytes = gemv_partials(K, N, B);
 }
 
 cudaError_t to_cuda_error(int status) {
@@ -162,18 +183,27 @@ int iq4xs_q8_1_quantize(const float* X, void* q8, int64_t K, int64_t M, cudaStre
     return status_from(launch_q8_1_quantize(X, static_cast<uint8_t*>(q8), K, M, K, 1, stream, false));
 }
 
-size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t B) {
-    if (K <= 0 || B <= 0) return 0;
-    return iq4xs_q8_1_bytes(K, B);
+size_t iq4xs_gemv_q8_workspace_bytes(int64_t K, int64_t N, int64_t B) {
+    if (K <= 0 || N <= 0 || B <= 0) return 0;
+    return kTicketBytes + gemv_partials(K, N, B);
 }
 
-int iq4xs_gemv_q8(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B, cudaStream_t stream) {
+size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t N, int64_t B) {
+    if (K <= 0 || N <= 0 || B <= 0) return 0;
+    return kTicketBytes + align256(iq4xs_q8_1_bytes(K, B)) + gemv_partials(K, N, B);
+}
+
+int iq4xs_gemv_q8(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B, void* workspace,
+                  size_t workspace_bytes, cudaStream_t stream) {
     int s = check_matrix(W, K, N);
     if (s) return s;
     if ((s = check_batch(B))) return s;
-    if (!q8 || !Y) return IQ4XS_ERR_INVALID_ARGUMENT;
-    if (!aligned(q8, 4) || !aligned(Y, 4)) return IQ4XS_ERR_MISALIGNED;
-    return status_from(launch_gemv_q8(make_gemv_args(W, q8, Y, K, N), (int)B, stream, false));
+    if (!q8 || !Y || !workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < iq4xs_gemv_q8_workspace_bytes(K, N, B)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned(q8, 4) || !aligned(Y, 4) || !aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
+    GemvArgs a = make_gemv_args(W, q8, Y, K, N);
+    attach_workspace(a, workspace, 0, K, N, B);
+    return status_from(launch_gemv_q8(a, (int)B, stream, false));
 }
 
 int iq4xs_gemv_q8_generic(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B,
@@ -189,16 +219,24 @@ int iq4xs_gemv_q8_generic(const void* W, const void* q8, float* Y, int64_t K, in
 
 int iq4xs_gemv_f32(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B, void* workspace,
                    size_t workspace_bytes, cudaStream_t stream) {
+    return iq4xs_gemv_f32_ex(W, X, Y, K, N, B, workspace, workspace_bytes, 0u, stream);
+}
+
+int iq4xs_gemv_f32_ex(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B, void* workspace,
+                      size_t workspace_bytes, unsigned flags, cudaStream_t stream) {
     int s = check_matrix(W, K, N);
     if (s) return s;
     if ((s = check_batch(B))) return s;
     if (!X || !Y || !workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
-    if (workspace_bytes < iq4xs_gemv_workspace_bytes(K, B)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
-    if (!aligned(X, 4) || !aligned(Y, 4) || !aligned(workspace, 16)) return IQ4XS_ERR_MISALIGNED;
-    uint8_t* q8 = static_cast<uint8_t*>(workspace);
-    cudaError_t e = launch_q8_1_quantize(X, q8, K, B, K, 1, stream, true);
+    if (workspace_bytes < iq4xs_gemv_workspace_bytes(K, N, B)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned(X, 4) || !aligned(Y, 4) || !aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
+    uint8_t* q8 = static_cast<uint8_t*>(workspace) + kTicketBytes;
+    const bool overlap = (flags & IQ4XS_FLAG_OVERLAP_PRECEDING) != 0;
+    cudaError_t e = launch_q8_1_quantize(X, q8, K, B, K, 1, stream, true, overlap);
     if (e != cudaSuccess) return IQ4XS_ERR_CUDA;
-    return status_from(launch_gemv_q8(make_gemv_args(W, q8, Y, K, N), (int)B, stream, true));
+    GemvArgs a = make_gemv_args(W, q8, Y, K, N);
+    attach_workspace(a, workspace, iq4xs_q8_1_bytes(K, B), K, N, B);
+    return status_from(launch_gemv_q8(a, (int)B, stream, true));
 }
 
 int iq4xs_debug_subblock_dots(const void* W, const void* q8, int32_t* S, int64_t K, int64_t N, int64_t B,
@@ -238,11 +276,11 @@ static cudaError_t gemv_f32_internal_ws(const void* W, const float* x, float* y,
     if (s) return to_cuda_error(s);
     if ((s = check_batch(B))) return cudaErrorInvalidValue;
     if (!x || !y) return cudaErrorInvalidValue;
-    const size_t need = iq4xs_gemv_workspace_bytes(K, B);
+    const size_t need = iq4xs_gemv_workspace_bytes(K, N, B);
     void* ws = nullptr;
     cudaError_t e = internal_workspace(stream, need, &ws);
     if (e != cudaSuccess) return e;
-    return to_cuda_error(iq4xs_gemv_f32(W, x, y, K, N, B, ws, need, stream));
+    return to_cuda_error(iq4xs_gemv_f32_ex(W, x, y, K, N, B, ws, need, IQ4XS_FLAG_OVERLAP_PRECEDING, stream));
 }
 
 cudaError_t gemv_iq4xs_dp4a_coop_gpu(const void* W, const float* x, float* y, int64_t K, int64_t N, cudaStream_t stream) {

@@ -5,14 +5,14 @@
 // cooperative gemv_iq4xs_dp4a_coop_kernel (kernels/matmul_iq4xs/impl_gemv_dp4a_gfx1100.hip:178-283,
 // vendored as patches/0001-gfx1100-mul-mat-custom.patch:237-260).
 //
+// Batch 1 runs here (dp4a); batch 2..8 run on the tensor cores (gemv_mma.cu).
 // Design (HBM-streaming, one CTA per SM):
-//  * every CTA owns a contiguous, balanced range of output rows and streams those rows' IQ4_XS
-//    bytes through a ring of shared-memory stages filled by 1-D bulk copies (cp.async.bulk, one
-//    copy per row segment, completion on an mbarrier, L2 evict-first);
-//  * warp 0 is the producer; NCW consumer warps compute.  Consumer lane layout: 8 lanes per row
-//    (lane & 7 = sub-block ib of each super-block), 4 rows per warp step, RPL steps per warp;
-//  * the Q8_1 activations of all B tokens are staged once per CTA in shared memory, permuted to
-//    the order of the codebook lookup and read back as 16-byte vectors;
+//  * every CTA owns a contiguous, balanced range of output rows and streams them through a ring of
+//    shared-memory stages; one stage = R consecutive full rows = ONE 1-D bulk copy (cp.async.bulk,
+//    completion on an mbarrier, L2 evict-first) -- many small copies starve the copy engine;
+//  * warp 0 is the producer; the consumer warps own rows (or, for long K, K slices of a row): lane l
+//    owns sub-blocks l, l+32, ... of its K slice, the same K positions for every row, so its Q8_1
+//    activations (permuted to the order of the codebook lookup) live in registers for the whole kernel;
 //  * the codebook gather is two prmt lookups per 4 codes with no merge (sign-replication zeroes
 //    the half that does not apply), the int8 dot products are dp4a, giving the exact int32
 //    sub-block dot of the reference; the term (d_w*d_x)*(float)(sumi*(ls-32)) is the reference's
@@ -26,34 +26,6 @@ namespace iq4xs {
 
 constexpr int kMaxStages = 16;
 
-template <int B, int NCW, int RPL, int KC>
-struct GemvCfg {
-    static constexpr int kThreads = 32 * (1 + NCW);
-    static constexpr int kRowsPerWarp = 4 * RPL;
-    static constexpr int kRT = kRowsPerWarp * NCW;           // rows per tile
-    static constexpr int kRowStride = KC * kBlockBytes + 16;  // smem bytes per row segment (16-aligned)
-    static constexpr int kStageBytes = kRT * kRowStride;
-    static constexpr int kActBytesPerSB = 256 + 32;            // permuted q8 (256) + 8 fp32 d_x (32)
-};
-
-struct SmemLayout {
-    uint32_t bar_off, abort_off, act_off, dx_off, ring_off, total;
-};
-
-// Barriers first, then the activation area, then the 128-byte aligned ring.
-template <int B, int NCW, int RPL, int KC>
-__host__ __device__ inline SmemLayout gemv_smem_layout(int kb_per_part, int stages) {
-    using Cfg = GemvCfg<B, NCW, RPL, KC>;
-    SmemLayout L;
-    L.bar_off = 0;
-    L.abort_off = 2 * kMaxStages * 8;
-    L.act_off = (L.abort_off + 16 + 127) & ~127u;
-    L.dx_off = L.act_off + (uint32_t)B * kb_per_part * 256;
-    L.ring_off = (L.dx_off + (uint32_t)B * kb_per_part * 32 + 127) & ~127u;
-    L.total = L.ring_off + (uint32_t)stages * Cfg::kStageBytes;
-    return L;
-}
-
 // Wait on an mbarrier phase, giving up when another warp already aborted or the spin limit hits.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
                                               uint32_t* err, uint32_t code) {
@@ -66,25 +38,78 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
     return false;
 }
 
-template <int B, int NCW, int RPL, int KC, bool kDebug>
-__global__ void __launch_bounds__(GemvCfg<B, NCW, RPL, KC>::kThreads, 1)
-    gemv_iq4xs_q8_kernel(const GemvArgs a) {
-    using Cfg = GemvCfg<B, NCW, RPL, KC>;
+// Sleeping variant: each try_wait suspends up to 1 ms; 20000 tries bound the wait to ~20 s.
+__device__ __forceinline__ bool wait_sleep_or_abort(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                                    uint32_t* err, uint32_t code) {
+    for (uint32_t i = 0; i < 20000u; ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+        if (*abort_flag) return false;
+    }
+    record_error(err, code);
+    *abort_flag = 1u;
+    return false;
+}
+
+// --------------------------------------------------------------------------------------------
+// Row-stage kernel (batch 1..2): one stage = R consecutive full rows = ONE bulk copy of R*rb bytes.
+// Warp (kw, slot) handles stage row `slot` over its contiguous K range kw; lane l owns sub-blocks
+// kw*32*SPL + l + 32*i (i < SPL), the same K positions for every row, so its Q8_1 activations are
+// loaded into registers once per kernel.  With KW > 1 warps per row, each warp leaves its partial
+// sum in shared memory and the last of the KW warps (shared-memory ticket) adds them in kw order:
+// deterministic.
+struct RowSmem {
+    uint32_t bar_off, abort_off, part_off, cnt_off, ring_off, total;
+};
+
+__host__ __device__ inline RowSmem gemv_row_smem(int B, int R, int KW, int stages, int64_t stage_bytes) {
+    RowSmem L;
+    L.bar_off = 0;
+    L.abort_off = 2 * kMaxStages * 8;
+    L.part_off = L.abort_off + 16;
+    L.cnt_off = L.part_off + (uint32_t)kMaxStages * R * KW * B * 4;
+    L.ring_off = (L.cnt_off + (uint32_t)kMaxStages * R * 4 + 127) & ~127u;
+    L.total = L.ring_off + (uint32_t)(stages * stage_bytes);
+    return L;
+}
+
+// x >> 16 on the FMA pipe: one mul.hi.u32 by 2^16 (the integer ALU pipe is the busier one).
+__device__ __forceinline__ uint32_t hi16_fma(uint32_t x) {
+    uint32_t d;
+    asm("mul.hi.u32 %0, %1, 65536;" : "=r"(d) : "r"(x));
+    return d;
+}
+
+// Weight side of the split codebook lookup for one qs word: hi/lo halves of both 16-bit selectors.
+// The >>16 selector shifts are done as umulhi(x, 2^16) so they issue on the FMA pipe next to the
+// dp4a instead of on the (half-rate) integer ALU pipe with the prmt lookups.
+// The table words come from the kernel parameters so prmt can read them from the constant bank.
+__device__ __forceinline__ void lut_word(const uint32_t (&tab)[4], uint32_t x, uint32_t& h0, uint32_t& l0, uint32_t& h1,
+                                         uint32_t& l1) {
+    const uint32_t xf = x ^ 0x88888888u;
+    h0 = prmt(tab[2], tab[3], xf);
+    l0 = prmt(tab[0], tab[1], x);
+    h1 = prmt(tab[2], tab[3], hi16_fma(xf));
+    l1 = prmt(tab[0], tab[1], hi16_fma(x));
+}
+
+template <int B, int SPL, int RPW, int NCW, bool kTail, bool kDebug>
+__global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const SmemLayout L = gemv_smem_layout<B, NCW, RPL, KC>(a.kb_per_part, a.stages);
+    const int R = a.rows_per_stage, KW = a.kw;
+    const int stages = a.stages;
+    const int64_t stage_bytes = (int64_t)R * a.rb;
+    const RowSmem L = gemv_row_smem(B, R, KW, stages, stage_bytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     uint64_t* empty = full + kMaxStages;
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.abort_off);
+    float* part = reinterpret_cast<float*>(smem + L.part_off);
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(smem + L.cnt_off);
     uint8_t* ring = smem + L.ring_off;
 
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int stages = a.stages;
-
-    // Balanced contiguous row range of this CTA.
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t r0 = a.N * (int64_t)blockIdx.x / gridDim.x;
     const int64_t r1 = a.N * (int64_t)(blockIdx.x + 1) / gridDim.x;
-    const int ntiles = (int)((r1 - r0 + Cfg::kRT - 1) / Cfg::kRT);
+    const int ntiles = (int)((r1 - r0 + R - 1) / R);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
@@ -94,45 +119,28 @@ __global__ void __launch_bounds__(GemvCfg<B, NCW, RPL, KC>::kThreads, 1)
         *abort_flag = 0u;
         fence_mbar_init();
     }
+    for (int i = threadIdx.x; i < kMaxStages * R; i += blockDim.x) cnt[i] = 0u;
     __syncthreads();
 
     if (warp == 0) {
-        // ------------------------------------------------------------------ producer
-        const uint64_t policy = l2_policy_evict_first();
-        uint32_t it = 0;
-        bool ok = true;
-        for (int p = 0; p < a.kparts && ok; ++p) {
-            const int pb0 = p * a.kb_per_part;
-            const int pb1 = min(a.kb, pb0 + a.kb_per_part);
-            const int nchunks = (pb1 - pb0 + KC - 1) / KC;
-            for (int t = 0; t < ntiles && ok; ++t) {
-                const int64_t row0 = r0 + (int64_t)t * Cfg::kRT;
-                const int rows = (int)imin64(Cfg::kRT, r1 - row0);
-                for (int c = 0; c < nchunks; ++c) {
-                    const int s = (int)(it % stages);
-                    const uint32_t use = it / stages;
-                    if (use > 0 && !wait_or_abort(&empty[s], (use - 1) & 1u, abort_flag, a.err, kDevErrEmptyWait)) {
-                        ok = false;
-                        break;
-                    }
-                    const int b0 = pb0 + c * KC;
-                    const uint32_t bytes = (uint32_t)min(KC, pb1 - b0) * kBlockBytes;
-                    if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes * (uint32_t)rows);
-                    __syncwarp();
-                    uint8_t* dst = ring + (size_t)s * Cfg::kStageBytes;
-                    for (int r = lane; r < rows; r += 32)
-                        bulk_g2s_evict_first(dst + r * Cfg::kRowStride, a.W + (row0 + r) * a.rb + (int64_t)b0 * kBlockBytes,
-                                             bytes, &full[s], policy);
-                    ++it;
-                }
-            }
-        }
-        // Drain: every issued stage must have landed before this CTA's shared memory goes away.
+        // ------------------------------------------------------------------ producer: one copy per stage
         if (lane == 0) {
+            const uint64_t policy = l2_policy_evict_first();
+            uint32_t it = 0;
+            for (int t = 0; t < ntiles; ++t, ++it) {
+                const int s = (int)(it % stages);
+                const uint32_t use = it / stages;
+                if (use > 0 && !wait_sleep_or_abort(&empty[s], (use - 1) & 1u, abort_flag, a.err, kDevErrEmptyWait)) break;
+                const int64_t row0 = r0 + (int64_t)t * R;
+                const uint32_t bytes = (uint32_t)(imin64(R, r1 - row0) * a.rb);
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_g2s_evict_first(ring + (size_t)s * stage_bytes, a.W + row0 * a.rb, bytes, &full[s], policy);
+            }
             const uint32_t first = it > (uint32_t)stages ? it - stages : 0u;
             for (uint32_t j = first; j < it; ++j) {
                 bool landed = false;
-                for (uint32_t i = 0; i < kSpinLimit && !landed; ++i) landed = mbar_try_wait(&full[j % stages], (j / stages) & 1u);
+                for (uint32_t i = 0; i < 20000u && !landed; ++i)
+                    landed = mbar_try_wait_sleep(&full[j % stages], (j / stages) & 1u, 1000000u);
                 if (!landed) record_error(a.err, kDevErrDrainWait);
             }
         }
@@ -141,142 +149,136 @@ __global__ void __launch_bounds__(GemvCfg<B, NCW, RPL, KC>::kThreads, 1)
 
     // ---------------------------------------------------------------------- consumers
     const int cw = warp - 1;
-    const int g = lane >> 3;   // row within a 4-row warp step
-    const int ib = lane & 7;   // sub-block within each super-block
-    const int ctid = threadIdx.x - 32;
-    const int nct = NCW * 32;
-    const uint32_t act_base = smem_addr(smem + L.act_off);
-    const uint32_t dx_base = smem_addr(smem + L.dx_off);
-    const uint32_t ring_base = smem_addr(ring);
-    const int nsb = a.K / kQK8;  // Q8_1 blocks per token
+    const int kw = cw % KW, slot = cw / KW;     // rows slot*RPW .. slot*RPW+RPW-1 of every stage
+    const int nsb = a.K / kQK8;
+    const int sb0 = kw * 32 * SPL + lane;       // this lane's first sub-block; ib = lane & 7
+    const int ib = lane & 7;
+    const uint32_t sh_lo = 4u * ib, sh_hi = 12u + 2u * ib;  // scale bit positions
+    // offsets inside a row of this lane's super-block header and qs words (sub-block i adds 4*136)
+    const uint32_t off_h = (uint32_t)(sb0 >> 3) * kBlockBytes;
+    const uint32_t off_q = off_h + 8 + 16 * ib;
 
-    grid_dependency_wait();  // activations may come from the immediately preceding kernel
-
-    uint32_t it = 0;
-    for (int p = 0; p < a.kparts; ++p) {
-        const int pb0 = p * a.kb_per_part;
-        const int pb1 = min(a.kb, pb0 + a.kb_per_part);
-        const int nchunks = (pb1 - pb0 + KC - 1) / KC;
-        const int pkb = pb1 - pb0;
-
-        // Stage this part's activations: per (token, super-block) 256 B of permuted q8 laid out as
-        // [half][ib][16 B] (8 lanes read 128 contiguous bytes) and 8 fp32 d_x.
-        if (p > 0) named_barrier(1, nct);  // everyone finished with the previous part
-        for (int e = ctid; e < B * pkb * 8; e += nct) {
-            const int t = e / (pkb * 8);
-            const int rem = e - t * pkb * 8;
-            const int bl = rem >> 3, sib = rem & 7;
-            const uint32_t* blk =
-                reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)t * nsb + (int64_t)(pb0 + bl) * 8 + sib) * kQ8Bytes);
-            uint32_t w[9];
+    grid_dependency_wait();
+    uint32_t alo[SPL][B][4], ahi[SPL][B][4];
+    float dx[SPL][B];
 #pragma unroll
-            for (int i = 0; i < 9; ++i) w[i] = __ldg(blk + i);
-            uint4 lo, hi;
-            lo.x = act_perm_lo(w[1], w[5]);
-            lo.y = act_perm_lo(w[2], w[6]);
-            lo.z = act_perm_lo(w[3], w[7]);
-            lo.w = act_perm_lo(w[4], w[8]);
-            hi.x = act_perm_hi(w[1], w[5]);
-            hi.y = act_perm_hi(w[2], w[6]);
-            hi.z = act_perm_hi(w[3], w[7]);
-            hi.w = act_perm_hi(w[4], w[8]);
-            uint8_t* dst = smem + L.act_off + ((size_t)(t * a.kb_per_part + bl) * 256) + sib * 16;
-            *reinterpret_cast<uint4*>(dst) = lo;
-            *reinterpret_cast<uint4*>(dst + 128) = hi;
-            reinterpret_cast<float*>(smem + L.dx_off)[(t * a.kb_per_part + bl) * 8 + sib] = f16_bits_to_f32(w[0]);
+    for (int i = 0; i < SPL; ++i) {
+        const int sb = sb0 + 32 * i;
+#pragma unroll
+        for (int t = 0; t < B; ++t) {
+            if (!kTail || sb < nsb) {
+                const uint32_t* q = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)t * nsb + sb) * kQ8Bytes);
+                uint32_t w[9];
+#pragma unroll
+                for (int j = 0; j < 9; ++j) w[j] = __ldg(q + j);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    alo[i][t][j] = act_perm_lo(w[1 + j], w[5 + j]);
+                    ahi[i][t][j] = act_perm_hi(w[1 + j], w[5 + j]);
+                }
+                dx[i][t] = f16_bits_to_f32(w[0]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) alo[i][t][j] = ahi[i][t][j] = 0u;
+                dx[i][t] = 0.0f;
+            }
         }
-        named_barrier(1, nct);
+    }
+    // Activations are in registers: a dependent kernel may now overwrite the Q8_1 workspace.
+    grid_launch_dependents();
+    const uint8_t* lane_h = ring + (size_t)(slot * RPW) * a.rb + off_h;  // + stage, row, sub-block offsets
 
-        for (int tl = 0; tl < ntiles; ++tl) {
-            const int64_t row0 = r0 + (int64_t)tl * Cfg::kRT;
-            const int rows = (int)imin64(Cfg::kRT, r1 - row0);
-            float acc[RPL][B];
+    for (int t = 0; t < ntiles; ++t) {
+        const int s = (int)((uint32_t)t % stages);
+        const bool ready =
+            !*abort_flag && wait_sleep_or_abort(&full[s], ((uint32_t)t / stages) & 1u, abort_flag, a.err, kDevErrFullWait);
+        const int64_t row0 = r0 + (int64_t)t * R;
+        const int rows = (int)imin64(R, r1 - row0);
+        if (ready && slot * RPW < rows) {
+            const uint8_t* sbase = lane_h + (size_t)s * stage_bytes;
+            float acc[RPW][B];
 #pragma unroll
-            for (int j = 0; j < RPL; ++j)
+            for (int r = 0; r < RPW; ++r)
 #pragma unroll
-                for (int t = 0; t < B; ++t) acc[j][t] = 0.0f;
-
-            for (int c = 0; c < nchunks; ++c) {
-                const int s = (int)(it % stages);
-                const bool ready = !*abort_flag && wait_or_abort(&full[s], (it / stages) & 1u, abort_flag, a.err, kDevErrFullWait);
-                if (ready) {
-                    const int b0 = pb0 + c * KC;
-                    const int nblk = min(KC, pb1 - b0);
-                    const uint32_t stage = ring_base + (uint32_t)s * Cfg::kStageBytes;
-                    for (int cb = 0; cb < nblk; ++cb) {
-                        const int bl = b0 - pb0 + cb;
-                        uint32_t alo[B][4], ahi[B][4];
-                        float dx[B];
+                for (int tt = 0; tt < B; ++tt) acc[r][tt] = 0.0f;
 #pragma unroll
-                        for (int t = 0; t < B; ++t) {
-                            const uint32_t ab = act_base + (uint32_t)(t * a.kb_per_part + bl) * 256 + ib * 16;
-                            const uint4 l4 = lds_u4(ab), h4 = lds_u4(ab + 128);
-                            alo[t][0] = l4.x; alo[t][1] = l4.y; alo[t][2] = l4.z; alo[t][3] = l4.w;
-                            ahi[t][0] = h4.x; ahi[t][1] = h4.y; ahi[t][2] = h4.z; ahi[t][3] = h4.w;
-                            dx[t] = lds_f32(dx_base + (uint32_t)((t * a.kb_per_part + bl) * 8 + ib) * 4);
-                        }
+            for (int i = 0; i < SPL; ++i) {
+                if (!kTail || sb0 + 32 * i < nsb) {
 #pragma unroll
-                        for (int j = 0; j < RPL; ++j) {
-                            const int rloc = cw * Cfg::kRowsPerWarp + j * 4 + g;
-                            const uint32_t rb = stage + (uint32_t)rloc * Cfg::kRowStride + cb * kBlockBytes;
-                            const uint2 h = lds_u2(rb);
-                            const uint2 qa = lds_u2(rb + 8 + 16 * ib);
-                            const uint2 qb = lds_u2(rb + 16 + 16 * ib);
-                            // Weight side of the lookup, shared by all tokens.
-                            uint32_t wh[8], wl[8];
-                            const uint32_t qw[4] = {qa.x, qa.y, qb.x, qb.y};
+                    for (int r = 0; r < RPW; ++r) {
+                        // rows past the tile read stale shared memory; their sums are discarded
+                        const uint8_t* rowp = sbase + (size_t)r * a.rb + i * 4 * kBlockBytes;
+                        const uint2 h = *reinterpret_cast<const uint2*>(rowp);
+                        const uint2 qa = *reinterpret_cast<const uint2*>(rowp + (off_q - off_h));
+                        const uint2 qb = *reinterpret_cast<const uint2*>(rowp + (off_q - off_h) + 8);
+                        uint32_t wh[8], wl[8];
+                        lut_word(a.lut, qa.x, wh[0], wl[0], wh[1], wl[1]);
+                        lut_word(a.lut, qa.y, wh[2], wl[2], wh[3], wl[3]);
+                        lut_word(a.lut, qb.x, wh[4], wl[4], wh[5], wl[5]);
+                        lut_word(a.lut, qb.y, wh[6], wl[6], wh[7], wl[7]);
+                        const float dw = f16_bits_to_f32(h.x);
+                        const int scale = (int)(((h.y >> sh_lo) & 0xFu) | ((h.x >> sh_hi) & 0x30u)) - 32;
 #pragma unroll
-                            for (int w = 0; w < 4; ++w) {
-                                const uint32_t x = qw[w], xf = x ^ 0x88888888u;
-                                wh[2 * w] = prmt(kPosHi0, kPosHi1, xf);
-                                wl[2 * w] = prmt(kNegLo0, kNegLo1, x);
-                                wh[2 * w + 1] = prmt(kPosHi0, kPosHi1, xf >> 16);
-                                wl[2 * w + 1] = prmt(kNegLo0, kNegLo1, x >> 16);
+                        for (int tt = 0; tt < B; ++tt) {
+                            int s0 = dp4a((int)wh[0], (int)alo[i][tt][0], 0);
+                            int s1 = dp4a((int)wl[0], (int)alo[i][tt][0], 0);
+                            int s2 = dp4a((int)wh[1], (int)ahi[i][tt][0], 0);
+                            int s3 = dp4a((int)wl[1], (int)ahi[i][tt][0], 0);
+#pragma unroll
+                            for (int w = 1; w < 4; ++w) {
+                                s0 = dp4a((int)wh[2 * w], (int)alo[i][tt][w], s0);
+                                s1 = dp4a((int)wl[2 * w], (int)alo[i][tt][w], s1);
+                                s2 = dp4a((int)wh[2 * w + 1], (int)ahi[i][tt][w], s2);
+                                s3 = dp4a((int)wl[2 * w + 1], (int)ahi[i][tt][w], s3);
                             }
-                            const float dw = f16_bits_to_f32(h.x);
-                            const int scale = subblock_scale(h.x, h.y, ib) - 32;
+                            const int sumi = (s0 + s2) - (s1 + s3);
+                            if constexpr (kDebug) {
+                                if (slot * RPW + r < rows)
+                                    a.sumi[((int64_t)tt * a.N + row0 + slot * RPW + r) * nsb + sb0 + 32 * i] = sumi;
+                            }
+                            acc[r][tt] += (dw * dx[i][tt]) * (float)(sumi * scale);
+                        }
+                    }
+                }
+            }
 #pragma unroll
-                            for (int t = 0; t < B; ++t) {
-                                int sh = 0, sl = 0;
+            for (int r = 0; r < RPW; ++r) {
+                const int rl = slot * RPW + r;
 #pragma unroll
-                                for (int w = 0; w < 4; ++w) {
-                                    sh = dp4a((int)wh[2 * w], (int)alo[t][w], sh);
-                                    sl = dp4a((int)wl[2 * w], (int)alo[t][w], sl);
-                                    sh = dp4a((int)wh[2 * w + 1], (int)ahi[t][w], sh);
-                                    sl = dp4a((int)wl[2 * w + 1], (int)ahi[t][w], sl);
-                                }
-                                const int sumi = sh - sl;
-                                if constexpr (kDebug) {
-                                    if (rloc < rows)
-                                        a.sumi[((int64_t)t * a.N + row0 + rloc) * nsb + (int64_t)(b0 + cb) * 8 + ib] = sumi;
-                                }
-                                acc[j][t] += (dw * dx[t]) * (float)(sumi * scale);
+                for (int tt = 0; tt < B; ++tt) {
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) acc[r][tt] += __shfl_xor_sync(0xFFFFFFFFu, acc[r][tt], off);
+                }
+                if (rl >= rows) continue;
+                const int64_t row = row0 + rl;
+                if (KW == 1) {
+                    if (lane == 0 && a.y) {
+#pragma unroll
+                        for (int tt = 0; tt < B; ++tt) a.y[(int64_t)tt * a.N + row] = acc[r][tt];
+                    }
+                } else if (lane == 0) {
+                    float* pp = part + ((s * R + rl) * KW) * B;
+#pragma unroll
+                    for (int tt = 0; tt < B; ++tt) pp[kw * B + tt] = acc[r][tt];
+                    __threadfence_block();
+                    const uint32_t old = atomicAdd(&cnt[s * R + rl], 1u);
+                    if (old == (uint32_t)KW - 1) {
+                        __threadfence_block();
+                        cnt[s * R + rl] = 0u;
+                        if (a.y) {
+#pragma unroll
+                            for (int tt = 0; tt < B; ++tt) {
+                                float v = 0.0f;
+                                for (int k = 0; k < KW; ++k) v += reinterpret_cast<volatile float*>(pp)[k * B + tt];
+                                a.y[(int64_t)tt * a.N + row] = v;
                             }
                         }
                     }
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-                ++it;
-            }
-
-            // Reduce over the 8 sub-block lanes of each row and store.
-#pragma unroll
-            for (int j = 0; j < RPL; ++j) {
-                const int rloc = cw * Cfg::kRowsPerWarp + j * 4 + g;
-#pragma unroll
-                for (int t = 0; t < B; ++t) {
-                    float v = acc[j][t];
-                    v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
-                    v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
-                    v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
-                    if (ib == 0 && rloc < rows && !*abort_flag && a.y) {
-                        float* yp = a.y + (int64_t)t * a.N + row0 + rloc;
-                        *yp = (p == 0) ? v : (*yp + v);
-                    }
-                }
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
     }
 }
 
@@ -351,32 +353,52 @@ void device_limits(int dev, int* sms, int* smem_optin) {
     *smem_optin = g_max_smem[dev];
 }
 
+// Row-stage kernel configuration for batch B: 16 consumer warps, one row each per stage; KW warps
+// per row so that a lane holds at most SPLMAX(B) sub-blocks of activations in registers.
+constexpr int kRowNCW = 12, kRowRPW = 2;
+
+template <int B, int SPL, bool kDebug>
+void* rows_kernel_ptr(bool tail) {
+    return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, kDebug>
+                : (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, false, kDebug>;
+}
+
 template <int B, bool kDebug>
-cudaError_t launch_bulk(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int smem_optin) {
-    using Cfg = GemvCfg<B, kNCW, kRPL, kKC>;
-    // Activation part: all of K when it fits next to a 4-stage ring, otherwise even halves.
-    const int ring4 = 4 * Cfg::kStageBytes;
-    int kparts = 1, kbpp = a.kb;
-    while ((int)gemv_smem_layout<B, kNCW, kRPL, kKC>(kbpp, 4).total > smem_optin && kbpp > 2) {
-        ++kparts;
-        kbpp = (a.kb + kparts - 1) / kparts;
-        kbpp += kbpp & 1;
-    }
-    (void)ring4;
-    int stages = 4;
-    while (stages < kMaxStages && (int)gemv_smem_layout<B, kNCW, kRPL, kKC>(kbpp, stages + 1).total <= smem_optin) ++stages;
-    a.kparts = kparts;
-    a.kb_per_part = kbpp;
+cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int smem_optin) {
+    constexpr int NCW = kRowNCW, RPW = kRowRPW;
+    const int nsb = a.K / kQK8;
+    const int spl_max = (B == 1) ? 5 : 2;
+    int kw = 1;
+    while (kw < 4 && (nsb + 32 * kw - 1) / (32 * kw) > spl_max) kw *= 2;
+    const int spl = (nsb + 32 * kw - 1) / (32 * kw);
+    if (spl > spl_max)  // K too long for register-resident activations: tensor-core kernel
+        return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.tickets, a.partials, a.partial_bytes, a.K, a.N,
+                               B, stream, pdl, sms, smem_optin, a.err, a.lut);
+    const bool tail = (nsb != 32 * kw * spl);
+    const int R = (NCW / kw) * RPW;
+    a.kw = kw;
+    a.rows_per_stage = R;
+    const int64_t stage_bytes = (int64_t)R * a.rb;
+    int stages = kMaxStages;
+    while (stages > 2 && (int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes).total > smem_optin) --stages;
     a.stages = stages;
-    const SmemLayout L = gemv_smem_layout<B, kNCW, kRPL, kKC>(kbpp, stages);
-    if ((int)L.total > smem_optin) return cudaErrorInvalidConfiguration;
-    auto kern = gemv_iq4xs_q8_kernel<B, kNCW, kRPL, kKC, kDebug>;
+    const RowSmem L = gemv_row_smem(B, R, kw, stages, stage_bytes);
+    if ((int64_t)L.total > smem_optin || stage_bytes >= (1 << 20)) return cudaErrorInvalidConfiguration;
+    void* kern = nullptr;
+    switch (spl) {
+        case 1: kern = rows_kernel_ptr<B, 1, kDebug>(tail); break;
+        case 2: kern = rows_kernel_ptr<B, 2, kDebug>(tail); break;
+        case 3: kern = B == 1 ? rows_kernel_ptr<1, 3, kDebug>(tail) : nullptr; break;
+        case 4: kern = B == 1 ? rows_kernel_ptr<1, 4, kDebug>(tail) : nullptr; break;
+        case 5: kern = B == 1 ? rows_kernel_ptr<1, 5, kDebug>(tail) : nullptr; break;
+        default: break;
+    }
+    if (!kern) return cudaErrorInvalidConfiguration;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
-    const int grid = (int)imin64((int64_t)sms, a.N);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(Cfg::kThreads);
+    cfg.gridDim = dim3((unsigned)imin64((int64_t)sms, a.N));
+    cfg.blockDim = dim3(32 * (NCW + 1));
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -384,7 +406,8 @@ cudaError_t launch_bulk(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, a);
+    void* args[] = {&a};
+    return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
 template <int B, bool kDebug>
@@ -410,25 +433,26 @@ cudaError_t dispatch(int B, GemvArgs a, cudaStream_t stream, bool pdl) {
     int sms = 0, smem_optin = 0;
     device_limits(dev, &sms, &smem_optin);
     const bool bulk_ok = (a.kb % 2 == 0) && ((reinterpret_cast<uintptr_t>(a.W) & 15u) == 0) && !a.force_generic;
-    switch (B) {
-#define IQ4XS_CASE(BB)                                                                                 \
-    case BB:                                                                                           \
-        return bulk_ok ? launch_bulk<BB, kDebug>(a, stream, pdl, sms, smem_optin)                      \
-                       : launch_generic<BB, kDebug>(a, stream, pdl, sms);
-        IQ4XS_CASE(1)
-        IQ4XS_CASE(2)
-        IQ4XS_CASE(3)
-        IQ4XS_CASE(4)
-        IQ4XS_CASE(5)
-        IQ4XS_CASE(6)
-        IQ4XS_CASE(7)
-        IQ4XS_CASE(8)
-#undef IQ4XS_CASE
-        default:
-            return cudaErrorInvalidValue;
+    if (!bulk_ok) {
+        switch (B) {
+#define IQ4XS_GEN(BB) case BB: return launch_generic<BB, kDebug>(a, stream, pdl, sms);
+            IQ4XS_GEN(1) IQ4XS_GEN(2) IQ4XS_GEN(3) IQ4XS_GEN(4) IQ4XS_GEN(5) IQ4XS_GEN(6) IQ4XS_GEN(7) IQ4XS_GEN(8)
+#undef IQ4XS_GEN
+            default: return cudaErrorInvalidValue;
+        }
     }
+    if (B == 1) return launch_rows<1, kDebug>(a, stream, pdl, sms, smem_optin);
+    return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.tickets, a.partials, a.partial_bytes, a.K, a.N, B,
+                           stream, pdl, sms, smem_optin, a.err, a.lut);
 }
 }  // namespace
+
+int device_sm_count() {
+    int dev = 0, sms = 0, smem = 0;
+    cudaGetDevice(&dev);
+    device_limits(dev, &sms, &smem);
+    return sms;
+}
 
 cudaError_t launch_gemv_q8(GemvArgs a, int B, cudaStream_t stream, bool pdl) {
     a.sumi = nullptr;

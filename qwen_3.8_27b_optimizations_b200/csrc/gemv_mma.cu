@@ -1,0 +1,397 @@
+// gemv_mma.cu -- IQ4_XS x Q8_1 decode GEMV for batch 2..8 on the tensor cores (mma.sync m16n8k32 s8).
+//
+// Same arithmetic contract as the dp4a GEMV (real_stock_dp4a_comparator.hip:145-166 per sub-block):
+// the int32 dot of one 32-weight sub-block with one Q8_1 block is exact, then
+// term = (d_w*(ls-32)) * d_x * sumi in fp32, summed over sub-blocks.
+//
+//  * The weight matrix is viewed as a 3-D tensor of uint64 [N rows][K/512 super-block pairs][34]
+//    (one pair = 272 bytes) and staged by TMA (cp.async.bulk.tensor.3d, no multicast) in units of
+//    16 rows x `pk` pairs.  pk is odd, so the shared-memory row pitch pk*272 bytes = 68*pk words is an
+//    odd multiple of 4 words: the 8 rows of an MMA fragment load hit 8 disjoint 4-bank groups.
+//    Rows and pairs past the matrix are zero-filled by TMA and never read from memory.
+//  * Work unit = (16-row tile, K part of pk pairs), ordered part-major and split in balanced
+//    contiguous ranges over one CTA per SM.  With more than one part, a tile's parts leave partial
+//    sums in the workspace and the last CTA to finish the tile (global ticket) adds them in part
+//    order: deterministic.
+//  * Warp w of 8 consumer warps handles sub-block ib = w of every super-block of the part.  Lane
+//    (g = lane/4, c = lane%4) holds A = qs word c of sub-block ib for rows g and g+8, expanded by
+//    the split codebook lookup (prmt tables -kv[0..7] and kv[8..15], zero elsewhere) into two A
+//    fragments H (codes >= 8) and L (codes < 8); B = the 8 tokens' Q8_1 values of the sub-block in
+//    the lookup's k order (staged once per part in shared memory); sumi = MMA(H,B) - MMA(L,B).
+//  * The 8 warps' partial tiles are combined in shared memory by the last warp to finish the
+//    unit (shared-memory ticket), again in warp order.
+//  * Every mbarrier wait is bounded (sleeping try_wait, error word, drain before exit).
+#include <cuda.h>
+
+#include "iq4xs_device.cuh"
+#include "iq4xs_kernels.h"
+
+namespace iq4xs {
+
+namespace {
+constexpr int kMmaStages = 8;  // one stage per consumer warp in flight
+constexpr int kNCW = 8;        // consumer warps
+
+struct MmaSmem {
+    uint32_t bar_off, flag_off, act_off, dx_off, ring_off, total;
+};
+
+// act: per staged part (up to 2) and sub-block: 32 lanes x uint2 (B fragment words) = 256 B;
+// dx: 8 fp32 per sub-block; ring: kMmaStages x (16 rows x pk pairs x 272 B).
+__host__ __device__ inline MmaSmem mma_smem(int pk) {
+    MmaSmem L;
+    L.bar_off = 0;
+    L.flag_off = 2 * kMmaStages * 8;
+    L.act_off = 256;
+    L.dx_off = L.act_off + 2u * (uint32_t)pk * 16 * 256;
+    L.ring_off = (L.dx_off + 2u * (uint32_t)pk * 16 * 32 + 127) & ~127u;
+    L.total = L.ring_off + (uint32_t)kMmaStages * 16u * (uint32_t)pk * 272u;
+    return L;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t hi16(uint32_t x) {
+    uint32_t d;
+    asm("mul.hi.u32 %0, %1, 65536;" : "=r"(d) : "r"(x));
+    return d;
+}
+
+__device__ __forceinline__ bool wait_sleep(uint64_t* bar, uint32_t parity, volatile uint32_t* flag, uint32_t* err,
+                                           uint32_t code) {
+    for (uint32_t i = 0; i < 20000u; ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+        if (*flag) return false;
+    }
+    record_error(err, code);
+    *flag = 1u;
+    return false;
+}
+}  // namespace
+
+template <int B, bool kDebug>
+__global__ void __launch_bounds__(32 * (kNCW + 1), 1)
+    gemv_iq4xs_q8_mma_kernel(const __grid_constant__ CUtensorMap tmap, const GemvMmaArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int pk = a.pk, P = a.parts;
+    const MmaSmem L = mma_smem(pk);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+    uint64_t* empty = full + kMmaStages;
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.flag_off);
+    uint8_t* ring = smem + L.ring_off;
+    const uint32_t stage_bytes = 16u * (uint32_t)pk * 272u;
+    const uint32_t row_pitch = (uint32_t)pk * 272u;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t T = (a.N + 15) / 16;
+    const int64_t U = T * P;
+    const int64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+    const int nunits = (int)(u1 - u0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kMmaStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        *abort_flag = 0u;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ producer
+        if (lane == 0) {
+            const uint64_t policy = l2_policy_evict_first();
+            int it = 0;
+            for (; it < nunits; ++it) {
+                const int s = it % kMmaStages;
+                const uint32_t use = (uint32_t)(it / kMmaStages);
+                if (use > 0 && !wait_sleep(&empty[s], (use - 1) & 1u, abort_flag, a.err, kDevErrEmptyWait)) break;
+                const int64_t u = u0 + it;
+                const int p = (int)(u / T);
+                const int64_t t = u - (int64_t)p * T;
+                mbar_arrive_expect_tx(&full[s], stage_bytes);
+                tma_load_3d(ring + (size_t)s * stage_bytes, &tmap, 0, p * pk, (int)(t * 16), &full[s], policy);
+            }
+            const int first = it > kMmaStages ? it - kMmaStages : 0;
+            for (int j = first; j < it; ++j) {
+                bool landed = false;
+                for (uint32_t i = 0; i < 20000u && !landed; ++i)
+                    landed = mbar_try_wait_sleep(&full[j % kMmaStages], (uint32_t)(j / kMmaStages) & 1u, 1000000u);
+                if (!landed) record_error(a.err, kDevErrDrainWait);
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------------- consumers
+    const int cw = warp - 1;
+    const int g = lane >> 2, c = lane & 3;
+    const int ctid = threadIdx.x - 32, nct = kNCW * 32;
+    const int nsb = a.K / kQK8;
+    const uint2* act = reinterpret_cast<const uint2*>(smem + L.act_off);
+    const float* dxs = reinterpret_cast<const float*>(smem + L.dx_off);
+
+    // Stage the activations of the (at most two) parts this CTA touches as MMA B fragments in the
+    // lookup's k order: slot = part - first part.
+    grid_dependency_wait();
+    const int pfirst = nunits > 0 ? (int)(u0 / T) : 0;
+    const int plast = nunits > 0 ? (int)((u1 - 1) / T) : -1;
+    for (int slot = 0; slot <= plast - pfirst && slot < 2; ++slot) {
+        const int p = pfirst + slot;
+        const int nsub = 16 * min(pk, a.pairs - p * pk);
+        const int sb_base = p * pk * 16;
+        for (int e = ctid; e < nsub * 8; e += nct) {
+            const int sbl = e >> 3, n = e & 7;
+            uint2 frag[4] = {make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u)};
+            float dxv = 0.0f;
+            if (n < B) {
+                const uint32_t* q = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb_base + sbl) * kQ8Bytes);
+                uint32_t w[9];
+#pragma unroll
+                for (int j = 0; j < 9; ++j) w[j] = __ldg(q + j);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) frag[j] = make_uint2(act_perm_lo(w[1 + j], w[5 + j]), act_perm_hi(w[1 + j], w[5 + j]));
+                dxv = f16_bits_to_f32(w[0]);
+            }
+            uint2* dst = reinterpret_cast<uint2*>(smem + L.act_off) + (slot * pk * 16 + sbl) * 32 + n * 4;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dst[j] = frag[j];
+            reinterpret_cast<float*>(smem + L.dx_off)[(slot * pk * 16 + sbl) * 8 + n] = dxv;
+        }
+    }
+    named_barrier(1, nct);
+    grid_launch_dependents();  // the workspace activations are no longer read
+
+    // Warp cw owns units it = cw, cw + 8, ... of this CTA: all 16 rows x all sub-blocks of the part.
+    for (int it = cw; it < nunits; it += kNCW) {
+        const int s = it % kMmaStages;
+        const int64_t u = u0 + it;
+        const int p = (int)(u / T);
+        const int64_t t = u - (int64_t)p * T;
+        const int nsup = 2 * min(pk, a.pairs - p * pk);
+        const int slot = p - pfirst;
+        const bool ready = !*abort_flag &&
+                           wait_sleep(&full[s], (uint32_t)(it / kMmaStages) & 1u, abort_flag, a.err, kDevErrFullWait);
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (ready) {
+            const uint8_t* rg = ring + (size_t)s * stage_bytes + (size_t)g * row_pitch;
+            const uint8_t* rg8 = rg + 8 * row_pitch;
+            const uint2* actp = act + (size_t)slot * pk * 16 * 32 + lane;
+            const float* dxp = dxs + (size_t)slot * pk * 16 * 8 + 2 * c;
+            for (int j = 0; j < nsup; ++j) {
+                const uint8_t* b0p = rg + j * kBlockBytes;
+                const uint8_t* b8p = rg8 + j * kBlockBytes;
+                const uint2 h0 = *reinterpret_cast<const uint2*>(b0p);
+                const uint2 h8 = *reinterpret_cast<const uint2*>(b8p);
+                const float dw0 = f16_bits_to_f32(h0.x), dw8 = f16_bits_to_f32(h8.x);
+#pragma unroll
+                for (int ib = 0; ib < 8; ++ib) {
+                    const int sbl = j * 8 + ib;
+                    const uint32_t x0 = *reinterpret_cast<const uint32_t*>(b0p + 8 + 16 * ib + 4 * c);
+                    const uint32_t x8 = *reinterpret_cast<const uint32_t*>(b8p + 8 + 16 * ib + 4 * c);
+                    const uint2 bf = actp[sbl * 32];
+                    const float2 dx = *reinterpret_cast<const float2*>(dxp + sbl * 8);
+                    const uint32_t xf0 = x0 ^ 0x88888888u, xf8 = x8 ^ 0x88888888u;
+                    const uint32_t ah[4] = {prmt(a.lut[2], a.lut[3], xf0), prmt(a.lut[2], a.lut[3], xf8),
+                                            prmt(a.lut[2], a.lut[3], hi16(xf0)), prmt(a.lut[2], a.lut[3], hi16(xf8))};
+                    const uint32_t al[4] = {prmt(a.lut[0], a.lut[1], x0), prmt(a.lut[0], a.lut[1], x8),
+                                            prmt(a.lut[0], a.lut[1], hi16(x0)), prmt(a.lut[0], a.lut[1], hi16(x8))};
+                    int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
+                    mma_s8(dh, ah, bf.x, bf.y);
+                    mma_s8(dl, al, bf.x, bf.y);
+                    const int ls0 = (int)(((h0.y >> (4 * ib)) & 0xFu) | ((h0.x >> (12 + 2 * ib)) & 0x30u));
+                    const int ls8 = (int)(((h8.y >> (4 * ib)) & 0xFu) | ((h8.x >> (12 + 2 * ib)) & 0x30u));
+                    const float f0 = dw0 * (float)(ls0 - 32), f8 = dw8 * (float)(ls8 - 32);
+                    const int s0 = dh[0] - dl[0], s1 = dh[1] - dl[1], s2 = dh[2] - dl[2], s3 = dh[3] - dl[3];
+                    if constexpr (kDebug) {
+                        const int64_t r0w = t * 16 + g, r8w = r0w + 8;
+                        const int sbg = p * pk * 16 + sbl;
+                        if (2 * c < B && r0w < a.N) a.sumi[((int64_t)(2 * c) * a.N + r0w) * nsb + sbg] = s0;
+                        if (2 * c + 1 < B && r0w < a.N) a.sumi[((int64_t)(2 * c + 1) * a.N + r0w) * nsb + sbg] = s1;
+                        if (2 * c < B && r8w < a.N) a.sumi[((int64_t)(2 * c) * a.N + r8w) * nsb + sbg] = s2;
+                        if (2 * c + 1 < B && r8w < a.N) a.sumi[((int64_t)(2 * c + 1) * a.N + r8w) * nsb + sbg] = s3;
+                    }
+                    acc[0] += (f0 * dx.x) * (float)s0;
+                    acc[1] += (f0 * dx.y) * (float)s1;
+                    acc[2] += (f8 * dx.x) * (float)s2;
+                    acc[3] += (f8 * dx.y) * (float)s3;
+                }
+            }
+        }
+        // The stage can be refilled as soon as this warp is done reading it.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+
+        const int64_t r0w = t * 16 + g, r8w = r0w + 8;
+        const int tk[4] = {2 * c, 2 * c + 1, 2 * c, 2 * c + 1};
+        const int64_t rw[4] = {r0w, r0w, r8w, r8w};
+        if (ready && a.y) {
+            if (P == 1) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (tk[k] < B && rw[k] < a.N) a.y[(int64_t)tk[k] * a.N + rw[k]] = acc[k];
+            } else {
+                // Partial sums of this part; the last of the P units of the tile adds them in part order.
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (tk[k] < B && rw[k] < a.N) a.partial[((int64_t)p * B + tk[k]) * a.N + rw[k]] = acc[k];
+                __threadfence();
+                __syncwarp();
+                uint32_t told = 0;
+                if (lane == 0) told = atomicAdd(&a.tile_cnt[t], 1u);
+                told = __shfl_sync(0xFFFFFFFFu, told, 0);
+                if (told == (uint32_t)P - 1) {
+                    __threadfence();
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        if (tk[k] < B && rw[k] < a.N) {
+                            float sum = 0.0f;
+                            for (int q = 0; q < P; ++q) sum += __ldcg(a.partial + ((int64_t)q * B + tk[k]) * a.N + rw[k]);
+                            a.y[(int64_t)tk[k] * a.N + rw[k]] = sum;
+                        }
+                    }
+                    if (lane == 0) a.tile_cnt[t] = 0u;
+                }
+            }
+        }
+    }
+}
+
+// --------------------------------------------------------------------------------------------
+// Host side: tensor map, part choice, launch.
+namespace {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Part size: odd number of pairs pk <= 5 (8 stages + two parts of activations fit in shared
+// memory).  A unit runs on one warp: cost of the busiest warp = units per warp x (pk + overhead),
+// the overhead of a unit (stage latency, stores, ticket) counted as 0.75 pairs.
+int choose_pk(int pairs, int64_t tiles, int ctas) {
+    if (ctas < 1) ctas = 1;
+    int best = 1;
+    double best_cost = 1e300;
+    for (int pk = 5; pk >= 1; pk -= 2) {
+        const int parts = (pairs + pk - 1) / pk;
+        const int64_t U = tiles * parts;
+        const int64_t per = (U + (int64_t)ctas * kNCW - 1) / ((int64_t)ctas * kNCW);
+        const double cost = (double)per * ((double)pk + 0.75) + (parts > 1 ? 0.25 : 0.0);
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = pk;
+        }
+    }
+    return best;
+}
+}  // namespace
+
+// Upper bound over every part choice (one part per pair), so the size does not depend on the device.
+size_t gemv_mma_partial_bytes(int64_t K, int64_t N, int B) {
+    if (K % 512 != 0 || K < 1024) return 0;
+    return (size_t)(K / 512) * B * N * sizeof(float);
+}
+
+template <int B, bool kDebug>
+static cudaError_t launch_mma_b(const CUtensorMap& map, GemvMmaArgs a, int smem, cudaStream_t stream, bool pdl, int grid) {
+    auto kern = gemv_iq4xs_q8_mma_kernel<B, kDebug>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(32 * (kNCW + 1));
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, map, a);
+}
+
+cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32_t* sumi, uint32_t* tickets,
+                            float* partials, size_t partial_bytes, int64_t K, int64_t N, int B, cudaStream_t stream,
+                            bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4]) {
+    if (B < 1 || B > 8 || K % 512 != 0 || (reinterpret_cast<uintptr_t>(W) & 15u)) return cudaErrorInvalidValue;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    const int pairs = (int)(K / 512);
+    const int64_t T = (N + 15) / 16;
+    const int pk = choose_pk(pairs, T, sms);
+    const int parts = (pairs + pk - 1) / pk;
+    if (parts > 1 && y) {  // partial sums and per-tile tickets (the debug path writes neither)
+        if (!tickets || !partials || partial_bytes < (size_t)parts * B * N * sizeof(float)) return cudaErrorInvalidValue;
+        if (T > (int64_t)(kTicketBytes / sizeof(uint32_t))) return cudaErrorInvalidValue;
+    }
+    const MmaSmem L = mma_smem(pk);
+    if ((int)L.total > smem_optin) return cudaErrorInvalidConfiguration;
+
+    CUtensorMap map;
+    const cuuint64_t dims[3] = {34, (cuuint64_t)pairs, (cuuint64_t)N};
+    const cuuint64_t strides[2] = {272, (cuuint64_t)pairs * 272};
+    const cuuint32_t box[3] = {34, (cuuint32_t)pk, 16};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(W), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+
+    GemvMmaArgs a = {};
+    a.q8 = q8;
+    a.y = y;
+    a.sumi = sumi;
+    a.err = err;
+    a.N = N;
+    a.K = (int)K;
+    a.pairs = pairs;
+    a.pk = pk;
+    a.parts = parts;
+    a.stages = kMmaStages;
+    a.partial = partials;
+    a.tile_cnt = tickets;
+    for (int i = 0; i < 4; ++i) a.lut[i] = lut[i];
+    const int64_t U = T * parts;
+    // A CTA holds the activations of at most two parts: its unit range must not exceed T units.
+    int64_t grid64 = std::min<int64_t>(sms, U);
+    while ((U + grid64 - 1) / grid64 > T) ++grid64;
+    const int grid = (int)grid64;
+    switch (B) {
+#define IQ4XS_MMA_B(BB)                                                                         \
+    case BB:                                                                                    \
+        return sumi ? launch_mma_b<BB, true>(map, a, (int)L.total, stream, pdl, grid)          \
+                    : launch_mma_b<BB, false>(map, a, (int)L.total, stream, pdl, grid);
+        IQ4XS_MMA_B(1) IQ4XS_MMA_B(2) IQ4XS_MMA_B(3) IQ4XS_MMA_B(4)
+        IQ4XS_MMA_B(5) IQ4XS_MMA_B(6) IQ4XS_MMA_B(7) IQ4XS_MMA_B(8)
+#undef IQ4XS_MMA_B
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace iq4xs

@@ -20,11 +20,43 @@ struct GemvArgs {
     int kb_per_part;     // set by the launcher
     int stages;          // set by the launcher
     int force_generic;   // test hook: take the direct-load kernel
+    int kw;              // row kernel: warps per row (set by the launcher)
+    int rows_per_stage;  // row kernel: rows per stage (set by the launcher)
+    uint32_t lut[4];     // codebook prmt tables {neg_lo0, neg_lo1, pos_hi0, pos_hi1} (read from the param bank)
+    uint32_t* tickets;   // tensor-core kernel: per-tile tickets (zero between calls)
+    float* partials;     // tensor-core kernel: cross-CTA partial sums
+    size_t partial_bytes;
 };
 
+struct GemvMmaArgs {
+    const uint8_t* q8;   // Q8_1 blocks [B][K/32][36]
+    float* y;            // [B][N]; nullptr: debug sums only
+    float* partial;      // [parts][B][N] when parts > 1
+    uint32_t* tile_cnt;  // [ceil(N/16)] tickets, zero between calls
+    int32_t* sumi;       // debug only
+    uint32_t* err;
+    int64_t N;
+    int K;
+    int pairs;           // K/512 super-block pairs per row
+    int pk;              // pairs per part (odd)
+    int parts;
+    int stages;
+    uint32_t lut[4];
+};
+
+// Tensor-core GEMV (batch 1..8).  Workspace = [tickets: kTicketBytes, zero between calls][partials].
+constexpr size_t kTicketBytes = 64 * 1024;  // one uint32 per 16-row tile: N <= 262144
+size_t gemv_mma_partial_bytes(int64_t K, int64_t N, int B);
+cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32_t* sumi, uint32_t* tickets,
+                            float* partials, size_t partial_bytes, int64_t K, int64_t N, int B, cudaStream_t stream,
+                            bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4]);
+int device_sm_count();
+
 // Q8_1 quantizer.  Element (m, k) of X is at X[m*stride_m + k*stride_k]; output blocks [M][K/32].
+// pdl: launch with programmatic stream serialization (the kernel waits on griddepcontrol before
+// reading X, so it may overlap the tail of the preceding kernel).
 cudaError_t launch_q8_1_quantize(const float* X, uint8_t* q8, int64_t K, int64_t M, int64_t stride_m,
-                                 int64_t stride_k, cudaStream_t stream, bool signal_dependents);
+                                 int64_t stride_k, cudaStream_t stream, bool signal_dependents, bool pdl = false);
 
 cudaError_t launch_gemv_q8(GemvArgs a, int B, cudaStream_t stream, bool pdl);
 cudaError_t launch_gemv_q8_debug(GemvArgs a, int B, cudaStream_t stream);

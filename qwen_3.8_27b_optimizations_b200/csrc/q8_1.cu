@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restr
                                                             int64_t K, int64_t M, int64_t stride_m,
                                                             int64_t stride_k, int signal_dependents) {
     if (signal_dependents) grid_launch_dependents();
+    grid_dependency_wait();  // X may be the output of the preceding kernel (no-op without PDL)
     const unsigned full = 0xFFFFFFFFu;
     const int lane = threadIdx.x & 31;
     const int64_t nb = K / kQK8;
@@ -46,14 +47,22 @@ __global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restr
 }
 
 cudaError_t launch_q8_1_quantize(const float* X, uint8_t* q8, int64_t K, int64_t M, int64_t stride_m,
-                                 int64_t stride_k, cudaStream_t stream, bool signal_dependents) {
+                                 int64_t stride_k, cudaStream_t stream, bool signal_dependents, bool pdl) {
     const int64_t total = (K / kQK8) * M;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t grid = std::min<int64_t>((total + 7) / 8, (int64_t)sms * 16);
-    q8_1_quantize_kernel<<<(unsigned)grid, 256, 0, stream>>>(X, q8, K, M, stride_m, stride_k, signal_dependents ? 1 : 0);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, q8_1_quantize_kernel, X, q8, K, M, stride_m, stride_k, signal_dependents ? 1 : 0);
 }
 
 }  // namespace iq4xs

@@ -53,16 +53,18 @@ FAKE = 0x10000  # never dereferenced: validation fails first
 
 def test_validation_before_any_launch(pkg):
     L = pkg.lib()
-    assert L.iq4xs_gemv_q8(None, FAKE, FAKE, 512, 64, 1, None) == 1
-    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 500, 64, 1, None) == 2      # K % 256
-    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 0, 1, None) == 1       # N <= 0
-    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 9, None) == 2      # batch > 8
-    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 0, None) == 2      # batch < 1
-    assert L.iq4xs_gemv_q8(FAKE + 4, FAKE, FAKE, 512, 64, 1, None) == 3  # W not 8-byte aligned
-    need = L.iq4xs_gemv_workspace_bytes(512, 2)
-    assert need == 2 * 16 * 36
-    assert L.iq4xs_gemv_f32(FAKE, FAKE, FAKE, 512, 64, 2, FAKE, need - 1, None) == 4
+    big = 1 << 30
+    assert L.iq4xs_gemv_q8(None, FAKE, FAKE, 512, 64, 1, FAKE, big, None) == 1
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 500, 64, 1, FAKE, big, None) == 2      # K % 256
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 0, 1, FAKE, big, None) == 1       # N <= 0
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 9, FAKE, big, None) == 2      # batch > 8
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 0, FAKE, big, None) == 2      # batch < 1
+    assert L.iq4xs_gemv_q8(FAKE + 4, FAKE, FAKE, 512, 64, 1, FAKE, big, None) == 3  # W not 8-byte aligned
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 1, FAKE, 0, None) == 4        # no workspace room
     assert L.iq4xs_q8_1_quantize(None, FAKE, 512, 1, None) == 1
+    need = L.iq4xs_gemv_workspace_bytes(512, 64, 2)
+    assert need >= 64 * 1024 + 2 * 16 * 36
+    assert L.iq4xs_gemv_f32(FAKE, FAKE, FAKE, 512, 64, 2, FAKE, need - 1, None) == 4
     assert L.iq4xs_q8_1_quantize(FAKE, FAKE, 100, 1, None) == 2
     assert L.iq4xs_q8_1_bytes(5120, 3) == 3 * 160 * 36
     assert L.iq4xs_quantize_weights(FAKE, FAKE, 4, 300, None) == 2

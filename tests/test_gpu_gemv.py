@@ -137,10 +137,16 @@ def test_gemv_full_size(pkg, O, name, B):
     check_close(O, Y.cpu().numpy()[:, rows], Y64, A, K, f"{name} B={B} sampled")
     S = pkg.debug_subblock_dots(Wr, q8, K, len(rows), B).cpu().numpy()
     assert np.array_equal(S, O.subblock_dots(Wr.cpu().numpy(), Qh, K, len(rows), B))
-    # row-range independence: a sub-matrix gives the same bits for its rows
-    r0, r1 = N // 3, N // 3 + 777
+    # row-range independence: a sub-matrix gives the same rows (bit for bit with the batch-1 kernel,
+    # whose per-row order does not depend on N; within tolerance for the tensor-core kernel, whose
+    # K-part grouping is chosen per shape)
+    r0 = N // 3
+    r1 = min(N, r0 + 777)
     Ys = pkg.gemv_q8(W[r0:r1].contiguous(), q8, K, r1 - r0, B)
-    assert torch.equal(Ys, Y[:, r0:r1])
+    if B == 1:
+        assert torch.equal(Ys, Y[:, r0:r1])
+    else:
+        check_close(O, Ys.cpu().numpy(), T64.cpu().numpy()[:, r0:r1], TA.cpu().numpy()[:, r0:r1], K, f"{name} slice")
     no_device_error(pkg)
 
 
@@ -195,13 +201,15 @@ def test_invalid_arguments_on_device(pkg, O):
     q8 = pkg.q8_1_quantize(dev(O.normal(K, 2)[None]))
     y = torch.empty(N, dtype=torch.float32, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
-    assert L.iq4xs_gemv_q8(W.data_ptr() + 4, q8.data_ptr(), y.data_ptr(), K, N, 1, s) == 3
-    assert L.iq4xs_gemv_q8(W.data_ptr(), q8.data_ptr(), y.data_ptr(), K, N, 9, s) == 2
+    ws = torch.zeros(pkg.gemv_q8_workspace_bytes(K, N, 1), dtype=torch.uint8, device="cuda")
+    wsb = ws.numel()
+    assert L.iq4xs_gemv_q8(W.data_ptr() + 4, q8.data_ptr(), y.data_ptr(), K, N, 1, ws.data_ptr(), wsb, s) == 3
+    assert L.iq4xs_gemv_q8(W.data_ptr(), q8.data_ptr(), y.data_ptr(), K, N, 9, ws.data_ptr(), wsb, s) == 2
     # 8-byte aligned but not 16: served by the direct-load kernel, same result
     buf = torch.empty(W.numel() + 8, dtype=torch.uint8, device="cuda")
     buf[8:] = W.view(-1)
     y8 = torch.empty(N, dtype=torch.float32, device="cuda")
-    assert L.iq4xs_gemv_q8(buf.data_ptr() + 8, q8.data_ptr(), y8.data_ptr(), K, N, 1, s) == 0
+    assert L.iq4xs_gemv_q8(buf.data_ptr() + 8, q8.data_ptr(), y8.data_ptr(), K, N, 1, ws.data_ptr(), wsb, s) == 0
     yg = pkg.gemv_q8(W, q8, K, N, 1, generic=True)
     assert torch.equal(y8, yg[0])
     no_device_error(pkg)
@@ -211,7 +219,7 @@ def test_cuda_graph_capture_replays_bit_exact(pkg, O):
     K, N, B = 5120, 8192, 2
     W = pkg.random_weights(N, K, seed=9)
     X = pkg.fill_normal(B * K, seed=10).view(B, K)
-    ws = torch.empty(pkg.gemv_workspace_bytes(K, B), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(pkg.gemv_workspace_bytes(K, N, B), dtype=torch.uint8, device="cuda")
     Y = torch.empty((B, N), dtype=torch.float32, device="cuda")
     pkg.gemv(W, X, N, workspace=ws, out=Y)
     ref = Y.clone()
