@@ -84,51 +84,90 @@ def ncu_traffic():
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock, max clock and throttle reasons during the timed region: NVML polled from a
+    thread every 2 ms (the timed regions are short), nvidia-smi -lms 200 as a fallback."""
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.proc = None
+    def __init__(self, torch_device_index: int):
+        self.idx = torch_device_index
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._proc = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.idx)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.idx)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            masks = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
+            self._stop = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        for name, m in masks.items():
+                            if r & m:
+                                self.reasons.add(name)
+                    except Exception:
+                        pass
+                    self._stop.wait(0.002)
+
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                      "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            try:
+                self._proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
+                                               "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                              stderr=subprocess.DEVNULL, text=True)
+            except Exception:
+                self._proc = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                out, _ = self._proc.communicate(timeout=5)
             except Exception:
-                self.proc.kill()
+                self._proc.kill()
                 out = ""
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for l in out.splitlines():
+                f = [x.strip() for x in l.split(",")]
+                if len(f) < 6:
+                    continue
+                try:
+                    self.samples.append(float(f[0]))
+                    self.max_mhz = max(self.max_mhz or 0.0, float(f[1]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[2:6]):
+                    if v.lower() == "active":
+                        self.reasons.add(n)
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
-            f = [x.strip() for x in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 # ----------------------------------------------------------------------------- reference arm (CPU)
@@ -201,7 +240,7 @@ def reference_arm(args, rank: int, world: int):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=256, help="rows per shape in the CPU samples")
@@ -291,23 +330,32 @@ def main():
     value_gbs = world * sb * args.steps / (ms_max * 1e-3) / 1e9
     clocks = clk.summary()
 
-    # ---- roofline: the GEMV kernel alone, per launch, on its stream
+    # ---- roofline: the GEMV kernel alone (no quantizer), per launch: a CUDA graph of `reps`
+    # back-to-back launches over the two weight copies, timed with events on its stream
     per = []
     q8s = {(B, i): P.q8_1_quantize(X[(B, i)], stream=stream) for B in BATCHES for i in range(len(SHAPES))}
     stream.synchronize()
-    reps = 20
+    reps = 10
     tot_bytes, tot_ms = 0, 0.0
     with torch.cuda.stream(stream):
         for B in BATCHES:
             for i, (name, N, K) in enumerate(SHAPES):
-                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-                for r in range(reps):
-                    a, b = evs[r]
-                    a.record(stream)
-                    P.gemv_q8(weights[r % 2][i], q8s[(B, i)], K, N, B, out=Y[(B, i)], stream=stream)
-                    b.record(stream)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for r in range(reps):
+                        P.gemv_q8(weights[r % 2][i], q8s[(B, i)], K, N, B, out=Y[(B, i)], stream=stream, workspace=ws)
+                g.replay()
                 stream.synchronize()
-                d = statistics.median([a.elapsed_time(b) for a, b in evs[2:]])
+                ts = []
+                for _ in range(3):
+                    a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a0.record(stream)
+                    g.replay()
+                    b0.record(stream)
+                    stream.synchronize()
+                    ts.append(a0.elapsed_time(b0) / reps)
+                del g
+                d = statistics.median(ts)
                 nb = gemv_bytes(N, K, B)
                 per.append({"shape": name, "B": B, "us": round(d * 1e3, 2), "gbs": round(nb / (d * 1e-3) / 1e9, 1)})
                 tot_bytes += nb
@@ -381,7 +429,8 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic.get("bytes_per_launch_weighted") if traffic else None,
-                         "kernel": "gemv_iq4xs_q8_kernel", "per_launch": per},
+                         "kernel": "gemv_iq4xs_q8_rows_kernel (B=1) / gemv_iq4xs_q8_mma_kernel (B=2..8)",
+                         "per_launch": per},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "custom_gemv_iq4xs_dispatch_batched from a C++ host loop, pinned host x/y"},
