@@ -102,6 +102,17 @@ size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t N, int64_t B);
 int iq4xs_gemv_f32_ex(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B,
                       void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream);
 
+/* iq4xs_gemv_f32 for callers that cannot allocate device memory where they call it (a ggml hook
+ * inside a graph with a fixed memory plan, a runtime that forbids cudaMalloc after start-up because
+ * it synchronises the device): no workspace argument, nothing allocated.  Its scratch (Q8_1
+ * activations, tile tickets, partial sums) is one static 4 MiB device array per GPU, kept until the
+ * process exits; shapes needing more are rejected with IQ4XS_ERR_WORKSPACE_TOO_SMALL.  All calls
+ * share that array, so calls that overlap on the GPU race: serialise them on one stream.  The first
+ * call on a device looks up the array's address; make it before any stream capture.
+ * No counterpart in the reference (its launchers hipMalloc a scratch buffer on every call). */
+int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B,
+                           cudaStream_t stream);
+
 /* ------------------------------------------------------------------------------------------ */
 /* Raw int32 sub-block dot products sum_j kvalues[q_j]*q8_j (before the (ls-32) factor) through
  * the production GEMV kernel's own inner loop: S [B][N][K/32].  Debug / parity entry point for

@@ -37,6 +37,7 @@ SIGNATURES = {
     "iq4xs_gemv_f32": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "iq4xs_gemv_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "iq4xs_gemv_f32_ex": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
+    "iq4xs_gemv_f32_noalloc": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_debug_subblock_dots": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_gemv_q8_generic": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_fill_normal": (_i, [_vp, _i64, _u64, _f, _f, _vp]),

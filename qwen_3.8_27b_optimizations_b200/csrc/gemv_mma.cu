@@ -318,6 +318,16 @@ size_t gemv_mma_partial_bytes(int64_t K, int64_t N, int B) {
     return (size_t)(K / 512) * B * N * sizeof(float);
 }
 
+// Partial-sum bytes the launch below actually uses for (K, N, B) on a device with `sms` SMs.
+size_t gemv_mma_partial_bytes_for(int64_t K, int64_t N, int B, int sms) {
+    if (K % 512 != 0) return 0;
+    const int pairs = (int)(K / 512);
+    const int64_t T = (N + 15) / 16;
+    const int pk = choose_pk(pairs, T, sms);
+    const int parts = (pairs + pk - 1) / pk;
+    return parts > 1 ? (size_t)parts * B * N * sizeof(float) : 0;
+}
+
 template <int B, bool kDebug>
 static cudaError_t launch_mma_b(const CUtensorMap& map, GemvMmaArgs a, int smem, cudaStream_t stream, bool pdl, int grid) {
     auto kern = gemv_iq4xs_q8_mma_kernel<B, kDebug>;
