@@ -362,7 +362,15 @@ def main():
                 tot_ms += d
     achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
+    # DRAM traffic per launch: the dominant kernel's ncu ratio (dram read+write / algorithmic bytes,
+    # captured on a 69632 x 5120 case) scaled to the mean algorithmic bytes of the sweep's launches.
     traffic = ncu_traffic()
+    traffic_per_launch, traffic_src = None, None
+    if traffic:
+        k = traffic["kernels"]["gemv_iq4xs_q8_mma_kernel"]
+        traffic_per_launch = round(k["traffic_ratio"] * tot_bytes / len(per))
+        traffic_src = (f"ncu dram__bytes_read+write of gemv_iq4xs_q8_mma_kernel on {k['N']}x{k['K']} B={k['B']} "
+                       f"(ratio {k['traffic_ratio']} of algorithmic), scaled to the mean launch of the sweep")
 
     # ---- e2e through the ggml hook from the C++ host loop, pinned host buffers
     e2e_steps = args.e2e_steps or args.steps
@@ -428,7 +436,9 @@ def main():
                        "timing": "CUDA graph replay of the step, CUDA events on the launch stream, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": traffic.get("bytes_per_launch_weighted") if traffic else None,
+                         "traffic": traffic_per_launch,
+                         "algorithmic_bytes_per_launch": round(tot_bytes / len(per)),
+                         "traffic_source": traffic_src,
                          "kernel": "gemv_iq4xs_q8_rows_kernel (B=1) / gemv_iq4xs_q8_mma_kernel (B=2..8)",
                          "per_launch": per},
             "cpu_baseline": cpu,
