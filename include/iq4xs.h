@@ -114,6 +114,21 @@ int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, int64_t K, i
                            cudaStream_t stream);
 
 /* ------------------------------------------------------------------------------------------ */
+/* Prefill GEMM (tensor cores): Y[M][N] = X[M][K] (fp32, quantised per 32-block with Q8_1
+ * semantics inside the call) times W^T (IQ4_XS [N][K/256]), ggml layouts.  Same per-sub-block
+ * arithmetic as the stock GEMM (real_stock_dp4a_comparator.hip:375-443).  K % 512 == 0 (whole
+ * super-block pairs, the tensor-map granule); M, N >= 1.  The workspace holds the quantised
+ * activations (iq4xs_gemm_workspace_bytes(K, M), 256-byte aligned, no zeroing needed).
+ * Replaces gemm_iq4xs_stock_dp4a_gpu / gemm_iq4xs_wmma_stream_gpu (which allocate per call). */
+size_t iq4xs_gemm_workspace_bytes(int64_t K, int64_t M);
+int iq4xs_gemm(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
+               void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* The GEMM's activation quantiser alone, into `workspace`: fp16 q [M][K] (exact integers, within
+ * each 32-block element 4w+i+16j at position 8w+2i+j) followed, at the next 256-byte boundary, by
+ * fp32 d [K/32][round_up(M,4)] (the value of the truncated fp16 d of each Q8_1 block).  For tests. */
+int iq4xs_debug_gemm_quantize(const float* X, void* workspace, int64_t K, int64_t M, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------------------------ */
 /* Raw int32 sub-block dot products sum_j kvalues[q_j]*q8_j (before the (ls-32) factor) through
  * the production GEMV kernel's own inner loop: S [B][N][K/32].  Debug / parity entry point for
  * the bit-exact contract of vec_dot_iq4_xs_q8_1 (real_stock_dp4a_comparator.hip:145-160). */
@@ -152,12 +167,20 @@ cudaError_t quantize_row_q8_1_gpu(const float* x, void* y, int64_t K, cudaStream
 /* real_stock_dp4a_comparator.hip:308-315: playground layout X [K][M] (X[k*M+m]) -> Y [M][K/32]. */
 cudaError_t quantize_row_q8_1_batched_gpu(const float* X, void* Y, int64_t K, int64_t M, cudaStream_t stream);
 
+/* real_stock_dp4a_comparator.hip:505-548 and impl_gemm_wmma_stream.hip:321-350: playground layouts
+ * X [K][M] (X[k*M+m]) and Y [N][M] (Y[n*M+m]); both run the tensor-core GEMM (K % 512 == 0). */
+cudaError_t gemm_iq4xs_stock_dp4a_gpu(const void* W, const float* X, float* Y, int64_t K, int64_t N,
+                                      int64_t M, cudaStream_t stream);
+cudaError_t gemm_iq4xs_wmma_stream_gpu(const void* W, const float* X, float* Y, int64_t K, int64_t N,
+                                       int64_t M, cudaStream_t stream);
+
 /* ggml MUL_MAT hook (patches/0001-gfx1100-mul-mat-custom.patch).  ggml layouts: W = src0 data
  * (ne00 = K, ne01 = N), x/X = src1 fp32 [M][K], y/Y = dst fp32 [M][N].
  * can_handle: patch:274-277 (GEMV) and :148-151 (GEMM); dispatch: :278-280 and :152-154.
  * GEMV handles M = 1..8 (the patch: M == 1 and three fixed shapes); the batched dispatch is the
  * M > 1 form of the same call.  Any non-success status lets the caller fall back to stock.
- * The GEMV dispatches treat W as static model weights (IQ4XS_FLAG_OVERLAP_PRECEDING). */
+ * The GEMV dispatches treat W as static model weights (IQ4XS_FLAG_OVERLAP_PRECEDING).
+ * GEMM can_handle: IQ4_XS, M >= 16 (the patch's gate), K % 512 == 0, N >= 1. */
 bool custom_gemv_iq4xs_can_handle(int64_t K, int64_t N, int64_t M, int type);
 cudaError_t custom_gemv_iq4xs_dispatch(const void* W, const float* x, float* y, int64_t K, int64_t N,
                                        cudaStream_t stream);

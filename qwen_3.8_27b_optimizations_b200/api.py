@@ -38,6 +38,9 @@ SIGNATURES = {
     "iq4xs_gemv_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "iq4xs_gemv_f32_ex": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
     "iq4xs_gemv_f32_noalloc": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "iq4xs_gemm_workspace_bytes": (_sz, [_i64, _i64]),
+    "iq4xs_gemm": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "iq4xs_debug_gemm_quantize": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "iq4xs_debug_subblock_dots": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_gemv_q8_generic": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_fill_normal": (_i, [_vp, _i64, _u64, _f, _f, _vp]),
@@ -47,6 +50,8 @@ SIGNATURES = {
     "gemv_iq4xs_stock_dp4a_gpu": (_i, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "quantize_row_q8_1_gpu": (_i, [_vp, _vp, _i64, _vp]),
     "quantize_row_q8_1_batched_gpu": (_i, [_vp, _vp, _i64, _i64, _vp]),
+    "gemm_iq4xs_stock_dp4a_gpu": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "gemm_iq4xs_wmma_stream_gpu": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "custom_gemv_iq4xs_can_handle": (C.c_bool, [_i64, _i64, _i64, _i]),
     "custom_gemv_iq4xs_dispatch": (_i, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "custom_gemv_iq4xs_dispatch_batched": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
@@ -129,10 +134,12 @@ def q8_1_quantize(X, stream=None):
 _ws_cache = {}
 
 
-def _workspace(nbytes: int, device):
-    """A zero-initialised workspace (the ticket region must start at zero) cached per device."""
+def _workspace(nbytes: int, device, kind: str = "gemv"):
+    """A zero-initialised workspace cached per (device, kind).  GEMV workspaces hold tickets that
+    must stay zero between calls; the GEMM writes its quantised activations over the whole of its
+    own, so the two never share one."""
     torch = _torch()
-    key = (str(device),)
+    key = (str(device), kind)
     ws = _ws_cache.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
@@ -179,6 +186,38 @@ def gemv(W, X, N: int, workspace=None, out=None, stream=None, flags: int = 0):
     _check("iq4xs_gemv_f32", lib().iq4xs_gemv_f32_ex(_ptr(W), _ptr(X), _ptr(Y), K, N, B, _ptr(ws),
                                                      ws.numel() * ws.element_size(), flags, _stream(stream)))
     return Y
+
+
+def gemm_workspace_bytes(K: int, M: int) -> int:
+    return int(lib().iq4xs_gemm_workspace_bytes(K, M))
+
+
+def gemm(W, X, N: int, workspace=None, out=None, stream=None):
+    """Y [M][N] = X [M][K] . W^T on the tensor cores (X fp32, quantised per 32-block inside)."""
+    torch = _torch()
+    X = X.contiguous()
+    M, K = X.shape
+    need = gemm_workspace_bytes(K, M)
+    ws = workspace if workspace is not None else _workspace(need, X.device, "gemm")
+    Y = out if out is not None else torch.empty((M, N), dtype=torch.float32, device=X.device)
+    _check("iq4xs_gemm", lib().iq4xs_gemm(_ptr(W), _ptr(X), _ptr(Y), K, N, M, _ptr(ws),
+                                          ws.numel() * ws.element_size(), _stream(stream)))
+    return Y
+
+
+def debug_gemm_quantize(X, stream=None):
+    """The GEMM's activation quantiser: (fp16 q [M][K] in the lookup order, fp32 d [K/32][M])."""
+    torch = _torch()
+    X = X.contiguous()
+    M, K = X.shape
+    ws = torch.zeros(gemm_workspace_bytes(K, M), dtype=torch.uint8, device=X.device)
+    _check("iq4xs_debug_gemm_quantize", lib().iq4xs_debug_gemm_quantize(_ptr(X), _ptr(ws), K, M, _stream(stream)))
+    qbytes = M * K * 2
+    off = (qbytes + 255) // 256 * 256
+    ld = (M + 3) // 4 * 4
+    xq = ws[:qbytes].view(torch.float16).view(M, K)
+    xs = ws[off:off + (K // 32) * ld * 4].view(torch.float32).view(K // 32, ld)[:, :M]
+    return xq, xs
 
 
 def debug_subblock_dots(W, q8, K: int, N: int, B: int, stream=None):
@@ -237,6 +276,16 @@ def quantize_row_q8_1_gpu(x, y, K: int, stream=None) -> None:
 
 def quantize_row_q8_1_batched_gpu(X_km, Y, K: int, M: int, stream=None) -> None:
     _check("quantize_row_q8_1_batched_gpu", lib().quantize_row_q8_1_batched_gpu(_ptr(X_km), _ptr(Y), K, M, _stream(stream)), True)
+
+
+def gemm_iq4xs_stock_dp4a_gpu(W, X_km, Y_nm, K: int, N: int, M: int, stream=None) -> None:
+    _check("gemm_iq4xs_stock_dp4a_gpu",
+           lib().gemm_iq4xs_stock_dp4a_gpu(_ptr(W), _ptr(X_km), _ptr(Y_nm), K, N, M, _stream(stream)), True)
+
+
+def gemm_iq4xs_wmma_stream_gpu(W, X_km, Y_nm, K: int, N: int, M: int, stream=None) -> None:
+    _check("gemm_iq4xs_wmma_stream_gpu",
+           lib().gemm_iq4xs_wmma_stream_gpu(_ptr(W), _ptr(X_km), _ptr(Y_nm), K, N, M, _stream(stream)), True)
 
 
 def custom_gemv_iq4xs_can_handle(K: int, N: int, M: int, type_: int = GGML_TYPE_IQ4_XS) -> bool:

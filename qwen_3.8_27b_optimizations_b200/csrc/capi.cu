@@ -7,6 +7,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 #include "../../include/iq4xs.h"
@@ -75,14 +76,17 @@ struct Ws {
     void* ptr = nullptr;
     size_t bytes = 0;
 };
-std::map<std::pair<int, cudaStream_t>, Ws> g_ws;
+// One buffer per (device, stream, kind): a GEMV workspace keeps zero tickets between calls, the GEMM
+// overwrites all of its own with quantised activations, so the two kinds never share a buffer.
+enum WsKind { kWsGemv = 0, kWsGemm = 1 };
+std::map<std::tuple<int, cudaStream_t, int>, Ws> g_ws;
 
-cudaError_t internal_workspace(cudaStream_t stream, size_t bytes, void** out) {
+cudaError_t internal_workspace(cudaStream_t stream, size_t bytes, void** out, WsKind kind = kWsGemv) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(g_mu);
-    Ws& w = g_ws[{dev, stream}];
+    Ws& w = g_ws[std::make_tuple(dev, stream, (int)kind)];
     if (w.bytes >= bytes) {
         *out = w.ptr;
         return cudaSuccess;
@@ -269,6 +273,59 @@ int iq4xs_dequantize(const void* W, float* out, int64_t K, int64_t N, cudaStream
     return status_from(launch_dequantize(static_cast<const uint8_t*>(W), out, K, N, stream));
 }
 
+// ------------------------------------------------------------------------------ GEMM
+static int check_gemm(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if (!X || !Y) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (M <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (K % 512 != 0 || M > ((int64_t)1 << 30) || N > ((int64_t)1 << 30) || K > ((int64_t)1 << 24))
+        return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(W, 16) || !aligned(X, 4) || !aligned(Y, 4)) return IQ4XS_ERR_MISALIGNED;
+    return IQ4XS_OK;
+}
+
+static int gemm_strided(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M, int64_t xsm,
+                        int64_t xsk, int64_t ysm, int64_t ysn, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream) {
+    int s = check_gemm(W, X, Y, K, N, M);
+    if (s) return s;
+    if (!workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < gemm_workspace_bytes(K, M)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
+    const uint32_t lut[4] = {kNegLo0, kNegLo1, kPosHi0, kPosHi1};
+    return status_from(launch_gemm(static_cast<const uint8_t*>(W), X, Y, K, N, M, xsm, xsk, ysm, ysn, workspace, stream,
+                                   device_error_word(), lut));
+}
+
+static cudaError_t gemm_internal_ws(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
+                                    int64_t xsm, int64_t xsk, int64_t ysm, int64_t ysn, cudaStream_t stream) {
+    int s = check_gemm(W, X, Y, K, N, M);
+    if (s) return to_cuda_error(s);
+    const size_t need = gemm_workspace_bytes(K, M);
+    void* ws = nullptr;
+    cudaError_t e = internal_workspace(stream, need, &ws, kWsGemm);
+    if (e != cudaSuccess) return e;
+    return to_cuda_error(gemm_strided(W, X, Y, K, N, M, xsm, xsk, ysm, ysn, ws, need, stream));
+}
+
+size_t iq4xs_gemm_workspace_bytes(int64_t K, int64_t M) {
+    if (K <= 0 || M <= 0 || K % kQK8 != 0) return 0;
+    return gemm_workspace_bytes(K, M);
+}
+
+int iq4xs_gemm(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M, void* workspace,
+               size_t workspace_bytes, cudaStream_t stream) {
+    return gemm_strided(W, X, Y, K, N, M, K, 1, N, 1, workspace, workspace_bytes, stream);
+}
+
+int iq4xs_debug_gemm_quantize(const float* X, void* workspace, int64_t K, int64_t M, cudaStream_t stream) {
+    if (!X || !workspace || K <= 0 || M <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (K % kQK8 != 0) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(X, 4) || !aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
+    return status_from(launch_gemm_quantize(X, workspace, K, M, K, 1, stream));
+}
+
 // ------------------------------------------------------------------------------ reference-named
 static cudaError_t gemv_f32_internal_ws(const void* W, const float* x, float* y, int64_t K, int64_t N, int64_t B,
                                         cudaStream_t stream) {
@@ -318,14 +375,25 @@ cudaError_t custom_gemv_iq4xs_dispatch_batched(const void* W, const float* x, fl
 }
 
 bool custom_gemm_iq4xs_can_handle(int64_t K, int64_t N, int64_t M, int type) {
-    (void)K; (void)N; (void)M; (void)type;
-    return false;  // prefill GEMM not built yet: the caller keeps its stock path
+    if (type != IQ4XS_GGML_TYPE_IQ4_XS) return false;
+    if (M < 16) return false;  // patch:149: smaller batches stay on the GEMV path
+    if (K <= 0 || N <= 0 || K % 512 != 0) return false;
+    return true;
 }
 
 cudaError_t custom_gemm_iq4xs_dispatch(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
                                        cudaStream_t stream) {
-    (void)W; (void)X; (void)Y; (void)K; (void)N; (void)M; (void)stream;
-    return cudaErrorNotSupported;
+    return gemm_internal_ws(W, X, Y, K, N, M, K, 1, N, 1, stream);
+}
+
+cudaError_t gemm_iq4xs_stock_dp4a_gpu(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
+                                      cudaStream_t stream) {
+    return gemm_internal_ws(W, X, Y, K, N, M, 1, M, 1, M, stream);
+}
+
+cudaError_t gemm_iq4xs_wmma_stream_gpu(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
+                                       cudaStream_t stream) {
+    return gemm_internal_ws(W, X, Y, K, N, M, 1, M, 1, M, stream);
 }
 
 }  // extern "C"

@@ -1,0 +1,593 @@
+// gemm.cu -- IQ4_XS x Q8_1 prefill GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// Arithmetic contract: the reference's stock GEMM (real_stock_dp4a_comparator.hip:375-443): every
+// 32-weight sub-block of a weight row meets every token's Q8_1 block as an exact integer dot
+// sumi = sum_j kv[q_j] * x_j, and the output is sum over sub-blocks of (d_w*(ls-32)) * d_x * sumi in
+// fp32.  Here:
+//
+//  * Operands are fp16 tensors holding exact small integers: the codebook values kv (|kv| <= 127)
+//    and the Q8_1 quants (|q| <= 127).  Products are exact, and the fp32 tensor-core sum of one
+//    sub-block (|sumi| <= 32*127*127 < 2^24) is exact too, so each TMEM accumulator holds the exact
+//    integer sumi of one (row, token, sub-block).  int8 operands (kind::i8) would halve the MMA time
+//    but leave an s32 -> f32 conversion on every drained element, and the drain is this kernel's
+//    bound (below); fp16 integers come out of TMEM as fp32 directly.
+//  * Per 32-wide sub-block the MMA (M = 128 weight rows, N = 128 tokens, two K = 16 steps) writes a
+//    fresh TMEM accumulator; drain warps load it (tcgen05.ld) and fold the scale in:
+//    acc[row][token] += (sumi * d_x[token]) * (d_w*(ls-32))[row] in fp32 registers.  Four TMEM
+//    accumulators (4 x 128 columns) let the MMA run up to four sub-blocks ahead of the drain.
+//  * Weights: the IQ4_XS rows as stored, viewed as uint64 [N][K/512 pairs][34] and loaded by TMA
+//    128 rows x one super-block pair (34,816 bytes) at a time.  Converter warps (one thread per row)
+//    expand each 64-wide K chunk to fp16 in the canonical K-major 128-byte-swizzled layout that
+//    tcgen05 descriptors read: split codebook lookup by prmt (tables -kv[0..7] and kv[8..15]), one
+//    IADD3 to the biased byte kv+128, prmt into the fp16 pattern 0x64XX (= 1024 + byte), HADD2 with
+//    -1152.  Within a sub-block the K order is the lookup's natural order: position 8w + 2i + j holds
+//    element 4w + i + 16j (w = qs word, i = byte in word, j = nibble); the activation quantizer
+//    writes the same order, and a permutation of K inside a sub-block leaves the dot unchanged.
+//  * Activations: quantised once per call to fp16 q [M][K] (that order) plus fp32 d_x [K/32][Mp]
+//    (the fp32 value of the truncated fp16 d of the Q8_1 block: the reference's low2float(ds));
+//    128 tokens x 64 K per stage by TMA with 128-byte swizzle, the scales by a second TMA.
+//  * Persistent kernel, one CTA per SM; tiles (128 rows x 128 tokens) in row-tile-major order so the
+//    CTAs running at once share weight rows in L2.  Warp roles: 0 weight TMA, 1 TMEM allocation and
+//    MMA issue (one thread), 2 activation TMA, 3-6 converters, 7-14 drain + epilogue.
+//  * Every mbarrier wait is bounded (sleeping try_wait); a wait that gives up records a device
+//    error, raises the CTA's abort flag, and every role leaves its loop; in-flight TMA copies and
+//    MMAs are waited for (bounded) and TMEM is freed before the CTA exits.  No cluster multicast.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "iq4xs_device.cuh"
+#include "iq4xs_kernels.h"
+
+namespace iq4xs {
+
+namespace {
+constexpr int kBM = 128;         // weight rows per tile = MMA M = TMEM lanes
+constexpr int kBN = 128;         // tokens per tile = MMA N = TMEM columns per accumulator
+constexpr int kBK = 64;          // K per stage (two sub-blocks, one 128-byte swizzle atom of fp16)
+constexpr int kStages = 4;       // A / B / scale ring depth
+constexpr int kRawStages = 2;    // raw weight ring depth (one super-block pair each)
+constexpr int kAccBufs = 4;      // TMEM accumulators (4 x 128 = 512 columns)
+constexpr int kConvWarps = 4;
+constexpr int kDrainWarps = 8;
+constexpr int kThreads = 32 * (3 + kConvWarps + kDrainWarps);  // 480
+
+constexpr uint32_t kRawBytes = kBM * 272;        // 34,816
+constexpr uint32_t kABytes = kBM * kBK * 2;      // 16,384
+constexpr uint32_t kBBytes = kBN * kBK * 2;      // 16,384
+constexpr uint32_t kSxBytes = 2 * kBN * 4;       // 1,024
+constexpr uint32_t kSwBytes = 2 * kBM * 4;       // 1,024
+
+constexpr uint32_t kOffA = 0;
+constexpr uint32_t kOffB = kOffA + kStages * kABytes;
+constexpr uint32_t kOffRaw = kOffB + kStages * kBBytes;
+constexpr uint32_t kOffSx = kOffRaw + kRawStages * kRawBytes;
+constexpr uint32_t kOffSw = kOffSx + kStages * kSxBytes;
+constexpr uint32_t kOffBar = kOffSw + kStages * kSwBytes;
+constexpr int kNumBars = 2 * kRawStages + 4 * kStages + 2 * kAccBufs + 1;
+constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;  // TMEM address, abort flag
+constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + slack to align the base to 1024
+
+// Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B fp16 (bits 7-9, 10-12 = 0),
+// both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: start address >> 4 (bits 0-13),
+// leading byte offset (unused for swizzled K-major, encoded 1), stride byte offset 1024 >> 4 (8-row
+// core groups are 1024 bytes apart, bits 32-45), fixed version bits 46-47 = 1, swizzle mode 2 at
+// bits 61-63.  Advancing K by 16 fp16 inside the swizzle atom adds 32 bytes to the start address.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_nohint(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                                   uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives once on `bar` when every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Bounded sleeping wait on one phase parity; gives up (error word + abort flag) after ~20 s or
+// when another role raised the abort flag.
+__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag, uint32_t* err,
+                                      uint32_t code) {
+    for (uint32_t i = 0; i < 20000u; ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+        if (*abort_flag) return false;
+    }
+    record_error(err, code);
+    *abort_flag = 1u;
+    return false;
+}
+
+// Bounded wait used while draining after an abort (no abort check: the copy must land first).
+__device__ __forceinline__ void gdrain(uint64_t* bar, uint32_t parity, uint32_t* err) {
+    for (uint32_t i = 0; i < 20000u; ++i)
+        if (mbar_try_wait_sleep(bar, parity, 1000000u)) return;
+    record_error(err, kDevErrDrainWait);
+}
+
+// fp16x2 add on raw bits.
+__device__ __forceinline__ uint32_t hadd2_bits(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// Four fp16 pairs (8 weights) of one qs word in the lookup order, exact codebook values:
+// [e(4w), e(4w+16)], [e(4w+1), e(4w+17)], [e(4w+2), e(4w+18)], [e(4w+3), e(4w+19)].
+__device__ __forceinline__ uint4 expand_word(uint32_t x, const uint32_t (&lut)[4]) {
+    const uint32_t xf = x ^ 0x88888888u;
+    const uint32_t lo_l = prmt(lut[0], lut[1], x), lo_h = prmt(lut[2], lut[3], xf);
+    const uint32_t hi_l = prmt(lut[0], lut[1], x >> 16), hi_h = prmt(lut[2], lut[3], xf >> 16);
+    // Biased bytes kv + 128: 128 - (-kv) for codes < 8, 128 + kv for codes >= 8 (no carries).
+    const uint32_t blo = 0x80808080u - lo_l + lo_h;
+    const uint32_t bhi = 0x80808080u - hi_l + hi_h;
+    // prmt with 0x64 high bytes makes fp16 1024 + byte; adding -1152 (0xE480) leaves kv exactly.
+    constexpr uint32_t kBias = 0xE480E480u;
+    uint4 r;
+    r.x = hadd2_bits(prmt(blo, 0x64646464u, 0x4140u), kBias);
+    r.y = hadd2_bits(prmt(blo, 0x64646464u, 0x4342u), kBias);
+    r.z = hadd2_bits(prmt(bhi, 0x64646464u, 0x4140u), kBias);
+    r.w = hadd2_bits(prmt(bhi, 0x64646464u, 0x4342u), kBias);
+    return r;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_iq4xs_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                         const __grid_constant__ CUtensorMap tmap_s, const GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* raw_full = bars;
+    uint64_t* raw_empty = raw_full + kRawStages;
+    uint64_t* a_full = raw_empty + kRawStages;
+    uint64_t* b_full = a_full + kStages;
+    uint64_t* ab_empty = b_full + kStages;
+    uint64_t* s_empty = ab_empty + kStages;
+    uint64_t* t_full = s_empty + kStages;
+    uint64_t* t_empty = t_full + kAccBufs;
+    uint64_t* mma_done = t_empty + kAccBufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_m = a.tiles_m;
+    const int64_t T = (int64_t)a.tiles_n * tiles_m;
+    const int pairs = a.K / 512;
+    const int S = a.K / kBK;  // stages per tile
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRawStages; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kConvWarps);
+        }
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&a_full[i], kConvWarps);
+            mbar_init(&b_full[i], 1);
+            mbar_init(&ab_empty[i], 1);
+            mbar_init(&s_empty[i], kDrainWarps);
+        }
+        for (int i = 0; i < kAccBufs; ++i) {
+            mbar_init(&t_full[i], 1);
+            mbar_init(&t_empty[i], kDrainWarps);
+        }
+        mbar_init(mma_done, 1);
+        *abort_flag = 0u;
+        fence_mbar_init();
+        prefetch_tmap(&tmap_w);
+        prefetch_tmap(&tmap_x);
+        prefetch_tmap(&tmap_s);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kAccBufs * kBN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    // X (and so the quantised activations) may come from the preceding kernel.
+    grid_dependency_wait();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ weight TMA
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < T && ok; t += gridDim.x) {
+                const int row0 = (int)(t / tiles_m) * kBM;
+                for (int p = 0; p < pairs && ok; ++p, ++it) {
+                    const int s = (int)(it % kRawStages);
+                    const uint32_t u = it / kRawStages;
+                    if (!(ok = gwait(&raw_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
+                    mbar_arrive_expect_tx(&raw_full[s], kRawBytes);
+                    tma_load_3d_nohint(smem + kOffRaw + s * kRawBytes, &tmap_w, 0, p, row0, &raw_full[s]);
+                }
+            }
+            // Let the last copies land before the CTA can exit.
+            for (uint32_t j = it > (uint32_t)kRawStages ? it - kRawStages : 0; j < it; ++j)
+                gdrain(&raw_full[j % kRawStages], (j / kRawStages) & 1u, a.err);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------------ activation TMA
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < T && ok; t += gridDim.x) {
+                const int m0 = (int)(t % tiles_m) * kBN;
+                for (int st = 0; st < S; ++st, ++it) {
+                    const int s = (int)(it % kStages);
+                    const uint32_t u = it / kStages;
+                    if (!(ok = gwait(&ab_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
+                    if (!(ok = gwait(&s_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
+                    mbar_arrive_expect_tx(&b_full[s], kBBytes + kSxBytes);
+                    tma_load_2d(smem + kOffB + s * kBBytes, &tmap_x, st * kBK, m0, &b_full[s]);
+                    tma_load_2d(smem + kOffSx + s * kSxBytes, &tmap_s, m0, 2 * st, &b_full[s]);
+                }
+            }
+            for (uint32_t j = it > (uint32_t)kStages ? it - kStages : 0; j < it; ++j)
+                gdrain(&b_full[j % kStages], (j / kStages) & 1u, a.err);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issue
+        if (lane == 0) {
+            uint32_t it = 0, q = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < T && ok; t += gridDim.x) {
+                for (int st = 0; st < S && ok; ++st, ++it) {
+                    const int s = (int)(it % kStages);
+                    const uint32_t u = it / kStages;
+                    if (!(ok = gwait(&a_full[s], u & 1u, abort_flag, a.err, kDevErrMmaWait))) break;
+                    if (!(ok = gwait(&b_full[s], u & 1u, abort_flag, a.err, kDevErrMmaWait))) break;
+                    tc_fence_after();
+                    const uint64_t ad = smem_desc_sw128(smem_addr(smem + kOffA + s * kABytes));
+                    const uint64_t bd = smem_desc_sw128(smem_addr(smem + kOffB + s * kBBytes));
+                    for (int h = 0; h < 2; ++h, ++q) {
+                        const int j = (int)(q % kAccBufs);
+                        const uint32_t uq = q / kAccBufs;
+                        if (!(ok = gwait(&t_empty[j], (uq & 1u) ^ 1u, abort_flag, a.err, kDevErrMmaWait))) break;
+                        tc_fence_after();
+                        const uint32_t d = tmem_base + (uint32_t)(j * kBN);
+                        // K offsets 32h and 32h+16 fp16 = 64h and 64h+32 bytes = 4h and 4h+2 in 16-byte units.
+                        tc_mma_f16(d, ad + (uint64_t)(4 * h), bd + (uint64_t)(4 * h), 0u);
+                        tc_mma_f16(d, ad + (uint64_t)(4 * h + 2), bd + (uint64_t)(4 * h + 2), 1u);
+                        tc_commit(&t_full[j]);
+                    }
+                    if (ok) tc_commit(&ab_empty[s]);
+                }
+            }
+            // All issued MMAs complete before TMEM is released.
+            tc_commit(mma_done);
+            gdrain(mma_done, 0u, a.err);
+        }
+        __syncwarp();
+    } else if (warp < 3 + kConvWarps) {
+        // ------------------------------------------------------------------ converters: thread = row
+        const int r = threadIdx.x - 96;
+        const uint32_t lut[4] = {a.lut[0], a.lut[1], a.lut[2], a.lut[3]};
+        uint32_t rit = 0, it = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < T && ok; t += gridDim.x) {
+            for (int p = 0; p < pairs && ok; ++p, ++rit) {
+                const int rs = (int)(rit % kRawStages);
+                if (!(ok = gwait(&raw_full[rs], (rit / kRawStages) & 1u, abort_flag, a.err, kDevErrFullWait))) break;
+                const uint32_t rowp = smem_addr(smem + kOffRaw + rs * kRawBytes) + (uint32_t)r * 272u;
+                for (int sp = 0; sp < 8; ++sp, ++it) {
+                    const int s = (int)(it % kStages);
+                    const uint32_t u = it / kStages;
+                    if (!(ok = gwait(&ab_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
+                    if (!(ok = gwait(&s_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
+                    const uint32_t sbp = rowp + (uint32_t)(sp >> 2) * 136u;
+                    const uint2 hdr = lds_u2(sbp);
+                    const float dw = f16_bits_to_f32(hdr.x);
+                    const int ib0 = 2 * (sp & 3);
+                    float* sw = reinterpret_cast<float*>(smem + kOffSw + s * kSwBytes);
+                    sw[r] = dw * (float)(subblock_scale(hdr.x, hdr.y, ib0) - 32);
+                    sw[kBM + r] = dw * (float)(subblock_scale(hdr.x, hdr.y, ib0 + 1) - 32);
+                    const uint32_t qp = sbp + 8u + 32u * (uint32_t)(sp & 3);
+                    uint32_t qw[8];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint2 v = lds_u2(qp + 8u * k);
+                        qw[2 * k] = v.x;
+                        qw[2 * k + 1] = v.y;
+                    }
+                    uint8_t* arow = smem + kOffA + s * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint4 v = expand_word(qw[c], lut);
+                        *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = v;
+                    }
+                    fence_proxy_async_smem();  // generic-proxy writes -> tensor-core (async proxy) reads
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[s]);
+                }
+                __syncwarp();
+                if (ok && lane == 0) mbar_arrive(&raw_empty[rs]);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ drain + epilogue
+        const int dw = warp - (3 + kConvWarps);       // 0..7
+        const int lq = warp & 3;                      // TMEM lane quarter this warp may access
+        const int ch = dw >> 2;                       // token half: columns 64*ch .. 64*ch+63
+        const int r = 32 * lq + lane;                 // tile row = TMEM lane
+        const uint32_t lane_base = tmem_base + ((uint32_t)(32 * lq) << 16) + (uint32_t)(64 * ch);
+        uint32_t it = 0, q = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < T && ok; t += gridDim.x) {
+            const int row0 = (int)(t / tiles_m) * kBM;
+            const int m0 = (int)(t % tiles_m) * kBN;
+            float acc[64];
+#pragma unroll
+            for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
+            for (int st = 0; st < S && ok; ++st, ++it) {
+                const int s = (int)(it % kStages);
+                const uint32_t u = it / kStages;
+                // Scales of this stage: weight side from the converters, token side from TMA.
+                if (!(ok = gwait(&a_full[s], u & 1u, abort_flag, a.err, kDevErrFullWait))) break;
+                if (!(ok = gwait(&b_full[s], u & 1u, abort_flag, a.err, kDevErrFullWait))) break;
+                const float* sw = reinterpret_cast<const float*>(smem + kOffSw + s * kSwBytes);
+                const float* sx = reinterpret_cast<const float*>(smem + kOffSx + s * kSxBytes);
+                for (int h = 0; h < 2; ++h, ++q) {
+                    const int j = (int)(q % kAccBufs);
+                    if (!(ok = gwait(&t_full[j], (q / kAccBufs) & 1u, abort_flag, a.err, kDevErrMmaWait))) break;
+                    tc_fence_after();
+                    const float wsc = sw[h * kBM + r];
+                    const float4* sxv = reinterpret_cast<const float4*>(sx + h * kBN + 64 * ch);
+                    uint32_t v[32];
+                    tmem_ld32(lane_base + (uint32_t)(j * kBN), v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; ++c4) {
+                        const float4 x = sxv[c4];
+                        acc[4 * c4 + 0] = fmaf(__uint_as_float(v[4 * c4 + 0]) * x.x, wsc, acc[4 * c4 + 0]);
+                        acc[4 * c4 + 1] = fmaf(__uint_as_float(v[4 * c4 + 1]) * x.y, wsc, acc[4 * c4 + 1]);
+                        acc[4 * c4 + 2] = fmaf(__uint_as_float(v[4 * c4 + 2]) * x.z, wsc, acc[4 * c4 + 2]);
+                        acc[4 * c4 + 3] = fmaf(__uint_as_float(v[4 * c4 + 3]) * x.w, wsc, acc[4 * c4 + 3]);
+                    }
+                    tmem_ld32(lane_base + (uint32_t)(j * kBN + 32), v);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&t_empty[j]);
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; ++c4) {
+                        const float4 x = sxv[8 + c4];
+                        acc[32 + 4 * c4 + 0] = fmaf(__uint_as_float(v[4 * c4 + 0]) * x.x, wsc, acc[32 + 4 * c4 + 0]);
+                        acc[32 + 4 * c4 + 1] = fmaf(__uint_as_float(v[4 * c4 + 1]) * x.y, wsc, acc[32 + 4 * c4 + 1]);
+                        acc[32 + 4 * c4 + 2] = fmaf(__uint_as_float(v[4 * c4 + 2]) * x.z, wsc, acc[32 + 4 * c4 + 2]);
+                        acc[32 + 4 * c4 + 3] = fmaf(__uint_as_float(v[4 * c4 + 3]) * x.w, wsc, acc[32 + 4 * c4 + 3]);
+                    }
+                }
+                if (!ok) break;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[s]);
+            }
+            if (!ok) break;
+            // Epilogue: Y[m][n] at Y + m*ldy_m + n*ldy_n.
+            const int64_t n = (int64_t)row0 + r;
+            if (n < a.N) {
+                float* yrow = a.y + n * a.ldy_n;
+#pragma unroll
+                for (int c = 0; c < 64; ++c) {
+                    const int64_t m = (int64_t)m0 + 64 * ch + c;
+                    if (m < a.M) yrow[m * a.ldy_m] = acc[c];
+                }
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kAccBufs * kBN)
+                     : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Activation quantizer for the GEMM: Q8_1 semantics bit for bit (amax / sum butterflies,
+// d = amax/127, q = roundf(x/d), q = 0 for an all-zero block), written as fp16 q [M][K] in the
+// lookup order within each 32-block (element e = 4w+i+16j at position 8w+2i+j) and fp32 scales
+// xs[K/32][ldxs] = the value of the truncated fp16 d.  One warp per block.
+__global__ void __launch_bounds__(256) gemm_act_quantize_kernel(const float* __restrict__ X, __half* __restrict__ xq,
+                                                                float* __restrict__ xs, int64_t K, int64_t M,
+                                                                int64_t stride_m, int64_t stride_k, int64_t ldxs) {
+    grid_dependency_wait();
+    const unsigned full = 0xFFFFFFFFu;
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = K / kQK8;
+    const int64_t total = nb * M;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int pos = 8 * ((lane & 15) >> 2) + 2 * (lane & 3) + (lane >> 4);
+    for (int64_t blk = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); blk < total; blk += nwarps) {
+        const int64_t m = blk / nb;
+        const int64_t ib = blk - m * nb;
+        const float x = X[m * stride_m + (ib * kQK8 + lane) * stride_k];
+        float amax = fabsf(x), sum = x;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(full, amax, off));
+            sum += __shfl_xor_sync(full, sum, off);
+        }
+        const float d = amax / 127.0f;
+        int q = 0;
+        if (amax != 0.0f) q = (int)roundf(x / d);
+        xq[m * K + ib * kQK8 + pos] = __int2half_rn(q);
+        if (lane == 0) xs[ib * ldxs + m] = f16_bits_to_f32(f32_to_f16_trunc(d));
+    }
+    grid_launch_dependents();
+}
+
+// ------------------------------------------------------------------------------------------
+// Host side.
+namespace {
+typedef CUresult (*EncodeTiledFn2)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn2 encode_fn2() {
+    static EncodeTiledFn2 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn2>(p);
+    }
+    return fn;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+int64_t ldxs_of(int64_t M) { return (M + 3) & ~(int64_t)3; }
+}  // namespace
+
+size_t gemm_workspace_bytes(int64_t K, int64_t M) {
+    return align256((size_t)M * (size_t)K * 2) + (size_t)(K / kQK8) * (size_t)ldxs_of(M) * 4;
+}
+
+cudaError_t launch_gemm_quantize(const float* X, void* workspace, int64_t K, int64_t M, int64_t stride_m,
+                                 int64_t stride_k, cudaStream_t stream) {
+    __half* xq = static_cast<__half*>(workspace);
+    float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)M * (size_t)K * 2));
+    const int64_t total = (K / kQK8) * M;
+    const int sms = device_sm_count() > 0 ? device_sm_count() : 148;
+    const int64_t grid = std::min<int64_t>((total + 7) / 8, (int64_t)sms * 16);
+    gemm_act_quantize_kernel<<<(unsigned)grid, 256, 0, stream>>>(X, xq, xs, K, M, stride_m, stride_k, ldxs_of(M));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(const uint8_t* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M, int64_t x_stride_m,
+                        int64_t x_stride_k, int64_t y_stride_m, int64_t y_stride_n, void* workspace, cudaStream_t stream,
+                        uint32_t* err, const uint32_t lut[4]) {
+    if (K % 512 != 0 || K <= 0 || N <= 0 || M <= 0 || (reinterpret_cast<uintptr_t>(W) & 15u)) return cudaErrorInvalidValue;
+    if (K > (int64_t)1 << 24 || M > (int64_t)1 << 30 || N > (int64_t)1 << 30) return cudaErrorInvalidValue;
+    EncodeTiledFn2 enc = encode_fn2();
+    if (!enc) return cudaErrorNotSupported;
+    cudaError_t e = launch_gemm_quantize(X, workspace, K, M, x_stride_m, x_stride_k, stream);
+    if (e != cudaSuccess) return e;
+    __half* xq = static_cast<__half*>(workspace);
+    float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)M * (size_t)K * 2));
+
+    CUtensorMap mw, mx, ms;
+    const int pairs = (int)(K / 512);
+    {
+        const cuuint64_t dims[3] = {34, (cuuint64_t)pairs, (cuuint64_t)N};
+        const cuuint64_t strides[2] = {272, (cuuint64_t)pairs * 272};
+        const cuuint32_t box[3] = {34, 1, (cuuint32_t)kBM};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(W), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+        const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+        const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBN};
+        const cuuint32_t estr[2] = {1, 1};
+        if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xq, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {
+        const int64_t ld = ldxs_of(M);
+        const cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)(K / kQK8)};
+        const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+        const cuuint32_t box[2] = {(cuuint32_t)kBN, 2};
+        const cuuint32_t estr[2] = {1, 1};
+        if (enc(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, xs, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+
+    GemmArgs a = {};
+    a.y = Y;
+    a.err = err;
+    a.N = N;
+    a.M = M;
+    a.K = (int)K;
+    a.ldy_m = y_stride_m;
+    a.ldy_n = y_stride_n;
+    a.tiles_n = (int)((N + kBM - 1) / kBM);
+    a.tiles_m = (int)((M + kBN - 1) / kBN);
+    for (int i = 0; i < 4; ++i) a.lut[i] = lut[i];
+    const int64_t T = (int64_t)a.tiles_n * a.tiles_m;
+    const int sms = device_sm_count() > 0 ? device_sm_count() : 148;
+    const int grid = (int)std::min<int64_t>(T, sms);
+
+    e = cudaFuncSetAttribute(gemm_iq4xs_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_iq4xs_tc_kernel, mw, mx, ms, a);
+}
+
+}  // namespace iq4xs

@@ -53,6 +53,25 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
                             bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4]);
 int device_sm_count();
 
+// Tensor-core prefill GEMM (gemm.cu).  Y[m][n] at y + m*ldy_m + n*ldy_n.
+struct GemmArgs {
+    float* y;
+    uint32_t* err;
+    int64_t N, M;
+    int K;
+    int64_t ldy_m, ldy_n;
+    int tiles_n, tiles_m;  // 128-row weight tiles, 128-token tiles
+    uint32_t lut[4];
+};
+// Workspace: fp16 activation quants [M][K] (256-aligned) + fp32 scales [K/32][round_up(M,4)].
+size_t gemm_workspace_bytes(int64_t K, int64_t M);
+cudaError_t launch_gemm_quantize(const float* X, void* workspace, int64_t K, int64_t M, int64_t stride_m,
+                                 int64_t stride_k, cudaStream_t stream);
+// Element (m, k) of X at X[m*x_stride_m + k*x_stride_k].  K % 512 == 0.
+cudaError_t launch_gemm(const uint8_t* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M, int64_t x_stride_m,
+                        int64_t x_stride_k, int64_t y_stride_m, int64_t y_stride_n, void* workspace, cudaStream_t stream,
+                        uint32_t* err, const uint32_t lut[4]);
+
 // Q8_1 quantizer.  Element (m, k) of X is at X[m*stride_m + k*stride_k]; output blocks [M][K/32].
 // pdl: launch with programmatic stream serialization (the kernel waits on griddepcontrol before
 // reading X, so it may overlap the tail of the preceding kernel).

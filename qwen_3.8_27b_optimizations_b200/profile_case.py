@@ -1,6 +1,8 @@
-"""Run one GEMV shape a few times on cuda:0 -- the small, self-ending case for ncu captures.
+"""Run one GEMV (or, with --M, GEMM) shape a few times on cuda:0 -- the small, self-ending case for
+ncu captures.
 
     python qwen_3.8_27b_optimizations_b200/profile_case.py --N 69632 --K 5120 --B 1 --launches 3
+    python qwen_3.8_27b_optimizations_b200/profile_case.py --N 17408 --K 5120 --M 2048
 
 Weights are synthetic IQ4_XS (N(0, 0.02) quantised on the device), activations N(0, 1), quantised
 to Q8_1 once up front, so the launches of interest are `--launches` GEMV kernels after `--warmup`
@@ -30,12 +32,15 @@ def main() -> int:
     ap.add_argument("--N", type=int, default=69632)
     ap.add_argument("--K", type=int, default=5120)
     ap.add_argument("--B", type=int, default=1)
+    ap.add_argument("--M", type=int, default=0, help="tokens: run the prefill GEMM instead of the GEMV")
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
     args = ap.parse_args()
     P = _load_pkg()
     N, K, B = args.N, args.K, args.B
     W = P.random_weights(N, K, seed=7)
+    if args.M:
+        return gemm_case(P, W, N, K, args.M, args.launches, args.warmup)
     X = P.fill_normal(B * K, seed=11).view(B, K)
     q8 = P.q8_1_quantize(X)
     ws = torch.zeros(P.gemv_q8_workspace_bytes(K, N, B), dtype=torch.uint8, device="cuda")
@@ -55,6 +60,27 @@ def main() -> int:
     nbytes = N * K * 17 // 32 + 4 * B * K + 4 * B * N
     print(json.dumps({"N": N, "K": K, "B": B, "us_per_launch": round(us, 2),
                       "algorithmic_bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}))
+    return 0
+
+
+def gemm_case(P, W, N, K, M, launches, warmup):
+    X = P.fill_normal(M * K, seed=11).view(M, K)
+    ws = torch.zeros(P.gemm_workspace_bytes(K, M), dtype=torch.uint8, device="cuda")
+    Y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    for _ in range(warmup):
+        P.gemm(W, X, N, workspace=ws, out=Y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(launches):
+        P.gemm(W, X, N, workspace=ws, out=Y)
+    e1.record()
+    torch.cuda.synchronize()
+    if P.device_error():
+        raise RuntimeError(f"device error word {P.device_error()}")
+    us = e0.elapsed_time(e1) * 1e3 / max(launches, 1)
+    ops = 2 * M * N * K
+    print(json.dumps({"N": N, "K": K, "M": M, "us_per_call": round(us, 2), "tops": round(ops / (us * 1e-6) / 1e12, 1)}))
     return 0
 
 
