@@ -118,14 +118,17 @@ int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, int64_t K, i
  * semantics inside the call) times W^T (IQ4_XS [N][K/256]), ggml layouts.  Same per-sub-block
  * arithmetic as the stock GEMM (real_stock_dp4a_comparator.hip:375-443).  K % 512 == 0 (whole
  * super-block pairs, the tensor-map granule); M, N >= 1.  The workspace holds the quantised
- * activations (iq4xs_gemm_workspace_bytes(K, M), 256-byte aligned, no zeroing needed).
+ * activations (iq4xs_gemm_workspace_bytes(K, M) bytes, 256-byte aligned, no zeroing needed).
  * Replaces gemm_iq4xs_stock_dp4a_gpu / gemm_iq4xs_wmma_stream_gpu (which allocate per call). */
 size_t iq4xs_gemm_workspace_bytes(int64_t K, int64_t M);
 int iq4xs_gemm(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
                void* workspace, size_t workspace_bytes, cudaStream_t stream);
-/* The GEMM's activation quantiser alone, into `workspace`: fp16 q [M][K] (exact integers, within
- * each 32-block element 4w+i+16j at position 8w+2i+j) followed, at the next 256-byte boundary, by
- * fp32 d [K/32][round_up(M,4)] (the value of the truncated fp16 d of each Q8_1 block).  For tests. */
+/* The GEMM's activation quantiser alone, into `workspace` (iq4xs_gemm_workspace_bytes(K, M)): one
+ * 17,408-byte block per (128-token tile t, 64-wide K stage s) at offset (t*(K/64) + s)*17408:
+ * fp16 q of the tile's tokens (exact integers) in the 128-byte-swizzled K-major layout (token r,
+ * 16-byte chunk c at (r/8)*1024 + (r%8)*128 + (c ^ r%8)*16; within each 32-block element 4w+i+16j
+ * at position 8w+2i+j), then fp32 d [2][128] (the value of the truncated fp16 d of each Q8_1
+ * block) for the stage's two 32-blocks.  Tokens past M are zeros.  For tests. */
 int iq4xs_debug_gemm_quantize(const float* X, void* workspace, int64_t K, int64_t M, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------------------------ */

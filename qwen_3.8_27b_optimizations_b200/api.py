@@ -206,17 +206,22 @@ def gemm(W, X, N: int, workspace=None, out=None, stream=None):
 
 
 def debug_gemm_quantize(X, stream=None):
-    """The GEMM's activation quantiser: (fp16 q [M][K] in the lookup order, fp32 d [K/32][M])."""
+    """The GEMM's activation quantiser, unpacked from its stage blocks into
+    (fp16 q [M][K] in the lookup order within each 32-block, fp32 d [K/32][M])."""
     torch = _torch()
     X = X.contiguous()
     M, K = X.shape
     ws = torch.zeros(gemm_workspace_bytes(K, M), dtype=torch.uint8, device=X.device)
     _check("iq4xs_debug_gemm_quantize", lib().iq4xs_debug_gemm_quantize(_ptr(X), _ptr(ws), K, M, _stream(stream)))
-    qbytes = M * K * 2
-    off = (qbytes + 255) // 256 * 256
-    ld = (M + 3) // 4 * 4
-    xq = ws[:qbytes].view(torch.float16).view(M, K)
-    xs = ws[off:off + (K // 32) * ld * 4].view(torch.float32).view(K // 32, ld)[:, :M]
+    T, S = (M + 127) // 128, K // 64
+    blocks = ws.view(T, S, 17408)
+    r = torch.arange(128, device=X.device)[:, None]
+    p = torch.arange(64, device=X.device)[None, :]
+    idx = ((r // 8) * 1024 + (r % 8) * 128 + (((p // 8) ^ (r % 8)) * 16) + (p % 8) * 2) // 2   # [128][64]
+    q16 = blocks[:, :, :16384].contiguous().view(torch.float16).view(T, S, 8192)
+    xq = q16[:, :, idx.reshape(-1)].view(T, S, 128, 64).permute(0, 2, 1, 3).reshape(T * 128, K)[:M]
+    xs = blocks[:, :, 16384:].contiguous().view(torch.float32).view(T, S, 2, 128)
+    xs = xs.permute(1, 2, 0, 3).reshape(K // 32, T * 128)[:, :M]
     return xq, xs
 
 

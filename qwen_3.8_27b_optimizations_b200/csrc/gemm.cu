@@ -23,12 +23,20 @@
 //    -1152.  Within a sub-block the K order is the lookup's natural order: position 8w + 2i + j holds
 //    element 4w + i + 16j (w = qs word, i = byte in word, j = nibble); the activation quantizer
 //    writes the same order, and a permutation of K inside a sub-block leaves the dot unchanged.
-//  * Activations: quantised once per call to fp16 q [M][K] (that order) plus fp32 d_x [K/32][Mp]
-//    (the fp32 value of the truncated fp16 d of the Q8_1 block: the reference's low2float(ds));
-//    128 tokens x 64 K per stage by TMA with 128-byte swizzle, the scales by a second TMA.
+//  * Activations: quantised once per call into stage blocks, one per (128-token tile, 64-wide K
+//    stage): 16 KB of fp16 q (exact integers, that K order) already in the 128-byte-swizzled K-major
+//    layout, then 2 x 128 fp32 d_x (the fp32 value of the truncated fp16 d of each Q8_1 block: the
+//    reference's low2float(ds)).  A stage is one contiguous 17,408-byte bulk copy: a 2-D tensor box
+//    of 128 rows x 128 bytes moves as 128 separate rows and ran several times slower.
 //  * Persistent kernel, one CTA per SM; tiles (128 rows x 128 tokens) in row-tile-major order so the
 //    CTAs running at once share weight rows in L2.  Warp roles: 0 weight TMA, 1 TMEM allocation and
-//    MMA issue (one thread), 2 activation TMA, 3-6 converters, 7-14 drain + epilogue.
+//    MMA issue (one thread), 2 activation TMA, 3 spare, 4-7 converters, 8-23 drain +
+//    epilogue.
+//  * Synchronisation is per 64-wide stage, not per sub-block: an mbarrier operation costs a few
+//    hundred cycles of latency here, so the single MMA-issuing thread waits on one "stage full"
+//    barrier (activation copy + four converter warps) and one "TMEM pair free" barrier per stage,
+//    and the two sub-block accumulators of a stage form a TMEM pair (two pairs, 512 columns).
+//    Waiters poll both of their barriers with one non-blocking test per round trip.
 //  * Every mbarrier wait is bounded (sleeping try_wait); a wait that gives up records a device
 //    error, raises the CTA's abort flag, and every role leaves its loop; in-flight TMA copies and
 //    MMAs are waited for (bounded) and TMEM is freed before the CTA exits.  No cluster multicast.
@@ -49,8 +57,11 @@ constexpr int kStages = 4;       // A / B / scale ring depth
 constexpr int kRawStages = 2;    // raw weight ring depth (one super-block pair each)
 constexpr int kAccBufs = 4;      // TMEM accumulators (4 x 128 = 512 columns)
 constexpr int kConvWarps = 4;
-constexpr int kDrainWarps = 8;
-constexpr int kThreads = 32 * (3 + kConvWarps + kDrainWarps);  // 480
+constexpr int kDrainWarps = 16;  // 4 per TMEM lane quarter, 32 token columns each
+constexpr int kFirstConvWarp = 4;                             // warps 0-3: weight TMA, MMA, act TMA, spare
+constexpr int kFirstDrainWarp = kFirstConvWarp + kConvWarps;  // 8
+constexpr int kThreads = 32 * (kFirstDrainWarp + kDrainWarps);  // 768
+
 
 constexpr uint32_t kRawBytes = kBM * 272;        // 34,816
 constexpr uint32_t kABytes = kBM * kBK * 2;      // 16,384
@@ -58,14 +69,15 @@ constexpr uint32_t kBBytes = kBN * kBK * 2;      // 16,384
 constexpr uint32_t kSxBytes = 2 * kBN * 4;       // 1,024
 constexpr uint32_t kSwBytes = 2 * kBM * 4;       // 1,024
 
+constexpr uint32_t kActStageBytes = kBBytes + kSxBytes;  // 17,408: one activation stage block
+
 constexpr uint32_t kOffA = 0;
-constexpr uint32_t kOffB = kOffA + kStages * kABytes;
-constexpr uint32_t kOffRaw = kOffB + kStages * kBBytes;
-constexpr uint32_t kOffSx = kOffRaw + kRawStages * kRawBytes;
-constexpr uint32_t kOffSw = kOffSx + kStages * kSxBytes;
+constexpr uint32_t kOffB = kOffA + kStages * kABytes;          // stage s: B at kOffB + s*17408, d_x after it
+constexpr uint32_t kOffRaw = kOffB + kStages * kActStageBytes;
+constexpr uint32_t kOffSw = kOffRaw + kRawStages * kRawBytes;
 constexpr uint32_t kOffBar = kOffSw + kStages * kSwBytes;
-constexpr int kNumBars = 2 * kRawStages + 4 * kStages + 2 * kAccBufs + 1;
-constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;  // TMEM address, abort flag
+constexpr int kNumBars = 2 * kRawStages + 2 * kStages + 2 * (kAccBufs / 2) + 1;
+constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;  // TMEM address, abort flag, stage verdict
 constexpr uint32_t kSmemBytes = kOffMisc + 16 + 1024;  // + slack to align the base to 1024
 
 // Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B fp16 (bits 7-9, 10-12 = 0),
@@ -79,14 +91,6 @@ constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
-        : "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d_nohint(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
@@ -121,20 +125,40 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr)
         : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void sts_u4(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
+__device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Packed fp32 pair arithmetic (sm_100): d = a * b and d = a * b + d, two lanes per instruction.
+__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rd, {%0, %1};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rd;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
 
 // Bounded sleeping wait on one phase parity; gives up (error word + abort flag) after ~20 s or
 // when another role raised the abort flag.
@@ -183,21 +207,53 @@ __device__ __forceinline__ uint4 expand_word(uint32_t x, const uint32_t (&lut)[4
 }
 }  // namespace
 
+// Spin (bounded) until two barrier phases have both completed; test_wait does not block, so one
+// poll of both costs one round trip.  Gives up when another role raised the abort flag.
+__device__ __forceinline__ bool gwait2(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2,
+                                       volatile uint32_t* abort_flag, uint32_t* err, uint32_t code) {
+    for (uint32_t i = 0; i < (1u << 28); ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred q1, q2;\n\t"
+            "mbarrier.test_wait.parity.shared::cta.b64 q1, [%1], %2;\n\t"
+            "mbarrier.test_wait.parity.shared::cta.b64 q2, [%3], %4;\n\t"
+            "and.pred q1, q1, q2;\n\t"
+            "selp.u32 %0, 1, 0, q1;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_addr(b1)), "r"(p1), "r"(smem_addr(b2)), "r"(p2)
+            : "memory");
+        if (ok) return true;
+        if ((i & 63u) == 63u && *abort_flag) return false;
+    }
+    record_error(err, code);
+    *abort_flag = 1u;
+    return false;
+}
+
+// Bounded wait without a suspend hint (prompt wake-up), giving up on abort.
+__device__ __forceinline__ bool gwait_fast(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag, uint32_t* err,
+                                           uint32_t code) {
+    for (uint32_t i = 0; i < (1u << 24); ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15u) == 15u && *abort_flag) return false;
+    }
+    record_error(err, code);
+    *abort_flag = 1u;
+    return false;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_iq4xs_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                         const __grid_constant__ CUtensorMap tmap_s, const GemmArgs a) {
+    gemm_iq4xs_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const GemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-    uint64_t* raw_full = bars;
-    uint64_t* raw_empty = raw_full + kRawStages;
-    uint64_t* a_full = raw_empty + kRawStages;
-    uint64_t* b_full = a_full + kStages;
-    uint64_t* ab_empty = b_full + kStages;
-    uint64_t* s_empty = ab_empty + kStages;
-    uint64_t* t_full = s_empty + kStages;
-    uint64_t* t_empty = t_full + kAccBufs;
-    uint64_t* mma_done = t_empty + kAccBufs;
+    uint64_t* raw_full = bars;                       // weight pair landed (TMA bytes)
+    uint64_t* raw_empty = raw_full + kRawStages;     // converters done with a weight pair
+    uint64_t* full = raw_empty + kRawStages;         // stage: activation copy landed + 4 converter warps
+    uint64_t* freeb = full + kStages;                // stage: MMAs done (commit) + drain done with its scales
+    uint64_t* t_full = freeb + kStages;              // TMEM pair: both sub-block MMAs of a stage done
+    uint64_t* t_empty = t_full + kAccBufs / 2;       // TMEM pair: drain warps have loaded it
+    uint64_t* mma_done = t_empty + kAccBufs / 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc + 4);
 
@@ -213,12 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&raw_empty[i], kConvWarps);
         }
         for (int i = 0; i < kStages; ++i) {
-            mbar_init(&a_full[i], kConvWarps);
-            mbar_init(&b_full[i], 1);
-            mbar_init(&ab_empty[i], 1);
-            mbar_init(&s_empty[i], kDrainWarps);
+            mbar_init(&full[i], 1 + kConvWarps);
+            mbar_init(&freeb[i], 1 + kDrainWarps);
         }
-        for (int i = 0; i < kAccBufs; ++i) {
+        for (int i = 0; i < kAccBufs / 2; ++i) {
             mbar_init(&t_full[i], 1);
             mbar_init(&t_empty[i], kDrainWarps);
         }
@@ -226,8 +280,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0u;
         fence_mbar_init();
         prefetch_tmap(&tmap_w);
-        prefetch_tmap(&tmap_x);
-        prefetch_tmap(&tmap_s);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
@@ -268,46 +320,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t it = 0;
             bool ok = true;
             for (int64_t t = blockIdx.x; t < T && ok; t += gridDim.x) {
-                const int m0 = (int)(t % tiles_m) * kBN;
+                const int64_t mt = t % tiles_m;
                 for (int st = 0; st < S; ++st, ++it) {
                     const int s = (int)(it % kStages);
                     const uint32_t u = it / kStages;
-                    if (!(ok = gwait(&ab_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
-                    if (!(ok = gwait(&s_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
-                    mbar_arrive_expect_tx(&b_full[s], kBBytes + kSxBytes);
-                    tma_load_2d(smem + kOffB + s * kBBytes, &tmap_x, st * kBK, m0, &b_full[s]);
-                    tma_load_2d(smem + kOffSx + s * kSxBytes, &tmap_s, m0, 2 * st, &b_full[s]);
+                    if (!(ok = gwait_fast(&freeb[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
+                    mbar_arrive_expect_tx(&full[s], kActStageBytes);
+                    bulk_g2s(smem + kOffB + s * kActStageBytes, a.act + ((size_t)mt * S + st) * kActStageBytes,
+                             kActStageBytes, &full[s]);
                 }
             }
             for (uint32_t j = it > (uint32_t)kStages ? it - kStages : 0; j < it; ++j)
-                gdrain(&b_full[j % kStages], (j / kStages) & 1u, a.err);
+                gdrain(&full[j % kStages], (j / kStages) & 1u, a.err);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issue
         if (lane == 0) {
-            uint32_t it = 0, q = 0;
+            uint32_t it = 0;
             bool ok = true;
             for (int64_t t = blockIdx.x; t < T && ok; t += gridDim.x) {
                 for (int st = 0; st < S && ok; ++st, ++it) {
                     const int s = (int)(it % kStages);
                     const uint32_t u = it / kStages;
-                    if (!(ok = gwait(&a_full[s], u & 1u, abort_flag, a.err, kDevErrMmaWait))) break;
-                    if (!(ok = gwait(&b_full[s], u & 1u, abort_flag, a.err, kDevErrMmaWait))) break;
+                    const int g = (int)(it & 1u);
+                    const uint32_t ug = it >> 1;
+                    if (!(ok = gwait2(&full[s], u & 1u, &t_empty[g], (ug & 1u) ^ 1u, abort_flag, a.err, kDevErrMmaWait)))
+                        break;
                     tc_fence_after();
                     const uint64_t ad = smem_desc_sw128(smem_addr(smem + kOffA + s * kABytes));
-                    const uint64_t bd = smem_desc_sw128(smem_addr(smem + kOffB + s * kBBytes));
-                    for (int h = 0; h < 2; ++h, ++q) {
-                        const int j = (int)(q % kAccBufs);
-                        const uint32_t uq = q / kAccBufs;
-                        if (!(ok = gwait(&t_empty[j], (uq & 1u) ^ 1u, abort_flag, a.err, kDevErrMmaWait))) break;
-                        tc_fence_after();
-                        const uint32_t d = tmem_base + (uint32_t)(j * kBN);
-                        // K offsets 32h and 32h+16 fp16 = 64h and 64h+32 bytes = 4h and 4h+2 in 16-byte units.
-                        tc_mma_f16(d, ad + (uint64_t)(4 * h), bd + (uint64_t)(4 * h), 0u);
-                        tc_mma_f16(d, ad + (uint64_t)(4 * h + 2), bd + (uint64_t)(4 * h + 2), 1u);
-                        tc_commit(&t_full[j]);
-                    }
-                    if (ok) tc_commit(&ab_empty[s]);
+                    const uint64_t bd = smem_desc_sw128(smem_addr(smem + kOffB + s * kActStageBytes));
+                    const uint32_t d = tmem_base + (uint32_t)(g * 2 * kBN);
+                    // Sub-block h -> accumulator d + h*128; K offsets 32h, 32h+16 fp16 = 4h, 4h+2 in 16-byte units.
+                    tc_mma_f16(d, ad, bd, 0u);
+                    tc_mma_f16(d, ad + 2, bd + 2, 1u);
+                    tc_mma_f16(d + kBN, ad + 4, bd + 4, 0u);
+                    tc_mma_f16(d + kBN, ad + 6, bd + 6, 1u);
+                    tc_commit(&t_full[g]);
+                    tc_commit(&freeb[s]);
                 }
             }
             // All issued MMAs complete before TMEM is released.
@@ -315,29 +364,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             gdrain(mma_done, 0u, a.err);
         }
         __syncwarp();
-    } else if (warp < 3 + kConvWarps) {
+    } else if (warp == 3) {
+        // spare warp (keeps the converter and drain warps on fixed sub-partitions)
+    } else if (warp < kFirstDrainWarp) {
         // ------------------------------------------------------------------ converters: thread = row
-        const int r = threadIdx.x - 96;
+        const int r = threadIdx.x - 32 * kFirstConvWarp;
         const uint32_t lut[4] = {a.lut[0], a.lut[1], a.lut[2], a.lut[3]};
         uint32_t rit = 0, it = 0;
         bool ok = true;
         for (int64_t t = blockIdx.x; t < T && ok; t += gridDim.x) {
             for (int p = 0; p < pairs && ok; ++p, ++rit) {
                 const int rs = (int)(rit % kRawStages);
-                if (!(ok = gwait(&raw_full[rs], (rit / kRawStages) & 1u, abort_flag, a.err, kDevErrFullWait))) break;
+                if (!(ok = gwait_fast(&raw_full[rs], (rit / kRawStages) & 1u, abort_flag, a.err, kDevErrFullWait))) break;
                 const uint32_t rowp = smem_addr(smem + kOffRaw + rs * kRawBytes) + (uint32_t)r * 272u;
                 for (int sp = 0; sp < 8; ++sp, ++it) {
                     const int s = (int)(it % kStages);
                     const uint32_t u = it / kStages;
-                    if (!(ok = gwait(&ab_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
-                    if (!(ok = gwait(&s_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
+                    if (!(ok = gwait_fast(&freeb[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
                     const uint32_t sbp = rowp + (uint32_t)(sp >> 2) * 136u;
                     const uint2 hdr = lds_u2(sbp);
                     const float dw = f16_bits_to_f32(hdr.x);
                     const int ib0 = 2 * (sp & 3);
-                    float* sw = reinterpret_cast<float*>(smem + kOffSw + s * kSwBytes);
-                    sw[r] = dw * (float)(subblock_scale(hdr.x, hdr.y, ib0) - 32);
-                    sw[kBM + r] = dw * (float)(subblock_scale(hdr.x, hdr.y, ib0 + 1) - 32);
+                    const uint32_t sw = smem_addr(smem + kOffSw + s * kSwBytes) + 4u * (uint32_t)r;
+                    sts_f32(sw, dw * (float)(subblock_scale(hdr.x, hdr.y, ib0) - 32));
+                    sts_f32(sw + 4u * kBM, dw * (float)(subblock_scale(hdr.x, hdr.y, ib0 + 1) - 32));
                     const uint32_t qp = sbp + 8u + 32u * (uint32_t)(sp & 3);
                     uint32_t qw[8];
 #pragma unroll
@@ -346,15 +396,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         qw[2 * k] = v.x;
                         qw[2 * k + 1] = v.y;
                     }
-                    uint8_t* arow = smem + kOffA + s * kABytes + (r >> 3) * 1024 + (r & 7) * 128;
+                    const uint32_t arow = smem_addr(smem + kOffA + s * kABytes) + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const uint4 v = expand_word(qw[c], lut);
-                        *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = v;
-                    }
+                    for (int c = 0; c < 8; ++c) sts_u4(arow + (uint32_t)((c ^ (r & 7)) << 4), expand_word(qw[c], lut));
                     fence_proxy_async_smem();  // generic-proxy writes -> tensor-core (async proxy) reads
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[s]);
+                    if (lane == 0) mbar_arrive(&full[s]);
                 }
                 __syncwarp();
                 if (ok && lane == 0) mbar_arrive(&raw_empty[rs]);
@@ -362,70 +409,69 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------------ drain + epilogue
-        const int dw = warp - (3 + kConvWarps);       // 0..7
+        const int dw = warp - kFirstDrainWarp;        // 0..15
         const int lq = warp & 3;                      // TMEM lane quarter this warp may access
-        const int ch = dw >> 2;                       // token half: columns 64*ch .. 64*ch+63
+        const int cg = dw >> 2;                       // token columns 32*cg .. 32*cg+31
         const int r = 32 * lq + lane;                 // tile row = TMEM lane
-        const uint32_t lane_base = tmem_base + ((uint32_t)(32 * lq) << 16) + (uint32_t)(64 * ch);
-        uint32_t it = 0, q = 0;
-        bool ok = true;
-        for (int64_t t = blockIdx.x; t < T && ok; t += gridDim.x) {
+        const uint32_t lane_base = tmem_base + ((uint32_t)(32 * lq) << 16) + (uint32_t)(32 * cg);
+        const uint32_t sw_base = smem_addr(smem + kOffSw) + 4u * (uint32_t)r;
+        const uint32_t sx_base = smem_addr(smem + kOffB + kBBytes) + 4u * (uint32_t)(32 * cg);
+        uint32_t it = 0;
+        bool go = true;
+        for (int64_t t = blockIdx.x; t < T && go; t += gridDim.x) {
             const int row0 = (int)(t / tiles_m) * kBM;
             const int m0 = (int)(t % tiles_m) * kBN;
-            float acc[64];
+            float acc[32];
 #pragma unroll
-            for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
-            for (int st = 0; st < S && ok; ++st, ++it) {
+            for (int c = 0; c < 32; ++c) acc[c] = 0.0f;
+            for (int st = 0; st < S; ++st, ++it) {
                 const int s = (int)(it % kStages);
-                const uint32_t u = it / kStages;
-                // Scales of this stage: weight side from the converters, token side from TMA.
-                if (!(ok = gwait(&a_full[s], u & 1u, abort_flag, a.err, kDevErrFullWait))) break;
-                if (!(ok = gwait(&b_full[s], u & 1u, abort_flag, a.err, kDevErrFullWait))) break;
-                const float* sw = reinterpret_cast<const float*>(smem + kOffSw + s * kSwBytes);
-                const float* sx = reinterpret_cast<const float*>(smem + kOffSx + s * kSxBytes);
-                for (int h = 0; h < 2; ++h, ++q) {
-                    const int j = (int)(q % kAccBufs);
-                    if (!(ok = gwait(&t_full[j], (q / kAccBufs) & 1u, abort_flag, a.err, kDevErrMmaWait))) break;
-                    tc_fence_after();
-                    const float wsc = sw[h * kBM + r];
-                    const float4* sxv = reinterpret_cast<const float4*>(sx + h * kBN + 64 * ch);
+                const int g = (int)(it & 1u);
+                // t_full: both sub-block MMAs of the stage are done; full[s] (complete before the MMAs were
+                // issued) makes the activation and weight scales of the stage visible to this warp.
+                if (lane == 0)
+                    go = gwait2(&t_full[g], (it >> 1) & 1u, &full[s], (it / kStages) & 1u, abort_flag, a.err, kDevErrMmaWait);
+                go = __shfl_sync(0xFFFFFFFFu, go ? 1 : 0, 0) != 0;
+                if (!go) break;
+                tc_fence_after();
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
                     uint32_t v[32];
-                    tmem_ld32(lane_base + (uint32_t)(j * kBN), v);
+                    tmem_ld16(lane_base + (uint32_t)(g * 2 * kBN + h * kBN), *reinterpret_cast<uint32_t(*)[16]>(v));
+                    tmem_ld16(lane_base + (uint32_t)(g * 2 * kBN + h * kBN + 16), *reinterpret_cast<uint32_t(*)[16]>(v + 16));
                     tmem_wait_ld();
-#pragma unroll
-                    for (int c4 = 0; c4 < 8; ++c4) {
-                        const float4 x = sxv[c4];
-                        acc[4 * c4 + 0] = fmaf(__uint_as_float(v[4 * c4 + 0]) * x.x, wsc, acc[4 * c4 + 0]);
-                        acc[4 * c4 + 1] = fmaf(__uint_as_float(v[4 * c4 + 1]) * x.y, wsc, acc[4 * c4 + 1]);
-                        acc[4 * c4 + 2] = fmaf(__uint_as_float(v[4 * c4 + 2]) * x.z, wsc, acc[4 * c4 + 2]);
-                        acc[4 * c4 + 3] = fmaf(__uint_as_float(v[4 * c4 + 3]) * x.w, wsc, acc[4 * c4 + 3]);
+                    if (h == 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&t_empty[g]);
                     }
-                    tmem_ld32(lane_base + (uint32_t)(j * kBN + 32), v);
-                    tmem_wait_ld();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&t_empty[j]);
+                    {
+                        const float wsc = lds_f32(sw_base + (uint32_t)(s * kSwBytes + h * kBM * 4));
+                        const uint32_t sxa = sx_base + (uint32_t)(s * kActStageBytes + h * kBN * 4);
 #pragma unroll
-                    for (int c4 = 0; c4 < 8; ++c4) {
-                        const float4 x = sxv[8 + c4];
-                        acc[32 + 4 * c4 + 0] = fmaf(__uint_as_float(v[4 * c4 + 0]) * x.x, wsc, acc[32 + 4 * c4 + 0]);
-                        acc[32 + 4 * c4 + 1] = fmaf(__uint_as_float(v[4 * c4 + 1]) * x.y, wsc, acc[32 + 4 * c4 + 1]);
-                        acc[32 + 4 * c4 + 2] = fmaf(__uint_as_float(v[4 * c4 + 2]) * x.z, wsc, acc[32 + 4 * c4 + 2]);
-                        acc[32 + 4 * c4 + 3] = fmaf(__uint_as_float(v[4 * c4 + 3]) * x.w, wsc, acc[32 + 4 * c4 + 3]);
+                        for (int c4 = 0; c4 < 8; ++c4) {
+                            const uint4 x = lds_u4(sxa + 16u * c4);
+                            float t0, t1, t2, t3;
+                            mul2(t0, t1, __uint_as_float(v[4 * c4 + 0]), __uint_as_float(v[4 * c4 + 1]), __uint_as_float(x.x),
+                                 __uint_as_float(x.y));
+                            mul2(t2, t3, __uint_as_float(v[4 * c4 + 2]), __uint_as_float(v[4 * c4 + 3]), __uint_as_float(x.z),
+                                 __uint_as_float(x.w));
+                            fma2(acc[4 * c4 + 0], acc[4 * c4 + 1], t0, t1, wsc, wsc);
+                            fma2(acc[4 * c4 + 2], acc[4 * c4 + 3], t2, t3, wsc, wsc);
+                        }
                     }
                 }
-                if (!ok) break;
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&s_empty[s]);
+                if (lane == 0) mbar_arrive(&freeb[s]);
             }
-            if (!ok) break;
+            if (!go) break;
             // Epilogue: Y[m][n] at Y + m*ldy_m + n*ldy_n.
             const int64_t n = (int64_t)row0 + r;
             if (n < a.N) {
                 float* yrow = a.y + n * a.ldy_n;
 #pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    const int64_t m = (int64_t)m0 + 64 * ch + c;
+                for (int c = 0; c < 32; ++c) {
+                    const int64_t m = (int64_t)m0 + 32 * cg + c;
                     if (m < a.M) yrow[m * a.ldy_m] = acc[c];
                 }
             }
@@ -444,23 +490,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------------------------------
 // Activation quantizer for the GEMM: Q8_1 semantics bit for bit (amax / sum butterflies,
-// d = amax/127, q = roundf(x/d), q = 0 for an all-zero block), written as fp16 q [M][K] in the
-// lookup order within each 32-block (element e = 4w+i+16j at position 8w+2i+j) and fp32 scales
-// xs[K/32][ldxs] = the value of the truncated fp16 d.  One warp per block.
-__global__ void __launch_bounds__(256) gemm_act_quantize_kernel(const float* __restrict__ X, __half* __restrict__ xq,
-                                                                float* __restrict__ xs, int64_t K, int64_t M,
-                                                                int64_t stride_m, int64_t stride_k, int64_t ldxs) {
+// d = amax/127, q = roundf(x/d), q = 0 for an all-zero block), written as the kernel's stage blocks:
+// block (tile mt, stage st) at act + (mt*S + st)*17408 holds fp16 q of tokens 128mt..128mt+127 for
+// K = 64st..64st+63 in the 128-byte-swizzled K-major layout (token r, 16-byte chunk c at
+// (r/8)*1024 + (r%8)*128 + ((c ^ r%8)*16)), K in the lookup order within each 32-block (element
+// e = 4w+i+16j at position 8w+2i+j), then fp32 d_x[h][r] for the stage's two sub-blocks h.  Tokens
+// past M (tail of the last tile) are written as zeros.  One warp per Q8_1 block.
+__global__ void __launch_bounds__(256) gemm_act_quantize_kernel(const float* __restrict__ X, uint8_t* __restrict__ act,
+                                                                int64_t K, int64_t M, int64_t Mpad, int64_t stride_m,
+                                                                int64_t stride_k) {
     grid_dependency_wait();
     const unsigned full = 0xFFFFFFFFu;
     const int lane = threadIdx.x & 31;
     const int64_t nb = K / kQK8;
-    const int64_t total = nb * M;
+    const int64_t S = K / kBK;
+    const int64_t total = nb * Mpad;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int pos = 8 * ((lane & 15) >> 2) + 2 * (lane & 3) + (lane >> 4);
     for (int64_t blk = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); blk < total; blk += nwarps) {
         const int64_t m = blk / nb;
         const int64_t ib = blk - m * nb;
-        const float x = X[m * stride_m + (ib * kQK8 + lane) * stride_k];
+        const float x = m < M ? X[m * stride_m + (ib * kQK8 + lane) * stride_k] : 0.0f;
         float amax = fabsf(x), sum = x;
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
@@ -470,8 +520,16 @@ __global__ void __launch_bounds__(256) gemm_act_quantize_kernel(const float* __r
         const float d = amax / 127.0f;
         int q = 0;
         if (amax != 0.0f) q = (int)roundf(x / d);
-        xq[m * K + ib * kQK8 + pos] = __int2half_rn(q);
-        if (lane == 0) xs[ib * ldxs + m] = f16_bits_to_f32(f32_to_f16_trunc(d));
+        const int64_t mt = m >> 7;
+        const int r = (int)(m & 127);
+        const int64_t st = ib >> 1;
+        const int h = (int)(ib & 1);
+        uint8_t* blkp = act + (mt * S + st) * (int64_t)kActStageBytes;
+        const int p = 32 * h + pos;                       // K position within the 64-wide stage
+        const int off = (r >> 3) * 1024 + (r & 7) * 128 + ((((p >> 3) ^ (r & 7))) << 4) + ((p & 7) << 1);
+        *reinterpret_cast<__half*>(blkp + off) = __int2half_rn(q);
+        if (lane == 0)
+            *reinterpret_cast<float*>(blkp + kBBytes + h * 512 + 4 * r) = f16_bits_to_f32(f32_to_f16_trunc(d));
     }
     grid_launch_dependents();
 }
@@ -495,22 +553,21 @@ EncodeTiledFn2 encode_fn2() {
     return fn;
 }
 
-size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
-int64_t ldxs_of(int64_t M) { return (M + 3) & ~(int64_t)3; }
+int64_t mpad_of(int64_t M) { return (M + kBN - 1) / kBN * kBN; }
 }  // namespace
 
 size_t gemm_workspace_bytes(int64_t K, int64_t M) {
-    return align256((size_t)M * (size_t)K * 2) + (size_t)(K / kQK8) * (size_t)ldxs_of(M) * 4;
+    return (size_t)(mpad_of(M) / kBN) * (size_t)(K / kBK) * kActStageBytes;
 }
 
 cudaError_t launch_gemm_quantize(const float* X, void* workspace, int64_t K, int64_t M, int64_t stride_m,
                                  int64_t stride_k, cudaStream_t stream) {
-    __half* xq = static_cast<__half*>(workspace);
-    float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)M * (size_t)K * 2));
-    const int64_t total = (K / kQK8) * M;
+    if (K % kBK != 0) return cudaErrorInvalidValue;
+    const int64_t total = (K / kQK8) * mpad_of(M);
     const int sms = device_sm_count() > 0 ? device_sm_count() : 148;
     const int64_t grid = std::min<int64_t>((total + 7) / 8, (int64_t)sms * 16);
-    gemm_act_quantize_kernel<<<(unsigned)grid, 256, 0, stream>>>(X, xq, xs, K, M, stride_m, stride_k, ldxs_of(M));
+    gemm_act_quantize_kernel<<<(unsigned)grid, 256, 0, stream>>>(X, static_cast<uint8_t*>(workspace), K, M, mpad_of(M),
+                                                                 stride_m, stride_k);
     return cudaGetLastError();
 }
 
@@ -523,10 +580,7 @@ cudaError_t launch_gemm(const uint8_t* W, const float* X, float* Y, int64_t K, i
     if (!enc) return cudaErrorNotSupported;
     cudaError_t e = launch_gemm_quantize(X, workspace, K, M, x_stride_m, x_stride_k, stream);
     if (e != cudaSuccess) return e;
-    __half* xq = static_cast<__half*>(workspace);
-    float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256((size_t)M * (size_t)K * 2));
-
-    CUtensorMap mw, mx, ms;
+    CUtensorMap mw;
     const int pairs = (int)(K / 512);
     {
         const cuuint64_t dims[3] = {34, (cuuint64_t)pairs, (cuuint64_t)N};
@@ -538,29 +592,9 @@ cudaError_t launch_gemm(const uint8_t* W, const float* X, float* Y, int64_t K, i
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
     }
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-        const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-        const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBN};
-        const cuuint32_t estr[2] = {1, 1};
-        if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xq, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-            CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
-    {
-        const int64_t ld = ldxs_of(M);
-        const cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)(K / kQK8)};
-        const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-        const cuuint32_t box[2] = {(cuuint32_t)kBN, 2};
-        const cuuint32_t estr[2] = {1, 1};
-        if (enc(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, xs, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-            CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
 
     GemmArgs a = {};
+    a.act = static_cast<const uint8_t*>(workspace);
     a.y = Y;
     a.err = err;
     a.N = N;
@@ -587,7 +621,7 @@ cudaError_t launch_gemm(const uint8_t* W, const float* X, float* Y, int64_t K, i
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_iq4xs_tc_kernel, mw, mx, ms, a);
+    return cudaLaunchKernelEx(&cfg, gemm_iq4xs_tc_kernel, mw, a);
 }
 
 }  // namespace iq4xs

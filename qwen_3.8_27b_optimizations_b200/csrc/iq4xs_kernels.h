@@ -55,6 +55,7 @@ int device_sm_count();
 
 // Tensor-core prefill GEMM (gemm.cu).  Y[m][n] at y + m*ldy_m + n*ldy_n.
 struct GemmArgs {
+    const uint8_t* act;  // quantised activations in stage blocks (gemm.cu)
     float* y;
     uint32_t* err;
     int64_t N, M;
@@ -63,7 +64,7 @@ struct GemmArgs {
     int tiles_n, tiles_m;  // 128-row weight tiles, 128-token tiles
     uint32_t lut[4];
 };
-// Workspace: fp16 activation quants [M][K] (256-aligned) + fp32 scales [K/32][round_up(M,4)].
+// Workspace: quantised activations as stage blocks of 17,408 bytes, [ceil(M/128)][K/64].
 size_t gemm_workspace_bytes(int64_t K, int64_t M);
 cudaError_t launch_gemm_quantize(const float* X, void* workspace, int64_t K, int64_t M, int64_t stride_m,
                                  int64_t stride_k, cudaStream_t stream);
