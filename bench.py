@@ -16,6 +16,9 @@ e2e    = same metric through the reference-facing ggml hook (custom_gemv_iq4xs_d
          and every output copied back, per GEMV, inside the timed region.
 roofline = the GEMV kernel alone (quantizer excluded), timed per launch with CUDA events on its
          stream, against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+gemm   = prefill GEMM: the same layer shapes at M = 512 and 2048 tokens
+         (iq4xs_gemm: Q8_1 activation quantisation + the tensor-core GEMM per call), TOPS = 2*M*N*K /
+         device time, against the measured dense bf16 tensor peak; reported beside the headline.
 --impl reference: the reference's own CPU path (kernels/matmul_iq4xs/ref_cpu.cpp, compiled unchanged
          into oracle/_ref/) on the host cores, same metric on a bounded row sample.
 """
@@ -44,6 +47,8 @@ SHAPES = [  # (name, N out, K in)
 ]
 BATCHES = [1, 2, 4, 8]
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+GEMM_TOKENS = [512, 2048]
 
 
 def gemv_bytes(N: int, K: int, B: int) -> int:
@@ -69,6 +74,53 @@ def hbm_peak():
         except Exception:
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def bf16_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def gemm_sweep(P, weights, dev, stream, reps: int = 3):
+    """Prefill GEMM over the layer shapes at M = 512 and 2048: per shape the median of 3 timed CUDA-graph
+    replays of `reps` calls (weights alternate between the two copies)."""
+    import torch
+    per, tot_flops, tot_ms = [], 0.0, 0.0
+    for M in GEMM_TOKENS:
+        for i, (name, N, K) in enumerate(SHAPES):
+            X = P.fill_normal(M * K, seed=77 + M + i).view(M, K)
+            Y = torch.empty((M, N), dtype=torch.float32, device=dev)
+            ws = torch.empty(P.gemm_workspace_bytes(K, M), dtype=torch.uint8, device=dev)
+            with torch.cuda.stream(stream):
+                P.gemm(weights[0][i], X, N, workspace=ws, out=Y, stream=stream)
+                stream.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for r in range(reps):
+                        P.gemm(weights[r % 2][i], X, N, workspace=ws, out=Y, stream=stream)
+                g.replay()
+                stream.synchronize()
+                ts = []
+                for _ in range(3):
+                    a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a0.record(stream)
+                    g.replay()
+                    b0.record(stream)
+                    stream.synchronize()
+                    ts.append(a0.elapsed_time(b0) / reps)
+            del g
+            d = statistics.median(ts)
+            fl = 2.0 * M * N * K
+            per.append({"shape": name, "M": M, "us": round(d * 1e3, 1), "tops": round(fl / (d * 1e-3) / 1e12, 1)})
+            tot_flops += fl
+            tot_ms += d
+            del X, Y, ws
+    return per, tot_flops / (tot_ms * 1e-3) / 1e12
 
 
 def ncu_traffic():
@@ -401,6 +453,10 @@ def main():
     h2d = sum(4 * B * K for B in BATCHES for _, _, K in SHAPES)
     d2h = sum(4 * B * N for B in BATCHES for _, N, _ in SHAPES)
 
+    # ---- prefill GEMM sweep (reported beside the headline)
+    gemm_per, gemm_tops = gemm_sweep(P, weights, dev, stream)
+    bpeak, bpeak_kind = bf16_peak()
+
     torch.cuda.synchronize()
     err = P.device_error()
     if err:
@@ -444,6 +500,12 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "custom_gemv_iq4xs_dispatch_batched from a C++ host loop, pinned host x/y"},
+            "gemm": {"metric": "IQ4_XS prefill GEMM TOPS (2*M*N*K / time, Q8_1 quantisation included)",
+                     "value": round(gemm_tops, 1), "unit": "TOPS", "tokens": GEMM_TOKENS,
+                     "roofline": {"bound": "tensor", "achieved": round(gemm_tops, 1), "peak": bpeak,
+                                  "unit": "TFLOP/s", "frac": round(gemm_tops / bpeak, 4), "peak_kind": bpeak_kind,
+                                  "kernel": "gemm_iq4xs_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators)"},
+                     "per_shape": gemm_per},
             "gpu_launches": args.steps * len(SHAPES) * len(BATCHES) * 2,
             "clocks": clocks,
         }

@@ -454,6 +454,13 @@ int device_sm_count() {
     return sms;
 }
 
+int device_smem_optin() {
+    int dev = 0, sms = 0, smem = 0;
+    cudaGetDevice(&dev);
+    device_limits(dev, &sms, &smem);
+    return smem;
+}
+
 cudaError_t launch_gemv_q8(GemvArgs a, int B, cudaStream_t stream, bool pdl) {
     a.sumi = nullptr;
     return dispatch<false>(B, a, stream, pdl);

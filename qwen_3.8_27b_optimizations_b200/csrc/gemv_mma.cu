@@ -29,24 +29,39 @@
 namespace iq4xs {
 
 namespace {
-constexpr int kMmaStages = 8;  // one stage per consumer warp in flight
-constexpr int kNCW = 8;        // consumer warps
+constexpr int kMaxMmaStages = 16;  // stage ring depth: as many as fit, at least one per consumer warp
+constexpr int kNCW = 8;            // consumer warps
 
 struct MmaSmem {
     uint32_t bar_off, flag_off, act_off, dx_off, ring_off, total;
 };
 
 // act: per staged part (up to 2) and sub-block: 32 lanes x uint2 (B fragment words) = 256 B;
-// dx: 8 fp32 per sub-block; ring: kMmaStages x (16 rows x pk pairs x 272 B).
-__host__ __device__ inline MmaSmem mma_smem(int pk) {
+// dx: 8 fp32 per sub-block; ring: `stages` x (16 rows x pk pairs x 272 B).
+__host__ __device__ inline MmaSmem mma_smem(int pk, int stages) {
     MmaSmem L;
     L.bar_off = 0;
-    L.flag_off = 2 * kMmaStages * 8;
-    L.act_off = 256;
+    L.flag_off = 2 * kMaxMmaStages * 8;
+    L.act_off = 384;
     L.dx_off = L.act_off + 2u * (uint32_t)pk * 16 * 256;
     L.ring_off = (L.dx_off + 2u * (uint32_t)pk * 16 * 32 + 127) & ~127u;
-    L.total = L.ring_off + (uint32_t)kMmaStages * 16u * (uint32_t)pk * 272u;
+    L.total = L.ring_off + (uint32_t)stages * 16u * (uint32_t)pk * 272u;
     return L;
+}
+
+// Fused multiply-add on fp32 pairs: (d0, d1) += (a0, a1) * (b0, b1), one instruction on sm_100.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rd, {%0, %1};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rd;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar,
@@ -87,10 +102,10 @@ template <int B, bool kDebug>
 __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
     gemv_iq4xs_q8_mma_kernel(const __grid_constant__ CUtensorMap tmap, const GemvMmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int pk = a.pk, P = a.parts;
-    const MmaSmem L = mma_smem(pk);
+    const int pk = a.pk, P = a.parts, S = a.stages;
+    const MmaSmem L = mma_smem(pk, S);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-    uint64_t* empty = full + kMmaStages;
+    uint64_t* empty = full + kMaxMmaStages;
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.flag_off);
     uint8_t* ring = smem + L.ring_off;
     const uint32_t stage_bytes = 16u * (uint32_t)pk * 272u;
@@ -103,7 +118,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
     const int nunits = (int)(u1 - u0);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kMmaStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -118,8 +133,8 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
             const uint64_t policy = l2_policy_evict_first();
             int it = 0;
             for (; it < nunits; ++it) {
-                const int s = it % kMmaStages;
-                const uint32_t use = (uint32_t)(it / kMmaStages);
+                const int s = it % S;
+                const uint32_t use = (uint32_t)(it / S);
                 if (use > 0 && !wait_sleep(&empty[s], (use - 1) & 1u, abort_flag, a.err, kDevErrEmptyWait)) break;
                 const int64_t u = u0 + it;
                 const int p = (int)(u / T);
@@ -127,11 +142,11 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                 mbar_arrive_expect_tx(&full[s], stage_bytes);
                 tma_load_3d(ring + (size_t)s * stage_bytes, &tmap, 0, p * pk, (int)(t * 16), &full[s], policy);
             }
-            const int first = it > kMmaStages ? it - kMmaStages : 0;
+            const int first = it > S ? it - S : 0;
             for (int j = first; j < it; ++j) {
                 bool landed = false;
                 for (uint32_t i = 0; i < 20000u && !landed; ++i)
-                    landed = mbar_try_wait_sleep(&full[j % kMmaStages], (uint32_t)(j / kMmaStages) & 1u, 1000000u);
+                    landed = mbar_try_wait_sleep(&full[j % S], (uint32_t)(j / S) & 1u, 1000000u);
                 if (!landed) record_error(a.err, kDevErrDrainWait);
             }
         }
@@ -179,14 +194,14 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
 
     // Warp cw owns units it = cw, cw + 8, ... of this CTA: all 16 rows x all sub-blocks of the part.
     for (int it = cw; it < nunits; it += kNCW) {
-        const int s = it % kMmaStages;
+        const int s = it % S;
         const int64_t u = u0 + it;
         const int p = (int)(u / T);
         const int64_t t = u - (int64_t)p * T;
         const int nsup = 2 * min(pk, a.pairs - p * pk);
         const int slot = p - pfirst;
-        const bool ready = !*abort_flag &&
-                           wait_sleep(&full[s], (uint32_t)(it / kMmaStages) & 1u, abort_flag, a.err, kDevErrFullWait);
+        bool ready = !*abort_flag && wait_sleep(&full[s], (uint32_t)(it / S) & 1u, abort_flag, a.err, kDevErrFullWait);
+        ready = __all_sync(0xFFFFFFFFu, ready);  // mma.sync and the shuffles below need the whole warp
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (ready) {
             const uint8_t* rg = ring + (size_t)s * stage_bytes + (size_t)g * row_pitch;
@@ -198,7 +213,20 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                 const uint8_t* b8p = rg8 + j * kBlockBytes;
                 const uint2 h0 = *reinterpret_cast<const uint2*>(b0p);
                 const uint2 h8 = *reinterpret_cast<const uint2*>(b8p);
-                const float dw0 = f16_bits_to_f32(h0.x), dw8 = f16_bits_to_f32(h8.x);
+                // Lane (g, c) computes the weight scale d*(ls-32) of rows g and g+8 for sub-blocks 2c
+                // and 2c+1; the sub-block loop fetches the one it needs from lane 4g + ib/2.
+                float fq0[2], fq8[2];
+                {
+                    const float dw0 = f16_bits_to_f32(h0.x), dw8 = f16_bits_to_f32(h8.x);
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int ib = 2 * c + e;
+                        const int ls0 = (int)(((h0.y >> (4 * ib)) & 0xFu) | ((h0.x >> (12 + 2 * ib)) & 0x30u));
+                        const int ls8 = (int)(((h8.y >> (4 * ib)) & 0xFu) | ((h8.x >> (12 + 2 * ib)) & 0x30u));
+                        fq0[e] = dw0 * (float)(ls0 - 32);
+                        fq8[e] = dw8 * (float)(ls8 - 32);
+                    }
+                }
 #pragma unroll
                 for (int ib = 0; ib < 8; ++ib) {
                     const int sbl = j * 8 + ib;
@@ -214,9 +242,8 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                     int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
                     mma_s8(dh, ah, bf.x, bf.y);
                     mma_s8(dl, al, bf.x, bf.y);
-                    const int ls0 = (int)(((h0.y >> (4 * ib)) & 0xFu) | ((h0.x >> (12 + 2 * ib)) & 0x30u));
-                    const int ls8 = (int)(((h8.y >> (4 * ib)) & 0xFu) | ((h8.x >> (12 + 2 * ib)) & 0x30u));
-                    const float f0 = dw0 * (float)(ls0 - 32), f8 = dw8 * (float)(ls8 - 32);
+                    const float f0 = __shfl_sync(0xFFFFFFFFu, fq0[ib & 1], 4 * g + (ib >> 1));
+                    const float f8 = __shfl_sync(0xFFFFFFFFu, fq8[ib & 1], 4 * g + (ib >> 1));
                     const int s0 = dh[0] - dl[0], s1 = dh[1] - dl[1], s2 = dh[2] - dl[2], s3 = dh[3] - dl[3];
                     if constexpr (kDebug) {
                         const int64_t r0w = t * 16 + g, r8w = r0w + 8;
@@ -226,10 +253,12 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                         if (2 * c < B && r8w < a.N) a.sumi[((int64_t)(2 * c) * a.N + r8w) * nsb + sbg] = s2;
                         if (2 * c + 1 < B && r8w < a.N) a.sumi[((int64_t)(2 * c + 1) * a.N + r8w) * nsb + sbg] = s3;
                     }
-                    acc[0] += (f0 * dx.x) * (float)s0;
-                    acc[1] += (f0 * dx.y) * (float)s1;
-                    acc[2] += (f8 * dx.x) * (float)s2;
-                    acc[3] += (f8 * dx.y) * (float)s3;
+                    // acc += (f * dx) * sumi, as one rounding of the product f*dx and one fused add.
+                    float c0, c1, c2, c3;
+                    mul2(c0, c1, f0, f0, dx.x, dx.y);
+                    mul2(c2, c3, f8, f8, dx.x, dx.y);
+                    fma2(acc[0], acc[1], c0, c1, (float)s0, (float)s1);
+                    fma2(acc[2], acc[3], c2, c3, (float)s2, (float)s3);
                 }
             }
         }
@@ -291,10 +320,18 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Part size: odd number of pairs pk <= 5 (8 stages + two parts of activations fit in shared
-// memory).  A unit runs on one warp: cost of the busiest warp = units per warp x (pk + overhead),
-// the overhead of a unit (stage latency, stores, ticket) counted as 0.75 pairs.
-int choose_pk(int pairs, int64_t tiles, int ctas) {
+// Stage ring depth for part size pk: as many 16-row stages as fit next to the activations (<= 16).
+int mma_stages(int pk, int smem_optin) {
+    int st = kMaxMmaStages;
+    while (st > kNCW && (int)mma_smem(pk, st).total > smem_optin) --st;
+    return st;
+}
+
+// Part size: odd number of pairs pk <= 5 (odd: conflict-free fragment loads).  A unit runs on one
+// warp: cost of the busiest warp = units per warp x (pk + overhead); the overhead of a unit (stage
+// latency, stores, ticket) is 0.75 pairs with one stage per warp and 0.35 once the ring holds at
+// least 1.5 stages per warp (the next unit's copy overlaps the current one).
+int choose_pk(int pairs, int64_t tiles, int ctas, int smem_optin) {
     if (ctas < 1) ctas = 1;
     int best = 1;
     double best_cost = 1e300;
@@ -302,7 +339,8 @@ int choose_pk(int pairs, int64_t tiles, int ctas) {
         const int parts = (pairs + pk - 1) / pk;
         const int64_t U = tiles * parts;
         const int64_t per = (U + (int64_t)ctas * kNCW - 1) / ((int64_t)ctas * kNCW);
-        const double cost = (double)per * ((double)pk + 0.75) + (parts > 1 ? 0.25 : 0.0);
+        const double ovh = mma_stages(pk, smem_optin) >= 12 ? 0.35 : 0.75;
+        const double cost = (double)per * ((double)pk + ovh) + (parts > 1 ? 0.25 : 0.0);
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = pk;
@@ -319,11 +357,11 @@ size_t gemv_mma_partial_bytes(int64_t K, int64_t N, int B) {
 }
 
 // Partial-sum bytes the launch below actually uses for (K, N, B) on a device with `sms` SMs.
-size_t gemv_mma_partial_bytes_for(int64_t K, int64_t N, int B, int sms) {
+size_t gemv_mma_partial_bytes_for(int64_t K, int64_t N, int B, int sms, int smem_optin) {
     if (K % 512 != 0) return 0;
     const int pairs = (int)(K / 512);
     const int64_t T = (N + 15) / 16;
-    const int pk = choose_pk(pairs, T, sms);
+    const int pk = choose_pk(pairs, T, sms, smem_optin);
     const int parts = (pairs + pk - 1) / pk;
     return parts > 1 ? (size_t)parts * B * N * sizeof(float) : 0;
 }
@@ -354,13 +392,14 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     if (!enc) return cudaErrorNotSupported;
     const int pairs = (int)(K / 512);
     const int64_t T = (N + 15) / 16;
-    const int pk = choose_pk(pairs, T, sms);
+    const int pk = choose_pk(pairs, T, sms, smem_optin);
+    const int stages = mma_stages(pk, smem_optin);
     const int parts = (pairs + pk - 1) / pk;
     if (parts > 1 && y) {  // partial sums and per-tile tickets (the debug path writes neither)
         if (!tickets || !partials || partial_bytes < (size_t)parts * B * N * sizeof(float)) return cudaErrorInvalidValue;
         if (T > (int64_t)(kTicketBytes / sizeof(uint32_t))) return cudaErrorInvalidValue;
     }
-    const MmaSmem L = mma_smem(pk);
+    const MmaSmem L = mma_smem(pk, stages);
     if ((int)L.total > smem_optin) return cudaErrorInvalidConfiguration;
 
     CUtensorMap map;
@@ -383,7 +422,7 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     a.pairs = pairs;
     a.pk = pk;
     a.parts = parts;
-    a.stages = kMmaStages;
+    a.stages = stages;
     a.partial = partials;
     a.tile_cnt = tickets;
     for (int i = 0; i < 4; ++i) a.lut[i] = lut[i];

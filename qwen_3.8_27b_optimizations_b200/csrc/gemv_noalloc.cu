@@ -70,7 +70,7 @@ extern "C" int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, i
 
     // Scratch layout: [tickets][Q8_1 activations][partial sums], as the workspace of iq4xs_gemv_f32.
     const size_t q8_bytes = (size_t)(K / kQK8) * (size_t)B * kQ8Bytes;
-    const size_t partials = gemv_mma_partial_bytes_for(K, N, (int)B, device_sm_count());
+    const size_t partials = gemv_mma_partial_bytes_for(K, N, (int)B, device_sm_count(), device_smem_optin());
     const size_t need = kTicketBytes + align_up256(q8_bytes) + partials;
     if (need > kNoAllocScratchBytes) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
 

@@ -47,7 +47,8 @@ struct GemvMmaArgs {
 // Tensor-core GEMV (batch 1..8).  Workspace = [tickets: kTicketBytes, zero between calls][partials].
 constexpr size_t kTicketBytes = 64 * 1024;  // one uint32 per 16-row tile: N <= 262144
 size_t gemv_mma_partial_bytes(int64_t K, int64_t N, int B);
-size_t gemv_mma_partial_bytes_for(int64_t K, int64_t N, int B, int sms);
+size_t gemv_mma_partial_bytes_for(int64_t K, int64_t N, int B, int sms, int smem_optin);
+int device_smem_optin();
 cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32_t* sumi, uint32_t* tickets,
                             float* partials, size_t partial_bytes, int64_t K, int64_t N, int B, cudaStream_t stream,
                             bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4]);
