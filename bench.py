@@ -123,6 +123,52 @@ def gemm_sweep(P, weights, dev, stream, reps: int = 3):
     return per, tot_flops / (tot_ms * 1e-3) / 1e12
 
 
+SHARDED = [("lm_head", 152064, 5120), ("gate_up", 34816, 5120)]
+
+
+def sharded_sweep(P, dev, stream, rank: int, world: int, barrier, reps: int = 5):
+    """lm_head and gate|up split by output rows over the ranks, GEMV at batch 1
+    and GEMM at M = 2048, each call followed by the all-gather of the output slices (NCCL).  Time per
+    call = max over ranks of the CUDA-event time of `reps` calls."""
+    import torch
+    import torch.distributed as dist
+    out = []
+    for name, N, K in SHARDED:
+        r0, r1 = P.sharded.shard_rows(N, world, rank)
+        W = P.random_weights(r1 - r0, K, seed=5000 + N + rank)
+        S = P.sharded.RowShardedIQ4XS(W, N, K, rank=rank, world=world) if world > 1 else \
+            P.sharded.RowShardedIQ4XS(W, N, K, rank=0, world=1)
+        for op, M in (("gemv", 1), ("gemm", 2048)):
+            X = P.fill_normal(M * K, seed=31 + M).view(M, K)
+            fn = (lambda: S.gemv(X)) if op == "gemv" else (lambda: S.gemm_nm(X))
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    fn()
+                stream.synchronize()
+                barrier()
+                a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                for _ in range(reps):
+                    fn()
+                b0.record(stream)
+                stream.synchronize()
+            ms = a0.elapsed_time(b0) / reps
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            rec = {"matrix": name, "N": N, "K": K, "op": op, "M": M, "ranks": world, "ms": round(ms, 4)}
+            if op == "gemv":
+                rec["GBs"] = round((N * K * 17 // 32 + 4 * K + 4 * N) / (ms * 1e-3) / 1e9, 1)
+            else:
+                rec["TOPS"] = round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1)
+            out.append(rec)
+            del X
+        del S, W
+        torch.cuda.empty_cache()
+    return out
+
+
 def ncu_traffic():
     """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary, if present."""
     p = ROOT / "profiles" / "gemv_ncu_traffic.json"
@@ -457,6 +503,9 @@ def main():
     gemm_per, gemm_tops = gemm_sweep(P, weights, dev, stream)
     bpeak, bpeak_kind = bf16_peak()
 
+    # ---- row-sharded lm_head / gate|up across the ranks (strong scaling, output all-gather)
+    sharded = sharded_sweep(P, dev, stream, rank, world, barrier)
+
     torch.cuda.synchronize()
     err = P.device_error()
     if err:
@@ -506,6 +555,8 @@ def main():
                                   "unit": "TFLOP/s", "frac": round(gemm_tops / bpeak, 4), "peak_kind": bpeak_kind,
                                   "kernel": "gemm_iq4xs_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators)"},
                      "per_shape": gemm_per},
+            "sharded": {"what": "row-sharded over the ranks (strong scaling), NCCL all-gather of the outputs, "
+                                "time = max over ranks", "results": sharded},
             "gpu_launches": args.steps * len(SHAPES) * len(BATCHES) * 2,
             "clocks": clocks,
         }

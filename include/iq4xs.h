@@ -123,6 +123,13 @@ int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, int64_t K, i
 size_t iq4xs_gemm_workspace_bytes(int64_t K, int64_t M);
 int iq4xs_gemm(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
                void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* iq4xs_gemm with explicit strides (elements): X(m, k) at X[m*ldx_m + k*ldx_k], Y(m, n) at
+ * Y[m*ldy_m + n*ldy_n].  ggml: ldx = (K, 1), ldy = (N, 1); playground X [K][M], Y [N][M]:
+ * ldx = (1, M), ldy = (1, M) -- the layout in which a row shard of Y is one contiguous block, as an
+ * all-gather of row shards needs.  Strides must be positive; Y must hold every addressed element. */
+int iq4xs_gemm_strided(const void* W, const float* X, int64_t ldx_m, int64_t ldx_k, float* Y, int64_t ldy_m,
+                       int64_t ldy_n, int64_t K, int64_t N, int64_t M, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream);
 /* The GEMM's activation quantiser alone, into `workspace` (iq4xs_gemm_workspace_bytes(K, M)): one
  * 17,408-byte block per (128-token tile t, 64-wide K stage s) at offset (t*(K/64) + s)*17408:
  * fp16 q of the tile's tokens (exact integers) in the 128-byte-swizzled K-major layout (token r,

@@ -40,6 +40,7 @@ SIGNATURES = {
     "iq4xs_gemv_f32_noalloc": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_gemm_workspace_bytes": (_sz, [_i64, _i64]),
     "iq4xs_gemm": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "iq4xs_gemm_strided": (_i, [_vp, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "iq4xs_debug_gemm_quantize": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "iq4xs_debug_subblock_dots": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_gemv_q8_generic": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
@@ -203,6 +204,20 @@ def gemm(W, X, N: int, workspace=None, out=None, stream=None):
     _check("iq4xs_gemm", lib().iq4xs_gemm(_ptr(W), _ptr(X), _ptr(Y), K, N, M, _ptr(ws),
                                           ws.numel() * ws.element_size(), _stream(stream)))
     return Y
+
+
+def gemm_nm(W, X, N: int, workspace=None, out=None, stream=None):
+    """Y^T [N][M] = W . X^T for X [M][K] (the transposed output layout: a row shard of W gives one
+    contiguous block of Y^T)."""
+    torch = _torch()
+    X = X.contiguous()
+    M, K = X.shape
+    need = gemm_workspace_bytes(K, M)
+    ws = workspace if workspace is not None else _workspace(need, X.device, "gemm")
+    Yt = out if out is not None else torch.empty((N, M), dtype=torch.float32, device=X.device)
+    _check("iq4xs_gemm_strided", lib().iq4xs_gemm_strided(_ptr(W), _ptr(X), K, 1, _ptr(Yt), 1, M, K, N, M, _ptr(ws),
+                                                          ws.numel() * ws.element_size(), _stream(stream)))
+    return Yt
 
 
 def debug_gemm_quantize(X, stream=None):

@@ -319,6 +319,13 @@ int iq4xs_gemm(const void* W, const float* X, float* Y, int64_t K, int64_t N, in
     return gemm_strided(W, X, Y, K, N, M, K, 1, N, 1, workspace, workspace_bytes, stream);
 }
 
+int iq4xs_gemm_strided(const void* W, const float* X, int64_t ldx_m, int64_t ldx_k, float* Y, int64_t ldy_m,
+                       int64_t ldy_n, int64_t K, int64_t N, int64_t M, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream) {
+    if (ldx_m <= 0 || ldx_k <= 0 || ldy_m <= 0 || ldy_n <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    return gemm_strided(W, X, Y, K, N, M, ldx_m, ldx_k, ldy_m, ldy_n, workspace, workspace_bytes, stream);
+}
+
 int iq4xs_debug_gemm_quantize(const float* X, void* workspace, int64_t K, int64_t M, cudaStream_t stream) {
     if (!X || !workspace || K <= 0 || M <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
     if (K % kQK8 != 0) return IQ4XS_ERR_UNSUPPORTED_SHAPE;

@@ -1,0 +1,122 @@
+"""Row-sharded IQ4_XS matmuls over the GPUs of one node (one process per GPU, torch.distributed).
+
+The weight matrix W [N][K] is split by output rows: every row is independent, so each rank owns a
+contiguous range of whole 16-row tiles (the GEMV tile height), multiplies it by the full activations
+(quantised to Q8_1 locally on every rank) and the only exchange is one all-gather of the output
+slices (NCCL over NVLink).  Shapes where N splits evenly (lm_head 152064 and gate|up 34816 at 2, 4
+and 8 ranks) gather without padding; otherwise slices are padded to the largest one.
+
+    GEMV (batch B <= 8): local y [B][Nr] -> gathered [P][B][Nr] -> Y [B][N]
+    GEMM (M tokens):     local Y^T [Nr][M] (row shard = one contiguous block) -> gathered Y^T [N][M]
+
+The local compute goes through the C ABI (iq4xs_gemv_f32 / iq4xs_gemm_strided).  `local_gemv` /
+`local_gemm` replace it only in tests that run the host logic on CPU ranks (gloo).
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional, Tuple
+
+TILE_ROWS = 16
+
+
+def shard_rows(N: int, world: int, rank: int) -> Tuple[int, int]:
+    """Row range [r0, r1) of `rank`: whole 16-row tiles, balanced over `world` ranks."""
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"bad rank {rank} of {world}")
+    tiles = (N + TILE_ROWS - 1) // TILE_ROWS
+    t0 = tiles * rank // world
+    t1 = tiles * (rank + 1) // world
+    return min(N, t0 * TILE_ROWS), min(N, t1 * TILE_ROWS)
+
+
+def max_shard_rows(N: int, world: int) -> int:
+    return max(r1 - r0 for r0, r1 in (shard_rows(N, world, r) for r in range(world)))
+
+
+class RowShardedIQ4XS:
+    """One rank's share of a row-sharded IQ4_XS matrix.
+
+    W_local: this rank's rows [r1 - r0][K/256*136] (uint8, on this rank's GPU), as produced by
+    shard_rows(N, world, rank) applied to the full matrix (or quantised there directly).
+    """
+
+    def __init__(self, W_local, N: int, K: int, group=None, rank: Optional[int] = None, world: Optional[int] = None,
+                 local_gemv: Optional[Callable] = None, local_gemm: Optional[Callable] = None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.rank = dist.get_rank(group) if rank is None else rank
+        self.world = dist.get_world_size(group) if world is None else world
+        self.N, self.K = N, K
+        self.r0, self.r1 = shard_rows(N, self.world, self.rank)
+        self.rows = self.r1 - self.r0
+        self.pad = max_shard_rows(N, self.world)
+        if W_local.shape[0] != self.rows:
+            raise ValueError(f"rank {self.rank}: expected {self.rows} weight rows, got {W_local.shape[0]}")
+        self.W = W_local
+        self._gemv = local_gemv
+        self._gemm = local_gemm
+        self._pkg = None
+        if local_gemv is None or local_gemm is None:
+            from . import api as _api  # the CUDA path; raises if the library is missing
+            self._pkg = _api
+
+    # ------------------------------------------------------------------ local compute
+    def _local_gemv(self, X, out):
+        if self._gemv is not None:
+            out.copy_(self._gemv(self.W, X))
+            return out
+        if self.rows == 0:
+            return out
+        return self._pkg.gemv(self.W, X, self.rows, out=out)
+
+    def _local_gemm_nm(self, X, out):
+        if self._gemm is not None:
+            out.copy_(self._gemm(self.W, X))
+            return out
+        if self.rows == 0:
+            return out
+        return self._pkg.gemm_nm(self.W, X, self.rows, out=out)
+
+    # ------------------------------------------------------------------ sharded ops
+    def gemv(self, X):
+        """Y [B][N] on every rank from X [B][K] (the same on every rank)."""
+        import torch
+        X = X if X.dim() == 2 else X[None]
+        B = X.shape[0]
+        loc = torch.zeros((B, self.pad), dtype=torch.float32, device=X.device)
+        if self.rows == self.pad:
+            self._local_gemv(X, loc)
+        else:  # the kernels write a dense [B][rows] block
+            tmp = torch.zeros((B, self.rows), dtype=torch.float32, device=X.device)
+            loc[:, :self.rows] = self._local_gemv(X, tmp)
+        if self.world == 1:
+            return loc[:, :self.N]
+        gathered = torch.empty((self.world * B, self.pad), dtype=torch.float32, device=X.device)
+        self.dist.all_gather_into_tensor(gathered, loc, group=self.group)
+        return self._assemble_bn(gathered.view(self.world, B, self.pad), B)
+
+    def gemm_nm(self, X):
+        """Y^T [N][M] on every rank from X [M][K]."""
+        import torch
+        M = X.shape[0]
+        loc = torch.zeros((self.pad, M), dtype=torch.float32, device=X.device)
+        self._local_gemm_nm(X, loc[:self.rows])
+        if self.world == 1:
+            return loc[:self.N]
+        gathered = torch.empty((self.world * self.pad, M), dtype=torch.float32, device=X.device)
+        self.dist.all_gather_into_tensor(gathered, loc, group=self.group)
+        if self.pad * self.world == self.N:
+            return gathered
+        return torch.cat([gathered[r * self.pad: r * self.pad + (b - a)]
+                          for r, (a, b) in enumerate(shard_rows(self.N, self.world, q) for q in range(self.world))])
+
+    def _assemble_bn(self, gathered, B):
+        import torch
+        if self.pad * self.world == self.N:
+            return gathered.permute(1, 0, 2).reshape(B, self.N)
+        parts = []
+        for r in range(self.world):
+            a, b = shard_rows(self.N, self.world, r)
+            parts.append(gathered[r, :, : b - a])
+        return torch.cat(parts, dim=1)

@@ -1,0 +1,78 @@
+"""Row-sharded GEMV / GEMM through the CUDA path with NCCL (2 ranks when the box has 2 GPUs,
+otherwise 1), against the single-GPU kernels on the full matrix: the GEMM and the batch-1 GEMV
+are per-row identical (bit-exact), batched GEMV partial sums may be split differently (tolerance)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import sys
+    from datetime import timedelta
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root))
+    sys.path.insert(0, str(root / "tests"))
+    import torch.distributed as dist
+    import torch_ref
+    from conftest import load_pkg
+    from oracle import oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        P = load_pkg()
+        res = []
+        for N, K in [(6144, 5120), (1000, 1024)]:
+            W = P.random_weights(N, K, seed=77)                       # same full matrix on every rank
+            r0, r1 = P.sharded.shard_rows(N, world, rank)
+            S = P.sharded.RowShardedIQ4XS(W[r0:r1].contiguous(), N, K)
+            for B in (1, 3):
+                X = P.fill_normal(B * K, seed=5 + B).view(B, K)
+                Y = S.gemv(X)
+                Yf = P.gemv(W, X, N)
+                if B == 1:
+                    res.append(bool(torch.equal(Y, Yf)))
+                else:
+                    Y64, A = torch_ref.matmul_q8(W, P.q8_1_quantize(X), K)
+                    tol = torch.from_numpy(O.tolerance(Y64.cpu().numpy(), A.cpu().numpy(), K // 32, 1e-5))
+                    res.append(bool(((Y.cpu().double() - Y64.cpu()).abs() <= tol).all()))
+            M = 200
+            Xm = P.fill_normal(M * K, seed=9).view(M, K)
+            Yt = S.gemm_nm(Xm)
+            res.append(bool(torch.equal(Yt, P.gemm(W, Xm, N).t())))
+        torch.cuda.synchronize()
+        q.put((rank, res, P.device_error()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_nccl():
+    world = min(2, torch.cuda.device_count())
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    out = [q.get(timeout=5) for _ in range(world)]
+    for rank, res, err in out:
+        assert all(res), (rank, res)
+        assert err == 0
