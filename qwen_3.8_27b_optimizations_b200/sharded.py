@@ -56,6 +56,7 @@ class RowShardedIQ4XS:
         self.W = W_local
         self._gemv = local_gemv
         self._gemm = local_gemm
+        self._bufs = {}
         self._pkg = None
         if local_gemv is None or local_gemm is None:
             from . import api as _api  # the CUDA path; raises if the library is missing
@@ -78,13 +79,23 @@ class RowShardedIQ4XS:
             return out
         return self._pkg.gemm_nm(self.W, X, self.rows, out=out)
 
+    def _buf(self, key, shape, device):
+        """Per-shape output buffers, reused across calls (the result of a call is valid until the
+        next call of the same shape)."""
+        import torch
+        b = self._bufs.get(key)
+        if b is None or tuple(b.shape) != tuple(shape) or b.device != device:
+            b = torch.zeros(shape, dtype=torch.float32, device=device)
+            self._bufs[key] = b
+        return b
+
     # ------------------------------------------------------------------ sharded ops
     def gemv(self, X):
         """Y [B][N] on every rank from X [B][K] (the same on every rank)."""
         import torch
         X = X if X.dim() == 2 else X[None]
         B = X.shape[0]
-        loc = torch.zeros((B, self.pad), dtype=torch.float32, device=X.device)
+        loc = self._buf(("gemv_loc", B), (B, self.pad), X.device)
         if self.rows == self.pad:
             self._local_gemv(X, loc)
         else:  # the kernels write a dense [B][rows] block
@@ -92,7 +103,7 @@ class RowShardedIQ4XS:
             loc[:, :self.rows] = self._local_gemv(X, tmp)
         if self.world == 1:
             return loc[:, :self.N]
-        gathered = torch.empty((self.world * B, self.pad), dtype=torch.float32, device=X.device)
+        gathered = self._buf(("gemv_all", B), (self.world * B, self.pad), X.device)
         self.dist.all_gather_into_tensor(gathered, loc, group=self.group)
         return self._assemble_bn(gathered.view(self.world, B, self.pad), B)
 
@@ -100,11 +111,11 @@ class RowShardedIQ4XS:
         """Y^T [N][M] on every rank from X [M][K]."""
         import torch
         M = X.shape[0]
-        loc = torch.zeros((self.pad, M), dtype=torch.float32, device=X.device)
+        loc = self._buf(("gemm_loc", M), (self.pad, M), X.device)
         self._local_gemm_nm(X, loc[:self.rows])
         if self.world == 1:
             return loc[:self.N]
-        gathered = torch.empty((self.world * self.pad, M), dtype=torch.float32, device=X.device)
+        gathered = self._buf(("gemm_all", M), (self.world * self.pad, M), X.device)
         self.dist.all_gather_into_tensor(gathered, loc, group=self.group)
         if self.pad * self.world == self.N:
             return gathered
