@@ -169,6 +169,47 @@ def sharded_sweep(P, dev, stream, rank: int, world: int, barrier, reps: int = 5)
     return out
 
 
+DECODER_PROMPT, DECODER_STEPS = 512, 128
+
+
+def decoder_run(P, dev, rank: int, world: int, barrier):
+    """the synthetic 64-layer decoder, tensor-parallel over the ranks: a
+    512-token uniform random prompt (seed 7), then 128 greedy decode steps (CUDA-graph replay per
+    token).  Times are CUDA events on each rank, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    cfg = P.decoder.DecoderConfig()
+    t0 = time.time()
+    m = P.decoder.TPDecoder(cfg, rank=rank, world=world, seed=1)
+    torch.cuda.synchronize()
+    build_s = time.time() - t0
+    prompt = torch.randint(0, cfg.vocab, (DECODER_PROMPT,), generator=torch.Generator().manual_seed(7)).to(dev)
+    m.prefill(prompt)
+    m.decode(4)                      # warm-up: eager steps and graph capture
+    barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev[0].record()
+    m.prefill(prompt)
+    ev[1].record()
+    ev[2].record()
+    toks = m.decode(DECODER_STEPS)
+    ev[3].record()
+    torch.cuda.synchronize()
+    t = torch.tensor([ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    pre_ms, dec_ms = float(t[0]), float(t[1])
+    m.release()
+    del m
+    torch.cuda.empty_cache()
+    return {"metric": "decode tok/s (greedy, batch 1)", "value": round(DECODER_STEPS / (dec_ms * 1e-3), 1),
+            "unit": "tok/s", "tp": world, "prompt": DECODER_PROMPT, "steps": DECODER_STEPS,
+            "prefill_ms": round(pre_ms, 1), "prefill_tok_s": round(DECODER_PROMPT / (pre_ms * 1e-3), 1),
+            "decode_ms": round(dec_ms, 1), "build_s": round(build_s, 1), "first_tokens": toks[:8],
+            "model": "64 x (hidden 5120, 64x128 q heads, 8 kv heads, SwiGLU 17408), vocab 152064, IQ4_XS "
+                     "linear layers, fp32 norms, f16 embeddings and KV cache, random N(0, 0.02) init"}
+
+
 def ncu_traffic():
     """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary, if present."""
     p = ROOT / "profiles" / "gemv_ncu_traffic.json"
@@ -506,6 +547,11 @@ def main():
     # ---- row-sharded lm_head / gate|up across the ranks (strong scaling, output all-gather)
     sharded = sharded_sweep(P, dev, stream, rank, world, barrier)
 
+    # ---- synthetic decoder, tensor-parallel over the ranks
+    del weights
+    torch.cuda.empty_cache()
+    decoder = decoder_run(P, dev, rank, world, barrier)
+
     torch.cuda.synchronize()
     err = P.device_error()
     if err:
@@ -555,6 +601,7 @@ def main():
                                   "unit": "TFLOP/s", "frac": round(gemm_tops / bpeak, 4), "peak_kind": bpeak_kind,
                                   "kernel": "gemm_iq4xs_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators)"},
                      "per_shape": gemm_per},
+            "decoder": decoder,
             "sharded": {"what": "row-sharded over the ranks (strong scaling), NCCL all-gather of the outputs, "
                                 "time = max over ranks", "results": sharded},
             "gpu_launches": args.steps * len(SHAPES) * len(BATCHES) * 2,

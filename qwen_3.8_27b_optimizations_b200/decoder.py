@@ -1,0 +1,248 @@
+"""Synthetic ~25B dense decoder on the IQ4_XS matmuls, tensor-parallel over the ranks of one node.
+
+The model of BASELINE.json configs[4]: 64 layers, hidden 5120, 64 query heads x 128 and 8 KV heads
+x 128 (GQA), SwiGLU FFN 17408, RMSNorm, RoPE (theta 1e6), vocab 152064; random N(0, 0.02) linear
+weights quantised to IQ4_XS, fp32 norms, f16 embeddings and KV cache.  Every linear layer runs on the
+IQ4_XS kernels (GEMV for batch <= 8 tokens, the tensor-core GEMM for the prompt); norms, RoPE,
+attention and sampling are plain torch tensor ops around them.
+
+Tensor parallelism (one exchange per block half):
+  * q|k|v fused and gate|up fused are column-parallel: each rank owns whole heads (64/P query,
+    8/P KV heads) and whole 512-wide FFN slices;
+  * o_proj and down_proj are row-parallel: each rank multiplies its K-slice (whole super-block
+    pairs) and the partial outputs are summed with an all-reduce;
+  * lm_head is row-sharded with an all-gather of the logits (sharded.RowShardedIQ4XS).
+The weights are generated identically on every rank from per-matrix seeds and sliced, so the model
+does not depend on P.
+
+The decode step (one token) is captured in a CUDA graph and replayed, the position and the token
+living in device tensors, so generating N tokens issues no host work per token.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable, List, Optional
+
+PAIR = 512  # weights per super-block pair: the K granule of the tensor-map kernels
+
+
+@dataclass
+class DecoderConfig:
+    layers: int = 64
+    hidden: int = 5120
+    heads: int = 64
+    kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 17408
+    vocab: int = 152064
+    rope_theta: float = 1.0e6
+    eps: float = 1.0e-6
+    max_seq: int = 640
+    std: float = 0.02
+
+
+def split_units(n: int, world: int, rank: int):
+    """[a, b) of `n` units for `rank`, balanced."""
+    return n * rank // world, n * (rank + 1) // world
+
+
+class TPDecoder:
+    """One rank's share of the decoder.  `matmul(W, X, N) -> Y [M][N]` (fp32 X [M][K]) defaults to the
+    CUDA kernels; tests on CPU ranks inject a reference."""
+
+    def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, group=None, seed: int = 0,
+                 device="cuda", matmul: Optional[Callable] = None, gen_weights: Optional[Callable] = None,
+                 gen_normal: Optional[Callable] = None):
+        import torch
+        from . import sharded
+        self.torch = torch
+        self.cfg, self.rank, self.world, self.group = cfg, rank, world, group
+        self.device = torch.device(device)
+        if cfg.kv_heads % world or cfg.heads % world:
+            raise ValueError("the rank count must divide the KV head count")
+        if (cfg.heads // world) * cfg.head_dim % PAIR or cfg.hidden % PAIR or cfg.ffn % PAIR:
+            raise ValueError("head groups, hidden and FFN must be whole super-block pairs")
+        self._api = None
+        if matmul is None or gen_weights is None or gen_normal is None:
+            from . import api
+            self._api = api
+        self.matmul = matmul or self._cuda_matmul
+        self.gen_weights = gen_weights or (lambda N, K, s: self._api.random_weights(N, K, seed=s, std=cfg.std))
+        self.gen_normal = gen_normal or (lambda n, s, mean, std: self._api.fill_normal(n, s, mean, std))
+
+        D, hd = cfg.hidden, cfg.head_dim
+        self.hq = cfg.heads // world
+        self.hkv = cfg.kv_heads // world
+        q0, kv0 = rank * self.hq, rank * self.hkv
+        p0, p1 = split_units(cfg.ffn // PAIR, world, rank)
+        self.f0, self.f1 = p0 * PAIR, p1 * PAIR
+        self.F = self.f1 - self.f0
+        self.nqkv = (self.hq + 2 * self.hkv) * hd
+
+        def kslice(W, K, k0, k1):  # columns [k0, k1) of an IQ4_XS matrix, k in whole super-blocks
+            N = W.shape[0]
+            return W.view(N, K // 256, 136)[:, k0 // 256:k1 // 256, :].contiguous().view(N, -1)
+
+        self.layers = []
+        for l in range(cfg.layers):
+            s = seed * 100003 + 16 * l
+            wq = self.gen_weights(cfg.heads * hd, D, s + 1)
+            wk = self.gen_weights(cfg.kv_heads * hd, D, s + 2)
+            wv = self.gen_weights(cfg.kv_heads * hd, D, s + 3)
+            wqkv = torch.cat([wq[q0 * hd:(q0 + self.hq) * hd], wk[kv0 * hd:(kv0 + self.hkv) * hd],
+                              wv[kv0 * hd:(kv0 + self.hkv) * hd]]).contiguous()
+            del wq, wk, wv
+            wo = kslice(self.gen_weights(D, cfg.heads * hd, s + 4), cfg.heads * hd, q0 * hd, (q0 + self.hq) * hd)
+            wg = self.gen_weights(cfg.ffn, D, s + 5)
+            wu = self.gen_weights(cfg.ffn, D, s + 6)
+            wgu = torch.cat([wg[self.f0:self.f1], wu[self.f0:self.f1]]).contiguous()
+            del wg, wu
+            wd = kslice(self.gen_weights(D, cfg.ffn, s + 7), cfg.ffn, self.f0, self.f1)
+            an = self.gen_normal(D, s + 8, 1.0, cfg.std).to(self.device)
+            fn = self.gen_normal(D, s + 9, 1.0, cfg.std).to(self.device)
+            self.layers.append(dict(wqkv=wqkv, wo=wo, wgu=wgu, wd=wd, an=an, fn=fn))
+        s = seed * 100003 + 16 * cfg.layers
+        self.emb = self.gen_normal(cfg.vocab * D, s + 1, 0.0, cfg.std).view(cfg.vocab, D).to(torch.float16)
+        self.final_norm = self.gen_normal(D, s + 2, 1.0, cfg.std).to(self.device)
+        lm = self.gen_weights(cfg.vocab, D, s + 3)
+        r0, r1 = sharded.shard_rows(cfg.vocab, world, rank)
+        self.lm_head = sharded.RowShardedIQ4XS(lm[r0:r1].contiguous(), cfg.vocab, D, group=group, rank=rank,
+                                               world=world, local_gemv=self._lm_local if matmul else None,
+                                               local_gemm=self._lm_local_t if matmul else None)
+        del lm
+        self.cache = torch.zeros((cfg.layers, 2, self.hkv, cfg.max_seq, hd), dtype=torch.float16, device=self.device)
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
+        ang = torch.arange(cfg.max_seq, dtype=torch.float64)[:, None] * inv[None, :]
+        self.cos = torch.cos(ang).to(torch.float32).to(self.device)   # [max_seq][hd/2]
+        self.sin = torch.sin(ang).to(torch.float32).to(self.device)
+        self.graph = None
+
+    # ------------------------------------------------------------------ building blocks
+    def _cuda_matmul(self, W, X, N):
+        if X.shape[0] <= 8:
+            return self._api.gemv(W, X, N, flags=self._api.FLAG_OVERLAP_PRECEDING)
+        return self._api.gemm(W, X, N)
+
+    def _lm_local(self, W, X):
+        return self.matmul(W, X, W.shape[0])
+
+    def _lm_local_t(self, W, X):
+        return self.matmul(W, X, W.shape[0]).t()
+
+    def _allreduce(self, t):
+        if self.world > 1:
+            self.torch.distributed.all_reduce(t, group=self.group)
+        return t
+
+    def _rmsnorm(self, x, w):
+        return x * self.torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.eps) * w
+
+    def _rope(self, x, pos):
+        """x [T][H][hd] at positions pos [T] (rotate-half form)."""
+        half = self.cfg.head_dim // 2
+        c = self.cos[pos][:, None, :]
+        s = self.sin[pos][:, None, :]
+        x1, x2 = x[..., :half], x[..., half:]
+        return self.torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+    def _attention(self, q, l, pos, T):
+        """q [T][hq][hd] for the T tokens at positions pos, against the f16 KV cache of layer l (keys up
+        to each token's own position), in fp32."""
+        torch = self.torch
+        cfg = self.cfg
+        g = self.hq // self.hkv
+        K = self.cache[l, 0].float()            # [hkv][max_seq][hd]
+        V = self.cache[l, 1].float()
+        qg = q.view(T, self.hkv, g, cfg.head_dim).permute(1, 2, 0, 3)          # [hkv][g][T][hd]
+        sc = torch.matmul(qg, K.transpose(1, 2)[:, None]) / math.sqrt(cfg.head_dim)  # [hkv][g][T][S]
+        keys = torch.arange(cfg.max_seq, device=q.device)
+        mask = keys[None, :] > pos[:, None]                                   # [T][S]
+        sc = sc.masked_fill(mask[None, None], float("-inf"))
+        p = torch.softmax(sc, dim=-1)
+        o = torch.matmul(p, V[:, None])                                       # [hkv][g][T][hd]
+        return o.permute(2, 0, 1, 3).reshape(T, self.hq * cfg.head_dim)
+
+    def forward(self, x, pos):
+        """x [T][hidden] fp32 embeddings of the tokens at positions pos [T]; updates the KV cache and
+        returns the final-norm hidden states [T][hidden]."""
+        torch = self.torch
+        cfg = self.cfg
+        T = x.shape[0]
+        hd = cfg.head_dim
+        for l, L in enumerate(self.layers):
+            h = self._rmsnorm(x, L["an"])
+            qkv = self.matmul(L["wqkv"], h, self.nqkv)
+            q = qkv[:, :self.hq * hd].view(T, self.hq, hd)
+            k = qkv[:, self.hq * hd:(self.hq + self.hkv) * hd].view(T, self.hkv, hd)
+            v = qkv[:, (self.hq + self.hkv) * hd:].view(T, self.hkv, hd)
+            q = self._rope(q, pos)
+            k = self._rope(k, pos)
+            self.cache[l, 0].index_copy_(1, pos, k.transpose(0, 1).to(torch.float16))
+            self.cache[l, 1].index_copy_(1, pos, v.transpose(0, 1).to(torch.float16))
+            a = self._attention(q, l, pos, T)
+            o = self._allreduce(self.matmul(L["wo"], a.contiguous(), cfg.hidden))
+            x = x + o
+            h2 = self._rmsnorm(x, L["fn"])
+            gu = self.matmul(L["wgu"], h2, 2 * self.F)
+            act = torch.nn.functional.silu(gu[:, :self.F]) * gu[:, self.F:]
+            d = self._allreduce(self.matmul(L["wd"], act.contiguous(), cfg.hidden))
+            x = x + d
+        return self._rmsnorm(x, self.final_norm)
+
+    def logits(self, h):
+        """h [T][hidden] -> logits [T][vocab] (row-sharded lm_head + all-gather); the result may be a
+        view of the lm_head's output buffer, valid until its next call."""
+        if h.shape[0] <= 8:
+            return self.lm_head.gemv(h.contiguous())
+        return self.lm_head.gemm_nm(h.contiguous()).t()
+
+    # ------------------------------------------------------------------ generation
+    def prefill(self, tokens):
+        """Run the prompt (token ids [T] on the device); returns the greedy next token [1]."""
+        torch = self.torch
+        T = tokens.shape[0]
+        pos = torch.arange(T, device=self.device)
+        h = self.forward(self.emb[tokens].float(), pos)
+        lg = self.logits(h[-1:]).clone()  # the sharded lm_head reuses its output buffer
+        self._pos = torch.full((1,), T, dtype=torch.long, device=self.device)
+        self._tok = torch.argmax(lg, dim=-1).to(torch.long)
+        return self._tok.clone(), lg
+
+    def _step(self):
+        torch = self.torch
+        h = self.forward(self.emb[self._tok].float(), self._pos)
+        lg = self.logits(h)
+        self._last_logits = lg.clone()
+        self._tok.copy_(torch.argmax(lg, dim=-1))
+        self._pos.add_(1)
+        return self._tok
+
+    def decode(self, steps: int, use_graph: bool = True) -> List[int]:
+        """Greedy decode `steps` tokens after prefill(); returns the generated token ids."""
+        torch = self.torch
+        out = torch.empty(steps, dtype=torch.long, device=self.device)
+        if steps <= 0:
+            return []
+        out[0:1].copy_(self._step())          # eager step: allocates the per-shape buffers
+        if not use_graph or steps == 1:
+            for i in range(1, steps):
+                out[i:i + 1].copy_(self._step())
+            return out.tolist()
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            out[1:2].copy_(self._step())      # second eager step on the capture stream
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._step()
+            for i in range(2, steps):
+                g.replay()
+                out[i:i + 1].copy_(self._tok)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.graph = g
+        return out.tolist()
+
+    def release(self):
+        """Drop the captured graph (before destroying the process group)."""
+        self.graph = None

@@ -1,0 +1,82 @@
+"""The tensor-parallel decoder's host logic on CPU ranks (gloo): a tiny config at TP=2 against TP=1.
+
+Matmuls are the FP64 oracle of the quantised pipeline (injected), weights are quantised by the C
+oracle; the test covers the head / FFN partition, the K-slicing of the row-parallel layers, the
+all-reduces, the KV cache and RoPE/attention indexing, and the sharded lm_head."""
+import os
+import socket
+
+import numpy as np
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def tiny_cfg(dec):
+    return dec.DecoderConfig(layers=2, hidden=512, heads=8, kv_heads=2, head_dim=128, ffn=1024, vocab=1000,
+                             max_seq=40)
+
+
+def _worker(rank, world, port, q):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root))
+    sys.path.insert(0, str(root / "tests"))
+    import torch.distributed as dist
+    from conftest import load_pkg
+    from oracle import oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        dec = load_pkg().decoder
+
+        def matmul(W, X, N):
+            Xn = np.ascontiguousarray(X.numpy(), dtype=np.float32)
+            K = Xn.shape[1]
+            Y, _ = O.matmul_q8(W.numpy(), O.quantize_q8_1(Xn), K, N, Xn.shape[0])
+            return torch.from_numpy(Y.astype(np.float32))
+
+        def gen_weights(N, K, s):
+            return torch.from_numpy(O.quantize_iq4_xs(O.normal(N * K, s, 0.0, 0.02).reshape(N, K)))
+
+        def gen_normal(n, s, mean, std):
+            return torch.from_numpy(O.normal(n, s, mean, std))
+
+        m = dec.TPDecoder(tiny_cfg(dec), rank=rank, world=world, seed=3, device="cpu", matmul=matmul,
+                          gen_weights=gen_weights, gen_normal=gen_normal)
+        prompt = torch.from_numpy(np.random.default_rng(7).integers(0, 1000, 12)).long()
+        first, lg = m.prefill(prompt)
+        toks = [int(first)] + m.decode(6, use_graph=False)
+        q.put((rank, toks, lg.numpy(), m._last_logits.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return sorted((q.get(timeout=5) for _ in range(world)), key=lambda r: r[0])
+
+
+def test_tp2_matches_tp1():
+    one = _run(1)[0]
+    two = _run(2)
+    for rank, toks, lg, last in two:
+        # the all-reduce adds the two halves of o_proj / down_proj in another order: tiny differences
+        assert np.max(np.abs(lg - one[2])) <= 1e-3 * np.max(np.abs(one[2]))
+        assert toks[:4] == one[1][:4], (toks, one[1])
+    assert two[0][1] == two[1][1]      # both ranks hold the same tokens
