@@ -4,22 +4,25 @@
 // the int32 dot of one 32-weight sub-block with one Q8_1 block is exact, then
 // term = (d_w*(ls-32)) * d_x * sumi in fp32, summed over sub-blocks.
 //
-//  * The weight matrix is viewed as a 3-D tensor of uint64 [N rows][K/512 super-block pairs][34]
-//    (one pair = 272 bytes) and staged by TMA (cp.async.bulk.tensor.3d, no multicast) in units of
-//    16 rows x `pk` pairs.  pk is odd, so the shared-memory row pitch pk*272 bytes = 68*pk words is an
+//  * The weight matrix is viewed as a 2-D tensor of uint64 [N rows][34 * K/512] (one super-block
+//    pair = 272 bytes) and staged by TMA (cp.async.bulk.tensor.2d, no multicast) in units of
+//    16 rows x `pk` pairs (one box: 16 rows of pk*272 bytes).  pk is odd, so the shared-memory row pitch pk*272 bytes = 68*pk words is an
 //    odd multiple of 4 words: the 8 rows of an MMA fragment load hit 8 disjoint 4-bank groups.
 //    Rows and pairs past the matrix are zero-filled by TMA and never read from memory.
 //  * Work unit = (16-row tile, K part of pk pairs), ordered part-major and split in balanced
-//    contiguous ranges over one CTA per SM.  With more than one part, a tile's parts leave partial
-//    sums in the workspace and the last CTA to finish the tile (global ticket) adds them in part
-//    order: deterministic.
-//  * Warp w of 8 consumer warps handles sub-block ib = w of every super-block of the part.  Lane
-//    (g = lane/4, c = lane%4) holds A = qs word c of sub-block ib for rows g and g+8, expanded by
-//    the split codebook lookup (prmt tables -kv[0..7] and kv[8..15], zero elsewhere) into two A
-//    fragments H (codes >= 8) and L (codes < 8); B = the 8 tokens' Q8_1 values of the sub-block in
-//    the lookup's k order (staged once per part in shared memory); sumi = MMA(H,B) - MMA(L,B).
-//  * The 8 warps' partial tiles are combined in shared memory by the last warp to finish the
-//    unit (shared-memory ticket), again in warp order.
+//    contiguous ranges over one CTA per SM.  With more than one part, the parts leave partial sums in
+//    the workspace (plain stores) and a small follow-on kernel adds them in part order
+//    (deterministic); a fence + ticket per unit to combine in-kernel cost ~11 us on a 95 MB matrix.
+//  * A unit is processed by a pair of consumer warps (8 pairs per CTA, units it = pair, pair+8, ...
+//    over a stage ring sized to shared memory); the two warps split the unit's super-blocks (even /
+//    odd) and add their partial sums through the stage buffer once both are done reading it (half 0
+//    + half 1, a fixed order).  Lane (g = lane/4, c = lane%4) holds A = qs word c of each sub-block
+//    for rows g and g+8, expanded by the split codebook lookup (prmt tables -kv[0..7] and kv[8..15],
+//    zero elsewhere) into two A fragments H (codes >= 8) and L (codes < 8); B = the 8 tokens' Q8_1
+//    values of the sub-block in the lookup's k order (staged once per part in shared memory);
+//    sumi = MMA(H,B) - MMA(L,B).  The weight scales d*(ls-32) of a super-block are computed once by
+//    the four lanes of a row group and fetched by shuffle; the fp32 update (d_w*(ls-32)*d_x)*sumi is
+//    one packed multiply and one packed fused add per two outputs.
 //  * Every mbarrier wait is bounded (sleeping try_wait, error word, drain before exit).
 #include <cuda.h>
 
@@ -30,23 +33,29 @@ namespace iq4xs {
 
 namespace {
 constexpr int kMaxMmaStages = 16;  // stage ring depth: as many as fit, at least one per consumer warp
-constexpr int kNCW = 8;            // consumer warps
+constexpr int kPairs = 8;          // consumer warp pairs: one unit (tile x part) per pair at a time
+constexpr int kNCW = 2 * kPairs;   // consumer warps; the two warps of a pair split the unit's super-blocks
 
 struct MmaSmem {
     uint32_t bar_off, flag_off, act_off, dx_off, ring_off, total;
 };
 
 // act: per staged part (up to 2) and sub-block: 32 lanes x uint2 (B fragment words) = 256 B;
-// dx: 8 fp32 per sub-block; ring: `stages` x (16 rows x pk pairs x 272 B).
+// dx: per sub-block and token pair c: {d_x[2c], d_x[2c+1], sum q[2c], sum q[2c+1]} (64 B);
+// ring: `stages` x (16 rows x pk pairs x 272 B).
 __host__ __device__ inline MmaSmem mma_smem(int pk, int stages) {
     MmaSmem L;
     L.bar_off = 0;
     L.flag_off = 2 * kMaxMmaStages * 8;
     L.act_off = 384;
     L.dx_off = L.act_off + 2u * (uint32_t)pk * 16 * 256;
-    L.ring_off = (L.dx_off + 2u * (uint32_t)pk * 16 * 32 + 127) & ~127u;
+    L.ring_off = (L.dx_off + 2u * (uint32_t)pk * 16 * 64 + 127) & ~127u;
     L.total = L.ring_off + (uint32_t)stages * 16u * (uint32_t)pk * 272u;
     return L;
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Fused multiply-add on fp32 pairs: (d0, d1) += (a0, a1) * (b0, b1), one instruction on sm_100.
@@ -64,13 +73,21 @@ __device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, f
         : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar,
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
                                             uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar)), "l"(policy)
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
+}
+
+// A unsigned 8-bit (the biased codebook byte kv + 128), B signed 8-bit (the Q8_1 quants).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -140,7 +157,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                 const int p = (int)(u / T);
                 const int64_t t = u - (int64_t)p * T;
                 mbar_arrive_expect_tx(&full[s], stage_bytes);
-                tma_load_3d(ring + (size_t)s * stage_bytes, &tmap, 0, p * pk, (int)(t * 16), &full[s], policy);
+                tma_load_2d(ring + (size_t)s * stage_bytes, &tmap, p * pk * 34, (int)(t * 16), &full[s], policy);
             }
             const int first = it > S ? it - S : 0;
             for (int j = first; j < it; ++j) {
@@ -174,6 +191,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
             const int sbl = e >> 3, n = e & 7;
             uint2 frag[4] = {make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u)};
             float dxv = 0.0f;
+            int qsum = 0;
             if (n < B) {
                 const uint32_t* q = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb_base + sbl) * kQ8Bytes);
                 uint32_t w[9];
@@ -182,18 +200,25 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) frag[j] = make_uint2(act_perm_lo(w[1 + j], w[5 + j]), act_perm_hi(w[1 + j], w[5 + j]));
                 dxv = f16_bits_to_f32(w[0]);
+#pragma unroll
+                for (int j = 1; j < 9; ++j) qsum = __dp4a((int)w[j], 0x01010101, qsum);  // sum of the 32 int8 q
             }
             uint2* dst = reinterpret_cast<uint2*>(smem + L.act_off) + (slot * pk * 16 + sbl) * 32 + n * 4;
 #pragma unroll
             for (int j = 0; j < 4; ++j) dst[j] = frag[j];
-            reinterpret_cast<float*>(smem + L.dx_off)[(slot * pk * 16 + sbl) * 8 + n] = dxv;
+            float* dq = reinterpret_cast<float*>(smem + L.dx_off) + (slot * pk * 16 + sbl) * 16 + (n >> 1) * 4 + (n & 1);
+            dq[0] = dxv;
+            dq[2] = __int_as_float(qsum);
         }
     }
-    named_barrier(1, nct);
+    named_barrier(kPairs + 1, nct);
     grid_launch_dependents();  // the workspace activations are no longer read
 
-    // Warp cw owns units it = cw, cw + 8, ... of this CTA: all 16 rows x all sub-blocks of the part.
-    for (int it = cw; it < nunits; it += kNCW) {
+    // Pair pr = cw/2 owns units it = pr, pr + 8, ... of this CTA (16 rows x the part's sub-blocks);
+    // warp half hf = cw%2 of the pair takes super-blocks hf, hf+2, ... and the two partial sums are
+    // added through the unit's stage buffer once both warps are done reading it.
+    const int pr = cw >> 1, hf = cw & 1;
+    for (int it = pr; it < nunits; it += kPairs) {
         const int s = it % S;
         const int64_t u = u0 + it;
         const int p = (int)(u / T);
@@ -207,8 +232,8 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
             const uint8_t* rg = ring + (size_t)s * stage_bytes + (size_t)g * row_pitch;
             const uint8_t* rg8 = rg + 8 * row_pitch;
             const uint2* actp = act + (size_t)slot * pk * 16 * 32 + lane;
-            const float* dxp = dxs + (size_t)slot * pk * 16 * 8 + 2 * c;
-            for (int j = 0; j < nsup; ++j) {
+            const float* dxp = dxs + (size_t)slot * pk * 16 * 16 + 4 * c;
+            for (int j = hf; j < nsup; j += 2) {
                 const uint8_t* b0p = rg + j * kBlockBytes;
                 const uint8_t* b8p = rg8 + j * kBlockBytes;
                 const uint2 h0 = *reinterpret_cast<const uint2*>(b0p);
@@ -233,18 +258,23 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                     const uint32_t x0 = *reinterpret_cast<const uint32_t*>(b0p + 8 + 16 * ib + 4 * c);
                     const uint32_t x8 = *reinterpret_cast<const uint32_t*>(b8p + 8 + 16 * ib + 4 * c);
                     const uint2 bf = actp[sbl * 32];
-                    const float2 dx = *reinterpret_cast<const float2*>(dxp + sbl * 8);
+                    const float4 dq = *reinterpret_cast<const float4*>(dxp + sbl * 16);
                     const uint32_t xf0 = x0 ^ 0x88888888u, xf8 = x8 ^ 0x88888888u;
-                    const uint32_t ah[4] = {prmt(a.lut[2], a.lut[3], xf0), prmt(a.lut[2], a.lut[3], xf8),
-                                            prmt(a.lut[2], a.lut[3], hi16(xf0)), prmt(a.lut[2], a.lut[3], hi16(xf8))};
-                    const uint32_t al[4] = {prmt(a.lut[0], a.lut[1], x0), prmt(a.lut[0], a.lut[1], x8),
-                                            prmt(a.lut[0], a.lut[1], hi16(x0)), prmt(a.lut[0], a.lut[1], hi16(x8))};
-                    int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
-                    mma_s8(dh, ah, bf.x, bf.y);
-                    mma_s8(dl, al, bf.x, bf.y);
+                    // Biased codebook bytes kv + 128 = 128 - (-kv) (codes < 8) or 128 + kv (codes >= 8):
+                    // one unsigned MMA, then sumi = MMA - 128 * sum(q) of the token's block.
+                    const uint32_t hl0 = prmt(a.lut[2], a.lut[3], xf0), ll0 = prmt(a.lut[0], a.lut[1], x0);
+                    const uint32_t hl8 = prmt(a.lut[2], a.lut[3], xf8), ll8 = prmt(a.lut[0], a.lut[1], x8);
+                    const uint32_t hh0 = prmt(a.lut[2], a.lut[3], hi16(xf0)), lh0 = prmt(a.lut[0], a.lut[1], hi16(x0));
+                    const uint32_t hh8 = prmt(a.lut[2], a.lut[3], hi16(xf8)), lh8 = prmt(a.lut[0], a.lut[1], hi16(x8));
+                    const uint32_t ab[4] = {0x80808080u - ll0 + hl0, 0x80808080u - ll8 + hl8, 0x80808080u - lh0 + hh0,
+                                            0x80808080u - lh8 + hh8};
+                    int dd[4] = {0, 0, 0, 0};
+                    mma_u8s8(dd, ab, bf.x, bf.y);
                     const float f0 = __shfl_sync(0xFFFFFFFFu, fq0[ib & 1], 4 * g + (ib >> 1));
                     const float f8 = __shfl_sync(0xFFFFFFFFu, fq8[ib & 1], 4 * g + (ib >> 1));
-                    const int s0 = dh[0] - dl[0], s1 = dh[1] - dl[1], s2 = dh[2] - dl[2], s3 = dh[3] - dl[3];
+                    const int qs0 = __float_as_int(dq.z), qs1 = __float_as_int(dq.w);
+                    const int s0 = dd[0] - 128 * qs0, s1 = dd[1] - 128 * qs1, s2 = dd[2] - 128 * qs0, s3 = dd[3] - 128 * qs1;
+                    const float2 dx = make_float2(dq.x, dq.y);
                     if constexpr (kDebug) {
                         const int64_t r0w = t * 16 + g, r8w = r0w + 8;
                         const int sbg = p * pk * 16 + sbl;
@@ -262,7 +292,23 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                 }
             }
         }
-        // The stage can be refilled as soon as this warp is done reading it.
+        // Both warps of the pair are done with the weights: half 1 parks its sums in the stage buffer,
+        // half 0 adds them (fixed order: half 0 + half 1) and releases the stage.
+        float* park = reinterpret_cast<float*>(ring + (size_t)s * stage_bytes) + 4 * lane;
+        named_barrier(1 + pr, 64);
+        if (hf == 1) {
+            park[0] = acc[0];
+            park[1] = acc[1];
+            park[2] = acc[2];
+            park[3] = acc[3];
+            fence_proxy_async_shared();  // generic writes before the stage's next TMA fill
+        }
+        named_barrier(1 + pr, 64);
+        if (hf == 1) continue;
+        acc[0] += park[0];
+        acc[1] += park[1];
+        acc[2] += park[2];
+        acc[3] += park[3];
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
 
@@ -275,29 +321,26 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                 for (int k = 0; k < 4; ++k)
                     if (tk[k] < B && rw[k] < a.N) a.y[(int64_t)tk[k] * a.N + rw[k]] = acc[k];
             } else {
-                // Partial sums of this part; the last of the P units of the tile adds them in part order.
+                // Partial sums of this part, plain stores; reduce_parts_kernel adds the parts in order.
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
                     if (tk[k] < B && rw[k] < a.N) a.partial[((int64_t)p * B + tk[k]) * a.N + rw[k]] = acc[k];
-                __threadfence();
-                __syncwarp();
-                uint32_t told = 0;
-                if (lane == 0) told = atomicAdd(&a.tile_cnt[t], 1u);
-                told = __shfl_sync(0xFFFFFFFFu, told, 0);
-                if (told == (uint32_t)P - 1) {
-                    __threadfence();
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        if (tk[k] < B && rw[k] < a.N) {
-                            float sum = 0.0f;
-                            for (int q = 0; q < P; ++q) sum += __ldcg(a.partial + ((int64_t)q * B + tk[k]) * a.N + rw[k]);
-                            a.y[(int64_t)tk[k] * a.N + rw[k]] = sum;
-                        }
-                    }
-                    if (lane == 0) a.tile_cnt[t] = 0u;
-                }
             }
         }
+    }
+}
+
+// y[b][n] = sum over parts p (in part order) of partial[p][b][n].  Launched after the GEMV with
+// programmatic serialization: griddepcontrol.wait returns once the GEMV grid has finished and its
+// stores are visible, so the GEMV needs no fences or tickets of its own.
+__global__ void __launch_bounds__(256) reduce_parts_kernel(const float* __restrict__ partial, float* __restrict__ y,
+                                                          int P, int64_t BN) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < BN; i += (int64_t)gridDim.x * blockDim.x) {
+        float sum = 0.0f;
+        for (int q = 0; q < P; ++q) sum += partial[(int64_t)q * BN + i];
+        y[i] = sum;
     }
 }
 
@@ -323,12 +366,12 @@ EncodeTiledFn encode_fn() {
 // Stage ring depth for part size pk: as many 16-row stages as fit next to the activations (<= 16).
 int mma_stages(int pk, int smem_optin) {
     int st = kMaxMmaStages;
-    while (st > kNCW && (int)mma_smem(pk, st).total > smem_optin) --st;
+    while (st > kPairs && (int)mma_smem(pk, st).total > smem_optin) --st;
     return st;
 }
 
 // Part size: odd number of pairs pk <= 5 (odd: conflict-free fragment loads).  A unit runs on one
-// warp: cost of the busiest warp = units per warp x (pk + overhead); the overhead of a unit (stage
+// warp pair: cost of the busiest pair = units per pair x (pk + overhead); the overhead of a unit (stage
 // latency, stores, ticket) is 0.75 pairs with one stage per warp and 0.35 once the ring holds at
 // least 1.5 stages per warp (the next unit's copy overlaps the current one).
 int choose_pk(int pairs, int64_t tiles, int ctas, int smem_optin) {
@@ -338,7 +381,7 @@ int choose_pk(int pairs, int64_t tiles, int ctas, int smem_optin) {
     for (int pk = 5; pk >= 1; pk -= 2) {
         const int parts = (pairs + pk - 1) / pk;
         const int64_t U = tiles * parts;
-        const int64_t per = (U + (int64_t)ctas * kNCW - 1) / ((int64_t)ctas * kNCW);
+        const int64_t per = (U + (int64_t)ctas * kPairs - 1) / ((int64_t)ctas * kPairs);
         const double ovh = mma_stages(pk, smem_optin) >= 12 ? 0.35 : 0.75;
         const double cost = (double)per * ((double)pk + ovh) + (parts > 1 ? 0.25 : 0.0);
         if (cost < best_cost - 1e-9) {
@@ -402,12 +445,14 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     const MmaSmem L = mma_smem(pk, stages);
     if ((int)L.total > smem_optin) return cudaErrorInvalidConfiguration;
 
+    // 2-D view uint64 [N][34*pairs]; a unit is one box of 16 rows x pk pairs (pk*272 bytes per row,
+    // 16 TMA rows per copy), landing as [16][pk*272] in shared memory.
     CUtensorMap map;
-    const cuuint64_t dims[3] = {34, (cuuint64_t)pairs, (cuuint64_t)N};
-    const cuuint64_t strides[2] = {272, (cuuint64_t)pairs * 272};
-    const cuuint32_t box[3] = {34, (cuuint32_t)pk, 16};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(W), dims, strides, box, estr,
+    const cuuint64_t dims[2] = {(cuuint64_t)pairs * 34, (cuuint64_t)N};
+    const cuuint64_t strides[1] = {(cuuint64_t)pairs * 272};
+    const cuuint32_t box[2] = {(cuuint32_t)(34 * pk), 16};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(W), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
@@ -431,16 +476,31 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     int64_t grid64 = std::min<int64_t>(sms, U);
     while ((U + grid64 - 1) / grid64 > T) ++grid64;
     const int grid = (int)grid64;
+    cudaError_t e = cudaErrorInvalidValue;
     switch (B) {
 #define IQ4XS_MMA_B(BB)                                                                         \
     case BB:                                                                                    \
-        return sumi ? launch_mma_b<BB, true>(map, a, (int)L.total, stream, pdl, grid)          \
-                    : launch_mma_b<BB, false>(map, a, (int)L.total, stream, pdl, grid);
+        e = sumi ? launch_mma_b<BB, true>(map, a, (int)L.total, stream, pdl, grid)             \
+                 : launch_mma_b<BB, false>(map, a, (int)L.total, stream, pdl, grid);            \
+        break;
         IQ4XS_MMA_B(1) IQ4XS_MMA_B(2) IQ4XS_MMA_B(3) IQ4XS_MMA_B(4)
         IQ4XS_MMA_B(5) IQ4XS_MMA_B(6) IQ4XS_MMA_B(7) IQ4XS_MMA_B(8)
 #undef IQ4XS_MMA_B
         default: return cudaErrorInvalidValue;
     }
+    if (e != cudaSuccess || parts == 1 || !y) return e;
+    // Sum the parts: a small follow-on kernel chained by programmatic dependent launch.
+    const int64_t BN = (int64_t)B * N;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min<int64_t>((BN + 255) / 256, (int64_t)sms * 4));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, reduce_parts_kernel, (const float*)partials, y, parts, BN);
 }
 
 }  // namespace iq4xs
