@@ -76,6 +76,27 @@ def hbm_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def graph_kernel_nodes(g) -> int:
+    """Kernel nodes in a captured torch CUDA graph (driver API: cuGraphGetNodes / cuGraphNodeGetType)."""
+    try:
+        drv = C.CDLL("libcuda.so.1")
+        graph = C.c_void_p(g.raw_cuda_graph())
+    except Exception:
+        return -1
+    n = C.c_size_t(0)
+    if drv.cuGraphGetNodes(graph, None, C.byref(n)) != 0 or n.value == 0:
+        return -1
+    nodes = (C.c_void_p * n.value)()
+    if drv.cuGraphGetNodes(graph, nodes, C.byref(n)) != 0:
+        return -1
+    kind = C.c_int(-1)
+    count = 0
+    for i in range(n.value):
+        if drv.cuGraphNodeGetType(C.c_void_p(nodes[i]), C.byref(kind)) == 0 and kind.value == 0:  # kernel
+            count += 1
+    return count
+
+
 def bf16_peak():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -385,6 +406,9 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=256, help="rows per shape in the CPU samples")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="default: same as --steps")
+    ap.add_argument("--extras", default="all", choices=["all", "none"],
+                    help="side measurements after the headline (prefill GEMM sweep, row-sharded matmuls, decoder); "
+                         "'none' leaves the headline, e2e, roofline and CPU baseline unchanged")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -431,15 +455,21 @@ def main():
         step(1, stream)
         stream.synchronize()
         for c in range(2):
-            g = torch.cuda.CUDAGraph()
+            g = torch.cuda.CUDAGraph(keep_graph=True)  # keep the cudaGraph_t: its kernel nodes are counted
             with torch.cuda.graph(g, stream=stream):
                 step(c, stream)
+            g.instantiate()
             graphs.append(g)
     torch.cuda.synchronize()
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
+
+    # kernels of one step: quantiser + GEMV (+ part reduction) per GEMV call, counted in the graph
+    launches_per_step = graph_kernel_nodes(graphs[0])
+    if launches_per_step <= 0:
+        launches_per_step = len(SHAPES) * len(BATCHES) * 2
 
     # ---- warmup
     with torch.cuda.stream(stream):
@@ -540,17 +570,17 @@ def main():
     h2d = sum(4 * B * K for B in BATCHES for _, _, K in SHAPES)
     d2h = sum(4 * B * N for B in BATCHES for _, N, _ in SHAPES)
 
-    # ---- prefill GEMM sweep (reported beside the headline)
-    gemm_per, gemm_tops = gemm_sweep(P, weights, dev, stream)
+    gemm_per, gemm_tops, sharded, decoder = [], None, [], None
     bpeak, bpeak_kind = bf16_peak()
-
-    # ---- row-sharded lm_head / gate|up across the ranks (strong scaling, output all-gather)
-    sharded = sharded_sweep(P, dev, stream, rank, world, barrier)
-
-    # ---- synthetic decoder, tensor-parallel over the ranks
-    del weights
-    torch.cuda.empty_cache()
-    decoder = decoder_run(P, dev, rank, world, barrier)
+    if args.extras == "all":
+        # ---- prefill GEMM sweep (reported beside the headline)
+        gemm_per, gemm_tops = gemm_sweep(P, weights, dev, stream)
+        # ---- row-sharded lm_head / gate|up across the ranks (strong scaling, output all-gather)
+        sharded = sharded_sweep(P, dev, stream, rank, world, barrier)
+        # ---- synthetic decoder, tensor-parallel over the ranks
+        del weights
+        torch.cuda.empty_cache()
+        decoder = decoder_run(P, dev, rank, world, barrier)
 
     torch.cuda.synchronize()
     err = P.device_error()
@@ -595,16 +625,18 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "custom_gemv_iq4xs_dispatch_batched from a C++ host loop, pinned host x/y"},
-            "gemm": {"metric": "IQ4_XS prefill GEMM TOPS (2*M*N*K / time, Q8_1 quantisation included)",
-                     "value": round(gemm_tops, 1), "unit": "TOPS", "tokens": GEMM_TOKENS,
-                     "roofline": {"bound": "tensor", "achieved": round(gemm_tops, 1), "peak": bpeak,
-                                  "unit": "TFLOP/s", "frac": round(gemm_tops / bpeak, 4), "peak_kind": bpeak_kind,
-                                  "kernel": "gemm_iq4xs_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators)"},
-                     "per_shape": gemm_per},
+            "gemm": None if gemm_tops is None else {
+                "metric": "IQ4_XS prefill GEMM TOPS (2*M*N*K / time, Q8_1 quantisation included)",
+                "value": round(gemm_tops, 1), "unit": "TOPS", "tokens": GEMM_TOKENS,
+                "roofline": {"bound": "tensor", "achieved": round(gemm_tops, 1), "peak": bpeak,
+                             "unit": "TFLOP/s", "frac": round(gemm_tops / bpeak, 4), "peak_kind": bpeak_kind,
+                             "kernel": "gemm_iq4xs_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators)"},
+                "per_shape": gemm_per},
             "decoder": decoder,
             "sharded": {"what": "row-sharded over the ranks (strong scaling), NCCL all-gather of the outputs, "
                                 "time = max over ranks", "results": sharded},
-            "gpu_launches": args.steps * len(SHAPES) * len(BATCHES) * 2,
+            "gpu_launches": args.steps * launches_per_step,
+            "gpu_launches_per_step": launches_per_step,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

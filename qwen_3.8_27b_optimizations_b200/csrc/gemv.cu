@@ -379,8 +379,13 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     a.kw = kw;
     a.rows_per_stage = R;
     const int64_t stage_bytes = (int64_t)R * a.rb;
+    // At most ~110 KB of stages (two of them always): deeper rings did not stream faster, and a CTA
+    // that leaves half the shared memory free lets the next kernel's CTA start on the same SM.
+    constexpr int64_t kRowSmemTarget = 110000;
     int stages = kMaxStages;
-    while (stages > 2 && (int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes).total > smem_optin) --stages;
+    while (stages > 2 && ((int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes).total > smem_optin ||
+                          (int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes).total > kRowSmemTarget))
+        --stages;
     a.stages = stages;
     const RowSmem L = gemv_row_smem(B, R, kw, stages, stage_bytes);
     if ((int64_t)L.total > smem_optin || stage_bytes >= (1 << 20)) return cudaErrorInvalidConfiguration;

@@ -13,16 +13,17 @@
 //    contiguous ranges over one CTA per SM.  With more than one part, the parts leave partial sums in
 //    the workspace (plain stores) and a small follow-on kernel adds them in part order
 //    (deterministic); a fence + ticket per unit to combine in-kernel cost ~11 us on a 95 MB matrix.
+//  * Lookup: the two split-table prmt lookups (tables -kv[0..7] and kv[8..15], zero elsewhere) merge
+//    into the signed codebook byte by one IADD3 (to kv+128) and one XOR (to kv): one s8 x s8 MMA
+//    per sub-block and 16 rows.
 //  * A unit is processed by a pair of consumer warps (8 pairs per CTA, units it = pair, pair+8, ...
 //    over a stage ring sized to shared memory); the two warps split the unit's super-blocks (even /
 //    odd) and add their partial sums through the stage buffer once both are done reading it (half 0
 //    + half 1, a fixed order).  Lane (g = lane/4, c = lane%4) holds A = qs word c of each sub-block
-//    for rows g and g+8, expanded by the split codebook lookup (prmt tables -kv[0..7] and kv[8..15],
-//    zero elsewhere) into two A fragments H (codes >= 8) and L (codes < 8); B = the 8 tokens' Q8_1
-//    values of the sub-block in the lookup's k order (staged once per part in shared memory);
-//    sumi = MMA(H,B) - MMA(L,B).  The weight scales d*(ls-32) of a super-block are computed once by
-//    the four lanes of a row group and fetched by shuffle; the fp32 update (d_w*(ls-32)*d_x)*sumi is
-//    one packed multiply and one packed fused add per two outputs.
+//    for rows g and g+8 (looked up as above); B = the 8 tokens' Q8_1 values of the sub-block in the
+//    lookup's k order (staged once per part in shared memory).  The weight scales d*(ls-32) of a
+//    super-block are computed once by the four lanes of a row group and fetched by shuffle; the fp32
+//    update (d_w*(ls-32)*d_x)*sumi is one packed multiply and one packed fused add per two outputs.
 //  * Every mbarrier wait is bounded (sleeping try_wait, error word, drain before exit).
 #include <cuda.h>
 
@@ -41,7 +42,7 @@ struct MmaSmem {
 };
 
 // act: per staged part (up to 2) and sub-block: 32 lanes x uint2 (B fragment words) = 256 B;
-// dx: per sub-block and token pair c: {d_x[2c], d_x[2c+1], sum q[2c], sum q[2c+1]} (64 B);
+// dx: per sub-block, d_x of the 8 tokens (32 B);
 // ring: `stages` x (16 rows x pk pairs x 272 B).
 __host__ __device__ inline MmaSmem mma_smem(int pk, int stages) {
     MmaSmem L;
@@ -49,7 +50,7 @@ __host__ __device__ inline MmaSmem mma_smem(int pk, int stages) {
     L.flag_off = 2 * kMaxMmaStages * 8;
     L.act_off = 384;
     L.dx_off = L.act_off + 2u * (uint32_t)pk * 16 * 256;
-    L.ring_off = (L.dx_off + 2u * (uint32_t)pk * 16 * 64 + 127) & ~127u;
+    L.ring_off = (L.dx_off + 2u * (uint32_t)pk * 16 * 32 + 127) & ~127u;
     L.total = L.ring_off + (uint32_t)stages * 16u * (uint32_t)pk * 272u;
     return L;
 }
@@ -80,14 +81,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
-}
-
-// A unsigned 8-bit (the biased codebook byte kv + 128), B signed 8-bit (the Q8_1 quants).
-__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -191,7 +184,6 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
             const int sbl = e >> 3, n = e & 7;
             uint2 frag[4] = {make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u)};
             float dxv = 0.0f;
-            int qsum = 0;
             if (n < B) {
                 const uint32_t* q = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb_base + sbl) * kQ8Bytes);
                 uint32_t w[9];
@@ -200,15 +192,11 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) frag[j] = make_uint2(act_perm_lo(w[1 + j], w[5 + j]), act_perm_hi(w[1 + j], w[5 + j]));
                 dxv = f16_bits_to_f32(w[0]);
-#pragma unroll
-                for (int j = 1; j < 9; ++j) qsum = __dp4a((int)w[j], 0x01010101, qsum);  // sum of the 32 int8 q
             }
             uint2* dst = reinterpret_cast<uint2*>(smem + L.act_off) + (slot * pk * 16 + sbl) * 32 + n * 4;
 #pragma unroll
             for (int j = 0; j < 4; ++j) dst[j] = frag[j];
-            float* dq = reinterpret_cast<float*>(smem + L.dx_off) + (slot * pk * 16 + sbl) * 16 + (n >> 1) * 4 + (n & 1);
-            dq[0] = dxv;
-            dq[2] = __int_as_float(qsum);
+            reinterpret_cast<float*>(smem + L.dx_off)[(slot * pk * 16 + sbl) * 8 + n] = dxv;
         }
     }
     named_barrier(kPairs + 1, nct);
@@ -232,7 +220,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
             const uint8_t* rg = ring + (size_t)s * stage_bytes + (size_t)g * row_pitch;
             const uint8_t* rg8 = rg + 8 * row_pitch;
             const uint2* actp = act + (size_t)slot * pk * 16 * 32 + lane;
-            const float* dxp = dxs + (size_t)slot * pk * 16 * 16 + 4 * c;
+            const float* dxp = dxs + (size_t)slot * pk * 16 * 8 + 2 * c;
             for (int j = hf; j < nsup; j += 2) {
                 const uint8_t* b0p = rg + j * kBlockBytes;
                 const uint8_t* b8p = rg8 + j * kBlockBytes;
@@ -258,23 +246,21 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                     const uint32_t x0 = *reinterpret_cast<const uint32_t*>(b0p + 8 + 16 * ib + 4 * c);
                     const uint32_t x8 = *reinterpret_cast<const uint32_t*>(b8p + 8 + 16 * ib + 4 * c);
                     const uint2 bf = actp[sbl * 32];
-                    const float4 dq = *reinterpret_cast<const float4*>(dxp + sbl * 16);
+                    const float2 dx = *reinterpret_cast<const float2*>(dxp + sbl * 8);
                     const uint32_t xf0 = x0 ^ 0x88888888u, xf8 = x8 ^ 0x88888888u;
-                    // Biased codebook bytes kv + 128 = 128 - (-kv) (codes < 8) or 128 + kv (codes >= 8):
-                    // one unsigned MMA, then sumi = MMA - 128 * sum(q) of the token's block.
+                    // Codebook bytes: biased kv + 128 = 128 - (-kv) (codes < 8) or 128 + kv (codes >= 8) by one
+                    // IADD3, back to signed kv by flipping the top bit: one s8 x s8 MMA gives sumi.
                     const uint32_t hl0 = prmt(a.lut[2], a.lut[3], xf0), ll0 = prmt(a.lut[0], a.lut[1], x0);
                     const uint32_t hl8 = prmt(a.lut[2], a.lut[3], xf8), ll8 = prmt(a.lut[0], a.lut[1], x8);
                     const uint32_t hh0 = prmt(a.lut[2], a.lut[3], hi16(xf0)), lh0 = prmt(a.lut[0], a.lut[1], hi16(x0));
                     const uint32_t hh8 = prmt(a.lut[2], a.lut[3], hi16(xf8)), lh8 = prmt(a.lut[0], a.lut[1], hi16(x8));
-                    const uint32_t ab[4] = {0x80808080u - ll0 + hl0, 0x80808080u - ll8 + hl8, 0x80808080u - lh0 + hh0,
-                                            0x80808080u - lh8 + hh8};
+                    const uint32_t ab[4] = {(0x80808080u - ll0 + hl0) ^ 0x80808080u, (0x80808080u - ll8 + hl8) ^ 0x80808080u,
+                                            (0x80808080u - lh0 + hh0) ^ 0x80808080u, (0x80808080u - lh8 + hh8) ^ 0x80808080u};
                     int dd[4] = {0, 0, 0, 0};
-                    mma_u8s8(dd, ab, bf.x, bf.y);
+                    mma_s8(dd, ab, bf.x, bf.y);
                     const float f0 = __shfl_sync(0xFFFFFFFFu, fq0[ib & 1], 4 * g + (ib >> 1));
                     const float f8 = __shfl_sync(0xFFFFFFFFu, fq8[ib & 1], 4 * g + (ib >> 1));
-                    const int qs0 = __float_as_int(dq.z), qs1 = __float_as_int(dq.w);
-                    const int s0 = dd[0] - 128 * qs0, s1 = dd[1] - 128 * qs1, s2 = dd[2] - 128 * qs0, s3 = dd[3] - 128 * qs1;
-                    const float2 dx = make_float2(dq.x, dq.y);
+                    const int s0 = dd[0], s1 = dd[1], s2 = dd[2], s3 = dd[3];
                     if constexpr (kDebug) {
                         const int64_t r0w = t * 16 + g, r8w = r0w + 8;
                         const int sbg = p * pk * 16 + sbl;
@@ -364,9 +350,11 @@ EncodeTiledFn encode_fn() {
 }
 
 // Stage ring depth for part size pk: as many 16-row stages as fit next to the activations (<= 16).
+// (4 KB of the per-block limit stay free: tools that instrument kernels reserve some of it.)
 int mma_stages(int pk, int smem_optin) {
+    const int budget = smem_optin - 4096;
     int st = kMaxMmaStages;
-    while (st > kPairs && (int)mma_smem(pk, st).total > smem_optin) --st;
+    while (st > kPairs && (int)mma_smem(pk, st).total > budget) --st;
     return st;
 }
 
