@@ -98,6 +98,14 @@ size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t N, int64_t B);
                                           the stream: the quantizer is launched as a programmatic
                                           dependent (it still waits for X) and the GEMV's prologue and
                                           weight prefetch overlap the preceding kernel's tail */
+/* iq4xs_gemv_q8 with flags (iq4xs_gemv_q8 == flags 0).  IQ4XS_FLAG_OVERLAP_PRECEDING: the GEMV is
+ * launched as a programmatic dependent of the preceding kernel (the producer of q8, which must not
+ * write W); its weight stream starts before that kernel ends and it waits for q8 before reading it.
+ * The library's own q8 producers (the decoder-step operations of iq4xs_decoder.h) are written for
+ * this.  No counterpart in the reference, whose prequantized GEMV takes no flags. */
+int iq4xs_gemv_q8_ex(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B,
+                     void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream);
+
 /* iq4xs_gemv_f32 with flags (iq4xs_gemv_f32 == flags 0). */
 int iq4xs_gemv_f32_ex(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B,
                       void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream);

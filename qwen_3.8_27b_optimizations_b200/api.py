@@ -34,6 +34,7 @@ SIGNATURES = {
     "iq4xs_q8_1_bytes": (_sz, [_i64, _i64]),
     "iq4xs_gemv_q8": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "iq4xs_gemv_q8_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "iq4xs_gemv_q8_ex": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
     "iq4xs_gemv_f32": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "iq4xs_gemv_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "iq4xs_gemv_f32_ex": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
@@ -64,6 +65,14 @@ BENCH_SIGNATURES = {
     "iq4xs_bench_e2e_gemv": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i, _vp, C.POINTER(C.c_float)]),
 }
 
+# include/iq4xs_decoder.h (the decoder-step operations around the GEMVs)
+DECODER_SIGNATURES = {
+    "iq4xs_dec_residual_rmsnorm_q8": (_i, [_vp, _vp, _vp, _i64, _i64, _f, _vp, _vp, C.c_uint, _vp]),
+    "iq4xs_dec_attention_decode_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp,
+                                           C.c_uint, _vp]),
+    "iq4xs_dec_swiglu_q8": (_i, [_vp, _i64, _i64, _vp, C.c_uint, _vp]),
+}
+
 _lib = None
 
 
@@ -81,7 +90,7 @@ def lib():
         if not LIB_PATH.exists():
             raise ImportError(f"{LIB_PATH} is missing; build it with __graft_entry__.build()")
         L = C.CDLL(str(LIB_PATH))
-        for name, (res, args) in {**SIGNATURES, **BENCH_SIGNATURES}.items():
+        for name, (res, args) in {**SIGNATURES, **BENCH_SIGNATURES, **DECODER_SIGNATURES}.items():
             fn = getattr(L, name)
             fn.restype = res
             fn.argtypes = args
@@ -162,6 +171,17 @@ def gemv_q8(W, q8, K: int, N: int, B: int, out=None, stream=None, generic: bool 
     ws = workspace if workspace is not None else _workspace(gemv_q8_workspace_bytes(K, N, B), W.device)
     _check("iq4xs_gemv_q8", lib().iq4xs_gemv_q8(_ptr(W), _ptr(q8), _ptr(Y), K, N, B, _ptr(ws),
                                                 ws.numel() * ws.element_size(), _stream(stream)))
+    return Y
+
+
+def gemv_q8_ex(W, q8, K: int, N: int, B: int, out=None, stream=None, flags: int = 0, workspace=None):
+    """gemv_q8 with flags: FLAG_OVERLAP_PRECEDING launches the GEMV as a programmatic dependent of
+    the kernel before it (the producer of q8, which must not write W)."""
+    torch = _torch()
+    Y = out if out is not None else torch.empty((B, N), dtype=torch.float32, device=W.device)
+    ws = workspace if workspace is not None else _workspace(gemv_q8_workspace_bytes(K, N, B), W.device)
+    _check("iq4xs_gemv_q8_ex", lib().iq4xs_gemv_q8_ex(_ptr(W), _ptr(q8), _ptr(Y), K, N, B, _ptr(ws),
+                                                      ws.numel() * ws.element_size(), flags, _stream(stream)))
     return Y
 
 
@@ -327,3 +347,50 @@ def custom_gemm_iq4xs_can_handle(K: int, N: int, M: int, type_: int = GGML_TYPE_
 
 def custom_gemm_iq4xs_dispatch(W, X, Y, K: int, N: int, M: int, stream=None) -> int:
     return int(lib().custom_gemm_iq4xs_dispatch(_ptr(W), _ptr(X), _ptr(Y), K, N, M, _stream(stream)))
+
+
+# ----------------------------------------------------------------------------- decoder step (iq4xs_decoder.h)
+FLAG_PDL = 1
+
+
+def _q8_out(rows: int, D: int, device, out):
+    torch = _torch()
+    if out is not None:
+        return out
+    return torch.empty((rows, D // QK8_1 * Q8_1_BYTES), dtype=torch.uint8, device=device)
+
+
+def dec_residual_rmsnorm_q8(x, w, eps: float, delta=None, q8=None, h_out=None, want_q8: bool = True,
+                            flags: int = 0, stream=None):
+    """x [T][D] fp32 (updated in place to x + delta when delta is given); returns (q8, h_out):
+    Q8_1 blocks [T][D/32*36] of rmsnorm(x) * w (when want_q8 or q8 is given) and the fp32 values
+    (when h_out is given)."""
+    T, D = x.shape
+    if want_q8 or q8 is not None:
+        q8 = _q8_out(T, D, x.device, q8)
+    _check("iq4xs_dec_residual_rmsnorm_q8", lib().iq4xs_dec_residual_rmsnorm_q8(
+        _ptr(x), _ptr(delta) if delta is not None else None, _ptr(w), D, T, eps,
+        _ptr(q8) if q8 is not None else None, _ptr(h_out) if h_out is not None else None, flags, _stream(stream)))
+    return q8, h_out
+
+
+def dec_attention_decode_q8(qkv, k_cache, v_cache, cos, sin, pos, q_heads: int, kv_heads: int, q8=None,
+                            o_out=None, flags: int = 0, stream=None):
+    """One decode token: qkv fp32 [(q_heads + 2 kv_heads) * 128], caches f16 [kv_heads][max_seq][128],
+    cos/sin fp32 [max_seq][64], pos int64 [1] on the device.  Returns Q8_1 blocks [1][q_heads*128/32*36]
+    of the attention output (and fills o_out fp32 [q_heads*128] when given)."""
+    hd = k_cache.shape[-1]
+    max_seq = k_cache.shape[-2]
+    q8 = _q8_out(1, q_heads * hd, qkv.device, q8)
+    _check("iq4xs_dec_attention_decode_q8", lib().iq4xs_dec_attention_decode_q8(
+        _ptr(qkv), _ptr(k_cache), _ptr(v_cache), _ptr(cos), _ptr(sin), _ptr(pos), q_heads, kv_heads, hd, max_seq,
+        _ptr(q8), _ptr(o_out) if o_out is not None else None, flags, _stream(stream)))
+    return q8
+
+
+def dec_swiglu_q8(gu, F: int, q8=None, flags: int = 0, stream=None):
+    """gu [T][2F] fp32 -> Q8_1 blocks [T][F/32*36] of silu(gate) * up."""
+    T = gu.shape[0]
+    q8 = _q8_out(T, F, gu.device, q8)
+    _check("iq4xs_dec_swiglu_q8", lib().iq4xs_dec_swiglu_q8(_ptr(gu), F, T, _ptr(q8), flags, _stream(stream)))
+    return q8

@@ -11,6 +11,7 @@
 #include <utility>
 
 #include "../../include/iq4xs.h"
+#include "../../include/iq4xs_decoder.h"
 #include "iq4xs_device.cuh"
 #include "iq4xs_kernels.h"
 
@@ -210,6 +211,19 @@ int iq4xs_gemv_q8(const void* W, const void* q8, float* Y, int64_t K, int64_t N,
     return status_from(launch_gemv_q8(a, (int)B, stream, false));
 }
 
+int iq4xs_gemv_q8_ex(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B, void* workspace,
+                     size_t workspace_bytes, unsigned flags, cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if ((s = check_batch(B))) return s;
+    if (!q8 || !Y || !workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < iq4xs_gemv_q8_workspace_bytes(K, N, B)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned(q8, 4) || !aligned(Y, 4) || !aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
+    GemvArgs a = make_gemv_args(W, q8, Y, K, N);
+    attach_workspace(a, workspace, 0, K, N, B);
+    return status_from(launch_gemv_q8(a, (int)B, stream, (flags & IQ4XS_FLAG_OVERLAP_PRECEDING) != 0));
+}
+
 int iq4xs_gemv_q8_generic(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B,
                           cudaStream_t stream) {
     int s = check_matrix(W, K, N);
@@ -401,6 +415,44 @@ cudaError_t gemm_iq4xs_stock_dp4a_gpu(const void* W, const float* X, float* Y, i
 cudaError_t gemm_iq4xs_wmma_stream_gpu(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
                                        cudaStream_t stream) {
     return gemm_internal_ws(W, X, Y, K, N, M, 1, M, 1, M, stream);
+}
+
+// ------------------------------------------------------------------------------ decoder step
+int iq4xs_dec_residual_rmsnorm_q8(float* x, const float* delta, const float* w, int64_t D, int64_t T, float eps,
+                                  void* q8, float* h_out, unsigned flags, cudaStream_t stream) {
+    if (!x || !w || (!q8 && !h_out) || D <= 0 || T <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (D % kQK8 != 0 || D > 8192 || T > 65535) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(x, 4) || !aligned(w, 4) || (delta && !aligned(delta, 4)) || (q8 && !aligned(q8, 4)) ||
+        (h_out && !aligned(h_out, 4)))
+        return IQ4XS_ERR_MISALIGNED;
+    return status_from(launch_residual_rmsnorm_q8(x, delta, w, (int)D, (int)T, eps, static_cast<uint8_t*>(q8), h_out,
+                                                  stream, (flags & IQ4XS_FLAG_PDL) != 0));
+}
+
+int iq4xs_dec_attention_decode_q8(const float* qkv, void* k_cache, void* v_cache, const float* cos_table,
+                                  const float* sin_table, const int64_t* pos, int64_t q_heads, int64_t kv_heads,
+                                  int64_t head_dim, int64_t max_seq, void* q8, float* o_out, unsigned flags,
+                                  cudaStream_t stream) {
+    if (!qkv || !k_cache || !v_cache || !cos_table || !sin_table || !pos || !q8) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (q_heads <= 0 || kv_heads <= 0 || max_seq <= 0 || head_dim <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (head_dim != 128 || q_heads % kv_heads != 0 || q_heads > 65535 || max_seq > 8192)
+        return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(qkv, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(cos_table, 4) ||
+        !aligned(sin_table, 4) || !aligned(pos, 8) || !aligned(q8, 4) || (o_out && !aligned(o_out, 4)))
+        return IQ4XS_ERR_MISALIGNED;
+    uint32_t* err = device_error_word();
+    if (!err) return IQ4XS_ERR_CUDA;
+    return status_from(launch_attention_decode_q8(qkv, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache),
+                                                  cos_table, sin_table, pos, (int)q_heads, (int)kv_heads,
+                                                  (int)max_seq, static_cast<uint8_t*>(q8), o_out, err, stream,
+                                                  (flags & IQ4XS_FLAG_PDL) != 0));
+}
+
+int iq4xs_dec_swiglu_q8(const float* gu, int64_t F, int64_t T, void* q8, unsigned flags, cudaStream_t stream) {
+    if (!gu || !q8 || F <= 0 || T <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (F % kQK8 != 0) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(gu, 4) || !aligned(q8, 4)) return IQ4XS_ERR_MISALIGNED;
+    return status_from(launch_swiglu_q8(gu, F, T, static_cast<uint8_t*>(q8), stream, (flags & IQ4XS_FLAG_PDL) != 0));
 }
 
 }  // extern "C"

@@ -31,6 +31,7 @@ enum DeviceError : uint32_t {
     kDevErrEmptyWait = 2,   // producer waited too long for a free stage
     kDevErrDrainWait = 3,   // copies still in flight after an error
     kDevErrMmaWait = 4,     // tensor-core pipeline barrier timed out
+    kDevErrPosition = 5,    // decode attention: the device-side position is outside the KV cache
 };
 
 // Spin limit for every mbarrier wait (each try_wait already suspends for a while in hardware);
@@ -59,6 +60,30 @@ __device__ __forceinline__ uint16_t f32_to_f16_trunc(float v) {
 
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t h16) {
     return __half2float(__ushort_as_half((unsigned short)(h16 & 0xFFFFu)));
+}
+
+// One Q8_1 block (kernels/matmul_iq4xs/real_stock_dp4a_comparator.hip:230-264): lane i of a full
+// warp holds x_i; amax and sum by a 16..1 xor butterfly, d = amax/127, q = (int8)roundf(x/d)
+// (0 when amax == 0), ds = {trunc_fp16(d), trunc_fp16(sum)}; the 36 bytes at `out` (4-byte aligned)
+// are written as nine 4-byte stores.  Every Q8_1 producer in the library goes through this.
+__device__ __forceinline__ void q8_1_block_store(float x, uint8_t* out, int lane) {
+    const unsigned full = 0xFFFFFFFFu;
+    float amax = fabsf(x), sum = x;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(full, amax, off));
+        sum += __shfl_xor_sync(full, sum, off);
+    }
+    const float d = amax / 127.0f;
+    int q = 0;
+    if (amax != 0.0f) q = (int)roundf(x / d);
+    const uint32_t b0 = (uint32_t)q & 0xFFu;
+    const uint32_t b1 = __shfl_down_sync(full, b0, 1);
+    const uint32_t b2 = __shfl_down_sync(full, b0, 2);
+    const uint32_t b3 = __shfl_down_sync(full, b0, 3);
+    if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(out + 4 + lane) = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    if (lane == 0)
+        *reinterpret_cast<uint32_t*>(out) = (uint32_t)f32_to_f16_trunc(d) | ((uint32_t)f32_to_f16_trunc(sum) << 16);
 }
 
 // ------------------------------------------------------------------------------ byte permute

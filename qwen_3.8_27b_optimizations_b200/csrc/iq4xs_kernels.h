@@ -1,6 +1,7 @@
 // iq4xs_kernels.h -- internal launch interface between the C-ABI layer (capi.cu) and the kernels.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -89,5 +90,13 @@ cudaError_t launch_quantize_iq4_xs(const float* src, uint8_t* dst, int64_t nrows
 cudaError_t launch_dequantize(const uint8_t* W, float* out, int64_t K, int64_t N, cudaStream_t stream);
 
 uint32_t* device_error_word();  // per-device error word (current device)
+
+// Decoder step operations (decode_ops.cu).
+cudaError_t launch_residual_rmsnorm_q8(float* x, const float* delta, const float* w, int D, int T, float eps,
+                                       uint8_t* q8, float* h_out, cudaStream_t stream, bool pdl);
+cudaError_t launch_attention_decode_q8(const float* qkv, __half* kc, __half* vc, const float* cosb,
+                                       const float* sinb, const int64_t* pos, int hq, int hkv, int max_seq,
+                                       uint8_t* q8, float* o_out, uint32_t* err, cudaStream_t stream, bool pdl);
+cudaError_t launch_swiglu_q8(const float* gu, int64_t F, int64_t T, uint8_t* q8, cudaStream_t stream, bool pdl);
 
 }  // namespace iq4xs

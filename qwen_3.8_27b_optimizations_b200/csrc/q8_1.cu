@@ -17,7 +17,6 @@ __global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restr
                                                             int64_t stride_k, int signal_dependents) {
     if (signal_dependents) grid_launch_dependents();
     grid_dependency_wait();  // X may be the output of the preceding kernel (no-op without PDL)
-    const unsigned full = 0xFFFFFFFFu;
     const int lane = threadIdx.x & 31;
     const int64_t nb = K / kQK8;
     const int64_t total = nb * M;
@@ -26,23 +25,7 @@ __global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restr
         const int64_t m = blk / nb;
         const int64_t ib = blk - m * nb;
         const float x = X[m * stride_m + (ib * kQK8 + lane) * stride_k];
-        float amax = fabsf(x), sum = x;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(full, amax, off));
-            sum += __shfl_xor_sync(full, sum, off);
-        }
-        const float d = amax / 127.0f;
-        int q = 0;
-        if (amax != 0.0f) q = (int)roundf(x / d);
-        const uint32_t b0 = (uint32_t)q & 0xFFu;
-        const uint32_t b1 = __shfl_down_sync(full, b0, 1);
-        const uint32_t b2 = __shfl_down_sync(full, b0, 2);
-        const uint32_t b3 = __shfl_down_sync(full, b0, 3);
-        uint8_t* out = q8 + blk * kQ8Bytes;
-        if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(out + 4 + lane) = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-        if (lane == 0)
-            *reinterpret_cast<uint32_t*>(out) = (uint32_t)f32_to_f16_trunc(d) | ((uint32_t)f32_to_f16_trunc(sum) << 16);
+        q8_1_block_store(x, q8 + blk * kQ8Bytes, lane);
     }
 }
 

@@ -16,7 +16,11 @@ The weights are generated identically on every rank from per-matrix seeds and sl
 does not depend on P.
 
 The decode step (one token) is captured in a CUDA graph and replayed, the position and the token
-living in device tensors, so generating N tokens issues no host work per token.
+living in device tensors, so generating N tokens issues no host work per token.  With the CUDA
+kernels, a decode layer is four Q8_1-input GEMVs and three fused kernels (include/iq4xs_decoder.h):
+residual+RMSNorm->Q8_1, RoPE+KV-append+attention->Q8_1, SwiGLU->Q8_1; each GEMV is launched as a
+programmatic dependent of the kernel before it, so its weight stream overlaps that kernel.  The
+prompt (prefill) runs the same model with torch ops around the tensor-core GEMM.
 """
 from __future__ import annotations
 
@@ -53,7 +57,7 @@ class TPDecoder:
 
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, group=None, seed: int = 0,
                  device="cuda", matmul: Optional[Callable] = None, gen_weights: Optional[Callable] = None,
-                 gen_normal: Optional[Callable] = None):
+                 gen_normal: Optional[Callable] = None, fused_decode: Optional[bool] = None):
         import torch
         from . import sharded
         self.torch = torch
@@ -68,6 +72,11 @@ class TPDecoder:
             from . import api
             self._api = api
         self.matmul = matmul or self._cuda_matmul
+        # fused decode layers need the CUDA kernels for every op
+        self.fused_decode = (matmul is None) if fused_decode is None else fused_decode
+        if self.fused_decode and (matmul is not None or self._api is None):
+            raise ValueError("fused decode runs on the CUDA kernels only")
+        self._dec = None
         self.gen_weights = gen_weights or (lambda N, K, s: self._api.random_weights(N, K, seed=s, std=cfg.std))
         self.gen_normal = gen_normal or (lambda n, s, mean, std: self._api.fill_normal(n, s, mean, std))
 
@@ -117,6 +126,7 @@ class TPDecoder:
         self.cos = torch.cos(ang).to(torch.float32).to(self.device)   # [max_seq][hd/2]
         self.sin = torch.sin(ang).to(torch.float32).to(self.device)
         self.graph = None
+        self._pos = self._tok = None
 
     # ------------------------------------------------------------------ building blocks
     def _cuda_matmul(self, W, X, N):
@@ -190,6 +200,46 @@ class TPDecoder:
             x = x + d
         return self._rmsnorm(x, self.final_norm)
 
+    def _decode_buffers(self):
+        if self._dec is None:
+            torch, cfg = self.torch, self.cfg
+            dev = self.device
+            D = cfg.hidden
+            q8 = lambda K: torch.empty((1, K // 32 * 36), dtype=torch.uint8, device=dev)
+            self._dec = dict(x=torch.empty((1, D), dtype=torch.float32, device=dev),
+                             h=torch.empty((1, D), dtype=torch.float32, device=dev),
+                             q8d=q8(D), q8a=q8(self.hq * cfg.head_dim), q8f=q8(self.F),
+                             qkv=torch.empty((1, self.nqkv), dtype=torch.float32, device=dev),
+                             o=torch.empty((1, D), dtype=torch.float32, device=dev),
+                             gu=torch.empty((1, 2 * self.F), dtype=torch.float32, device=dev),
+                             d=torch.empty((1, D), dtype=torch.float32, device=dev))
+        return self._dec
+
+    def forward_decode(self, x):
+        """One token through the fused decode layers: x [1][hidden] fp32 embedding at position
+        self._pos; returns the final-norm hidden state [1][hidden] (a reused buffer)."""
+        api, cfg = self._api, self.cfg
+        b = self._decode_buffers()
+        D, hd = cfg.hidden, cfg.head_dim
+        OV, PDL = api.FLAG_OVERLAP_PRECEDING, api.FLAG_PDL
+        xs = b["x"]
+        xs.copy_(x)
+        delta = None
+        for l, L in enumerate(self.layers):
+            api.dec_residual_rmsnorm_q8(xs, L["an"], cfg.eps, delta=delta, q8=b["q8d"], flags=PDL)
+            api.gemv_q8_ex(L["wqkv"], b["q8d"], D, self.nqkv, 1, out=b["qkv"], flags=OV)
+            api.dec_attention_decode_q8(b["qkv"], self.cache[l, 0], self.cache[l, 1], self.cos, self.sin, self._pos,
+                                        self.hq, self.hkv, q8=b["q8a"], flags=PDL)
+            self._allreduce(api.gemv_q8_ex(L["wo"], b["q8a"], self.hq * hd, D, 1, out=b["o"], flags=OV))
+            api.dec_residual_rmsnorm_q8(xs, L["fn"], cfg.eps, delta=b["o"], q8=b["q8d"], flags=PDL)
+            api.gemv_q8_ex(L["wgu"], b["q8d"], D, 2 * self.F, 1, out=b["gu"], flags=OV)
+            api.dec_swiglu_q8(b["gu"], self.F, q8=b["q8f"], flags=PDL)
+            self._allreduce(api.gemv_q8_ex(L["wd"], b["q8f"], self.F, D, 1, out=b["d"], flags=OV))
+            delta = b["d"]
+        api.dec_residual_rmsnorm_q8(xs, self.final_norm, cfg.eps, delta=delta, h_out=b["h"], want_q8=False,
+                                    flags=PDL)
+        return b["h"]
+
     def logits(self, h):
         """h [T][hidden] -> logits [T][vocab] (row-sharded lm_head + all-gather); the result may be a
         view of the lm_head's output buffer, valid until its next call."""
@@ -205,13 +255,17 @@ class TPDecoder:
         pos = torch.arange(T, device=self.device)
         h = self.forward(self.emb[tokens].float(), pos)
         lg = self.logits(h[-1:]).clone()  # the sharded lm_head reuses its output buffer
-        self._pos = torch.full((1,), T, dtype=torch.long, device=self.device)
-        self._tok = torch.argmax(lg, dim=-1).to(torch.long)
+        if self._pos is None:  # the decode graph reads these two tensors: keep them, refill them
+            self._pos = torch.empty((1,), dtype=torch.long, device=self.device)
+            self._tok = torch.empty((1,), dtype=torch.long, device=self.device)
+        self._pos.fill_(T)
+        self._tok.copy_(torch.argmax(lg, dim=-1))
         return self._tok.clone(), lg
 
     def _step(self):
         torch = self.torch
-        h = self.forward(self.emb[self._tok].float(), self._pos)
+        x = self.emb[self._tok].float()
+        h = self.forward_decode(x) if self.fused_decode else self.forward(x, self._pos)
         lg = self.logits(h)
         self._last_logits = lg.clone()
         self._tok.copy_(torch.argmax(lg, dim=-1))
@@ -219,28 +273,35 @@ class TPDecoder:
         return self._tok
 
     def decode(self, steps: int, use_graph: bool = True) -> List[int]:
-        """Greedy decode `steps` tokens after prefill(); returns the generated token ids."""
+        """Greedy decode `steps` tokens after prefill(); returns the generated token ids.  With
+        use_graph the step is captured once (the first call runs two eager steps, then captures) and
+        every later token, in this and later calls, is one graph replay."""
         torch = self.torch
         out = torch.empty(steps, dtype=torch.long, device=self.device)
         if steps <= 0:
             return []
-        out[0:1].copy_(self._step())          # eager step: allocates the per-shape buffers
-        if not use_graph or steps == 1:
-            for i in range(1, steps):
+        i = 0
+        if not use_graph:
+            for i in range(steps):
                 out[i:i + 1].copy_(self._step())
             return out.tolist()
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            out[1:2].copy_(self._step())      # second eager step on the capture stream
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=s):
-                self._step()
-            for i in range(2, steps):
-                g.replay()
-                out[i:i + 1].copy_(self._tok)
+            if self.graph is None:
+                out[0:1].copy_(self._step())      # eager: allocates the per-shape buffers
+                i = 1
+                if i < steps:
+                    out[1:2].copy_(self._step())  # second eager step on the capture stream
+                    i = 2
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=s):
+                        self._step()
+                    self.graph = g
+            for j in range(i, steps):
+                self.graph.replay()
+                out[j:j + 1].copy_(self._tok)
         torch.cuda.current_stream(self.device).wait_stream(s)
-        self.graph = g
         return out.tolist()
 
     def release(self):

@@ -9,6 +9,7 @@ from conftest import ROOT
 
 HEADER = ROOT / "include" / "iq4xs.h"
 BENCH_HEADER = ROOT / "include" / "iq4xs_bench.h"
+DECODER_HEADER = ROOT / "include" / "iq4xs_decoder.h"
 
 
 def declared_functions(header=HEADER):
@@ -33,12 +34,41 @@ def test_every_declared_symbol_is_exported(pkg):
 def test_python_signatures_cover_header(pkg):
     assert set(pkg.SIGNATURES) == set(declared_functions())
     assert set(pkg.api.BENCH_SIGNATURES) == set(declared_functions(BENCH_HEADER))
+    assert set(pkg.api.DECODER_SIGNATURES) == set(declared_functions(DECODER_HEADER))
+
+
+def test_every_header_is_covered():
+    assert sorted(p.name for p in (ROOT / "include").glob("*.h")) == sorted(
+        p.name for p in (HEADER, BENCH_HEADER, DECODER_HEADER))
 
 
 def test_bench_header_symbols_exported(pkg):
     L = pkg.lib()
-    for name in declared_functions(BENCH_HEADER):
+    for name in declared_functions(BENCH_HEADER) + declared_functions(DECODER_HEADER):
         assert hasattr(L, name), name
+
+
+def test_decoder_op_validation(pkg):
+    L = pkg.lib()
+    # rmsnorm: D % 32, D > 8192, neither output, misaligned x
+    assert L.iq4xs_dec_residual_rmsnorm_q8(FAKE, None, FAKE, 100, 1, 1e-6, FAKE, None, 0, None) == 2
+    assert L.iq4xs_dec_residual_rmsnorm_q8(FAKE, None, FAKE, 8224, 1, 1e-6, FAKE, None, 0, None) == 2
+    assert L.iq4xs_dec_residual_rmsnorm_q8(FAKE, None, FAKE, 5120, 1, 1e-6, None, None, 0, None) == 1
+    assert L.iq4xs_dec_residual_rmsnorm_q8(FAKE + 2, None, FAKE, 5120, 1, 1e-6, FAKE, None, 0, None) == 3
+    # attention: head_dim, GQA divisibility, max_seq, cache alignment, null pos
+    args = (FAKE, FAKE, FAKE, FAKE, FAKE, FAKE)
+    assert L.iq4xs_dec_attention_decode_q8(*args, 64, 8, 64, 640, FAKE, None, 0, None) == 2
+    assert L.iq4xs_dec_attention_decode_q8(*args, 60, 8, 128, 640, FAKE, None, 0, None) == 2
+    assert L.iq4xs_dec_attention_decode_q8(*args, 64, 8, 128, 9000, FAKE, None, 0, None) == 2
+    assert L.iq4xs_dec_attention_decode_q8(FAKE, FAKE + 8, FAKE, FAKE, FAKE, FAKE, 64, 8, 128, 640, FAKE, None, 0,
+                                           None) == 3
+    assert L.iq4xs_dec_attention_decode_q8(FAKE, FAKE, FAKE, FAKE, FAKE, None, 64, 8, 128, 640, FAKE, None, 0,
+                                           None) == 1
+    # swiglu: F % 32
+    assert L.iq4xs_dec_swiglu_q8(FAKE, 100, 1, FAKE, 0, None) == 2
+    assert L.iq4xs_dec_swiglu_q8(None, 128, 1, FAKE, 0, None) == 1
+    # gemv_q8_ex shares gemv_q8's checks
+    assert L.iq4xs_gemv_q8_ex(FAKE, FAKE, FAKE, 500, 64, 1, FAKE, 1 << 30, 1, None) == 2
 
 
 def test_status_strings(pkg):

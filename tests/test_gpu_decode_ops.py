@@ -1,0 +1,121 @@
+"""The fused decoder-step operations (include/iq4xs_decoder.h) against the decoder's torch
+formulation of the same ops in fp32, and their Q8_1 output against the library's quantizer applied
+to their own fp32 values (bit-exact: both go through the same block routine)."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _gen(seed):
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
+def test_residual_rmsnorm_q8(pkg):
+    T, D, eps = 3, 5120, 1e-6
+    g = _gen(1)
+    x = torch.randn((T, D), generator=g, device="cuda")
+    delta = torch.randn((T, D), generator=g, device="cuda") * 0.5
+    w = 1.0 + 0.02 * torch.randn(D, generator=g, device="cuda")
+    x_ref = x + delta
+    h_ref = x_ref * torch.rsqrt(x_ref.pow(2).mean(-1, keepdim=True) + eps) * w
+    h = torch.empty_like(x)
+    q8, _ = pkg.api.dec_residual_rmsnorm_q8(x, w, eps, delta=delta, h_out=h)
+    torch.cuda.synchronize()
+    assert torch.equal(x, x_ref)  # the residual add is a single rounded add, as in torch
+    assert torch.allclose(h, h_ref, rtol=2e-6, atol=1e-6)
+    assert torch.equal(q8, pkg.q8_1_quantize(h))
+    # no residual, q8 only (the first layer), and h only (the final norm)
+    x2 = torch.randn((1, D), generator=g, device="cuda")
+    q8b, _ = pkg.api.dec_residual_rmsnorm_q8(x2, w, eps)
+    hb = torch.empty_like(x2)
+    pkg.api.dec_residual_rmsnorm_q8(x2, w, eps, h_out=hb, want_q8=False)
+    torch.cuda.synchronize()
+    assert torch.equal(q8b, pkg.q8_1_quantize(hb))
+
+
+def _rope_ref(x, c, s):
+    half = x.shape[-1] // 2
+    x1, x2 = x[..., :half], x[..., half:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+@pytest.mark.parametrize("hq,hkv,p", [(64, 8, 0), (64, 8, 1), (64, 8, 300), (32, 4, 639), (8, 1, 77), (8, 8, 5)])
+def test_attention_decode_q8(pkg, hq, hkv, p):
+    hd, max_seq = 128, 640
+    g = _gen(100 + p + hq)
+    qkv = torch.randn((1, (hq + 2 * hkv) * hd), generator=g, device="cuda")
+    kc = torch.randn((hkv, max_seq, hd), generator=g, device="cuda").half()
+    vc = torch.randn((hkv, max_seq, hd), generator=g, device="cuda").half()
+    kc0, vc0 = kc.clone(), vc.clone()
+    inv = 1.0 / (1.0e6 ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
+    ang = torch.arange(max_seq, dtype=torch.float64)[:, None] * inv[None, :]
+    cos = torch.cos(ang).float().cuda()
+    sin = torch.sin(ang).float().cuda()
+    pos = torch.tensor([p], dtype=torch.long, device="cuda")
+    o = torch.empty((hq * hd,), dtype=torch.float32, device="cuda")
+    q8 = pkg.api.dec_attention_decode_q8(qkv, kc, vc, cos, sin, pos, hq, hkv, o_out=o)
+    torch.cuda.synchronize()
+
+    # torch formulation (the decoder's forward for one token)
+    c, s = cos[p][None, :], sin[p][None, :]
+    q = _rope_ref(qkv[0, :hq * hd].view(hq, hd), c, s)
+    k = _rope_ref(qkv[0, hq * hd:(hq + hkv) * hd].view(hkv, hd), c, s)
+    v = qkv[0, (hq + hkv) * hd:].view(hkv, hd)
+    kc0[:, p] = k.half()
+    vc0[:, p] = v.half()
+    assert torch.equal(kc, kc0) and torch.equal(vc, vc0)  # appended at p, nothing else touched
+    gq = hq // hkv
+    K = kc0[:, :p + 1].float()
+    V = vc0[:, :p + 1].float()
+    qg = q.view(hkv, gq, hd)
+    sc = torch.matmul(qg.double(), K.double().transpose(1, 2)) / math.sqrt(hd)
+    ref = torch.matmul(torch.softmax(sc, dim=-1), V.double()).reshape(hq * hd)
+    err = (o.double() - ref).abs()
+    assert err.max().item() <= 2e-5 * max(1.0, ref.abs().max().item())
+    assert torch.equal(q8[0], pkg.q8_1_quantize(o)[0])
+    assert pkg.device_error() == 0
+
+
+def test_attention_position_out_of_range_is_an_error(pkg):
+    """The kernel's own bounds check: a position at max_seq records device error 5 and writes nothing."""
+    hq, hkv, hd, max_seq = 8, 2, 128, 16
+    qkv = torch.randn((1, (hq + 2 * hkv) * hd), device="cuda")
+    kc = torch.zeros((hkv, max_seq, hd), device="cuda").half()
+    vc = torch.zeros_like(kc)
+    cs = torch.zeros((max_seq, hd // 2), device="cuda")
+    pos = torch.tensor([max_seq], dtype=torch.long, device="cuda")
+    q8 = torch.zeros((1, hq * hd // 32 * 36), dtype=torch.uint8, device="cuda")
+    pkg.api.dec_attention_decode_q8(qkv, kc, vc, cs, cs, pos, hq, hkv, q8=q8)
+    torch.cuda.synchronize()
+    assert pkg.device_error() == 5
+    assert int(kc.abs().sum()) == 0 and int(q8.sum()) == 0
+    assert pkg.device_error() == 0  # read-and-clear
+
+
+def test_swiglu_q8(pkg):
+    T, F = 2, 17408
+    g = _gen(9)
+    gu = torch.randn((T, 2 * F), generator=g, device="cuda") * 3
+    q8 = pkg.api.dec_swiglu_q8(gu, F)
+    act = torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
+    ref = pkg.q8_1_quantize(act)
+    torch.cuda.synchronize()
+    # same op order as torch's silu (x / (1 + exp(-x))) and mul; allow rare last-bit differences of exp
+    diff = (q8 != ref).sum().item()
+    assert diff <= q8.numel() // 10000, diff
+    deq = lambda b: b.view(T, F // 32, 36)[..., 4:].view(torch.int8).float()
+    assert (deq(q8) - deq(ref)).abs().max().item() <= 1
+
+
+def test_gemv_q8_ex_matches_gemv_q8(pkg):
+    N, K, B = 4096, 5120, 1
+    W = pkg.api.random_weights(N, K, seed=3)
+    x = torch.randn((B, K), device="cuda")
+    q8 = pkg.q8_1_quantize(x)
+    y0 = pkg.api.gemv_q8(W, q8, K, N, B)
+    y1 = pkg.api.gemv_q8_ex(W, q8, K, N, B, flags=pkg.api.FLAG_OVERLAP_PRECEDING)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
