@@ -13,9 +13,10 @@
 //    contiguous ranges over one CTA per SM.  With more than one part, the parts leave partial sums in
 //    the workspace (plain stores) and a small follow-on kernel adds them in part order
 //    (deterministic); a fence + ticket per unit to combine in-kernel cost ~11 us on a 95 MB matrix.
-//  * Lookup: the two split-table prmt lookups (tables -kv[0..7] and kv[8..15], zero elsewhere) merge
-//    into the signed codebook byte by one IADD3 (to kv+128) and one XOR (to kv): one s8 x s8 MMA
-//    per sub-block and 16 rows.
+//  * Lookup: the two split-table prmt lookups (tables -kv[0..7] and kv[8..15], zero elsewhere) feed
+//    one s8 x s8 MMA each (no merge on the integer pipe, which is the busiest one); both accumulators
+//    start at the bit pattern of 1.5*2^23, so the two sums are read as floats and one packed fp32
+//    subtraction gives the exact int32 sub-block dot sumi as an fp32 value.
 //  * A unit is processed by a pair of consumer warps (8 pairs per CTA, units it = pair, pair+8, ...
 //    over a stage ring sized to shared memory); the two warps split the unit's super-blocks (even /
 //    odd) and add their partial sums through the stage buffer once both are done reading it (half 0
@@ -38,11 +39,15 @@ constexpr int kPairs = 8;          // consumer warp pairs: one unit (tile x part
 constexpr int kNCW = 2 * kPairs;   // consumer warps; the two warps of a pair split the unit's super-blocks
 
 struct MmaSmem {
-    uint32_t bar_off, flag_off, act_off, dx_off, ring_off, total;
+    uint32_t bar_off, flag_off, act_off, dx_off, scr_off, ring_off, total;
 };
+
+constexpr int kStageChunk = 8;                      // Q8_1 blocks per coalesced staging chunk
+constexpr int kChunkWords = kStageChunk * kQ8Bytes / 4;  // 72
 
 // act: per staged part (up to 2) and sub-block: 32 lanes x uint2 (B fragment words) = 256 B;
 // dx: per sub-block, d_x of the 8 tokens (32 B);
+// scr: per consumer warp, one chunk of 8 raw Q8_1 blocks (288 B) while staging;
 // ring: `stages` x (16 rows x pk pairs x 272 B).
 __host__ __device__ inline MmaSmem mma_smem(int pk, int stages) {
     MmaSmem L;
@@ -50,7 +55,8 @@ __host__ __device__ inline MmaSmem mma_smem(int pk, int stages) {
     L.flag_off = 2 * kMaxMmaStages * 8;
     L.act_off = 384;
     L.dx_off = L.act_off + 2u * (uint32_t)pk * 16 * 256;
-    L.ring_off = (L.dx_off + 2u * (uint32_t)pk * 16 * 32 + 127) & ~127u;
+    L.scr_off = L.dx_off + 2u * (uint32_t)pk * 16 * 32;
+    L.ring_off = (L.scr_off + (uint32_t)kNCW * kChunkWords * 4 + 127) & ~127u;
     L.total = L.ring_off + (uint32_t)stages * 16u * (uint32_t)pk * 272u;
     return L;
 }
@@ -66,6 +72,19 @@ __device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, f
         : "+f"(d0), "+f"(d1)
         : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
+
+// (d0, d1) = (a0, a1) - (b0, b1), one instruction on sm_100.
+__device__ __forceinline__ void sub2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// int32 -> fp32 without conversion instructions: MMA accumulators that start at kMagicI (the bit
+// pattern of 1.5 * 2^23) end as the bit pattern of the float 1.5 * 2^23 + s, exact while
+// |s| < 2^22 (a half-table sub-block dot is at most 32 * 127 * 127 = 516128 in magnitude).
+constexpr int kMagicI = 0x4B400000;
 
 __device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
     asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
@@ -176,27 +195,48 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
     grid_dependency_wait();
     const int pfirst = nunits > 0 ? (int)(u0 / T) : 0;
     const int plast = nunits > 0 ? (int)((u1 - 1) / T) : -1;
-    for (int slot = 0; slot <= plast - pfirst && slot < 2; ++slot) {
-        const int p = pfirst + slot;
-        const int nsub = 16 * min(pk, a.pairs - p * pk);
-        const int sb_base = p * pk * 16;
-        for (int e = ctid; e < nsub * 8; e += nct) {
-            const int sbl = e >> 3, n = e & 7;
-            uint2 frag[4] = {make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u)};
-            float dxv = 0.0f;
-            if (n < B) {
-                const uint32_t* q = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb_base + sbl) * kQ8Bytes);
-                uint32_t w[9];
+    {
+        // One warp per chunk of 8 consecutive Q8_1 blocks of one token (288 contiguous bytes): three
+        // coalesced word loads into the warp's scratch, then lane (b, j) = (lane/4, lane%4) builds
+        // B-fragment word pair j of block b and lane (b, 0) its d_x.  Tokens >= B stay zero.
+        const int nslot = min(plast - pfirst + 1, 2);
+        int nsubs[2] = {0, 0};
+        for (int sl = 0; sl < nslot; ++sl) nsubs[sl] = 16 * min(pk, a.pairs - (pfirst + sl) * pk);
+        uint32_t* scr = reinterpret_cast<uint32_t*>(smem + L.scr_off) + cw * kChunkWords;
+        uint2* actw = reinterpret_cast<uint2*>(smem + L.act_off);
+        float* dxw = reinterpret_cast<float*>(smem + L.dx_off);
+        const int ch0 = nsubs[0] / kStageChunk, ch1 = nsubs[1] / kStageChunk;  // chunks per token
+        const int nchunks = (ch0 + ch1) * B;
+        for (int q = cw; q < nchunks; q += kNCW) {
+            const int n = q % B, r = q / B;
+            const int slot = r < ch0 ? 0 : 1;
+            const int sbl0 = (r - slot * ch0) * kStageChunk;
+            const int sb = (pfirst + slot) * pk * 16 + sbl0;
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb) * kQ8Bytes);
+            const uint32_t v0 = __ldg(src + lane), v1 = __ldg(src + 32 + lane);
+            const uint32_t v2 = lane < kChunkWords - 64 ? __ldg(src + 64 + lane) : 0u;
+            scr[lane] = v0;
+            scr[32 + lane] = v1;
+            if (lane < kChunkWords - 64) scr[64 + lane] = v2;
+            __syncwarp();
+            const int bq = lane >> 2, j = lane & 3;
+            const uint32_t* blk = scr + bq * (kQ8Bytes / 4);
+            const int sbl = sbl0 + bq;
+            actw[(slot * pk * 16 + sbl) * 32 + n * 4 + j] = make_uint2(act_perm_lo(blk[1 + j], blk[5 + j]), act_perm_hi(blk[1 + j], blk[5 + j]));
+            if (j == 0) dxw[(slot * pk * 16 + sbl) * 8 + n] = f16_bits_to_f32(blk[0]);
+            __syncwarp();
+        }
+        if (B < 8) {
+            const int zitems = (nsubs[0] + nsubs[1]) * (8 - B);
+            for (int e = ctid; e < zitems; e += nct) {
+                const int n = B + e % (8 - B), sbg = e / (8 - B);
+                const int slot = sbg < nsubs[0] ? 0 : 1;
+                const int sbl = sbg - slot * nsubs[0];
+                uint2* dst = actw + (slot * pk * 16 + sbl) * 32 + n * 4;
 #pragma unroll
-                for (int j = 0; j < 9; ++j) w[j] = __ldg(q + j);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) frag[j] = make_uint2(act_perm_lo(w[1 + j], w[5 + j]), act_perm_hi(w[1 + j], w[5 + j]));
-                dxv = f16_bits_to_f32(w[0]);
+                for (int j = 0; j < 4; ++j) dst[j] = make_uint2(0u, 0u);
+                dxw[(slot * pk * 16 + sbl) * 8 + n] = 0.0f;
             }
-            uint2* dst = reinterpret_cast<uint2*>(smem + L.act_off) + (slot * pk * 16 + sbl) * 32 + n * 4;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) dst[j] = frag[j];
-            reinterpret_cast<float*>(smem + L.dx_off)[(slot * pk * 16 + sbl) * 8 + n] = dxv;
         }
     }
     named_barrier(kPairs + 1, nct);
@@ -248,20 +288,22 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                     const uint2 bf = actp[sbl * 32];
                     const float2 dx = *reinterpret_cast<const float2*>(dxp + sbl * 8);
                     const uint32_t xf0 = x0 ^ 0x88888888u, xf8 = x8 ^ 0x88888888u;
-                    // Codebook bytes: biased kv + 128 = 128 - (-kv) (codes < 8) or 128 + kv (codes >= 8) by one
-                    // IADD3, back to signed kv by flipping the top bit: one s8 x s8 MMA gives sumi.
-                    const uint32_t hl0 = prmt(a.lut[2], a.lut[3], xf0), ll0 = prmt(a.lut[0], a.lut[1], x0);
-                    const uint32_t hl8 = prmt(a.lut[2], a.lut[3], xf8), ll8 = prmt(a.lut[0], a.lut[1], x8);
-                    const uint32_t hh0 = prmt(a.lut[2], a.lut[3], hi16(xf0)), lh0 = prmt(a.lut[0], a.lut[1], hi16(x0));
-                    const uint32_t hh8 = prmt(a.lut[2], a.lut[3], hi16(xf8)), lh8 = prmt(a.lut[0], a.lut[1], hi16(x8));
-                    const uint32_t ab[4] = {(0x80808080u - ll0 + hl0) ^ 0x80808080u, (0x80808080u - ll8 + hl8) ^ 0x80808080u,
-                                            (0x80808080u - lh0 + hh0) ^ 0x80808080u, (0x80808080u - lh8 + hh8) ^ 0x80808080u};
-                    int dd[4] = {0, 0, 0, 0};
-                    mma_s8(dd, ab, bf.x, bf.y);
+                    // Codebook bytes of the two table halves: ah = kv (codes >= 8, else 0), al = -kv (codes
+                    // < 8, else 0), so kv = ah - al.  Two s8 x s8 MMAs (both accumulators starting at
+                    // kMagicI) give 1.5*2^23 + sum(ah*a) and 1.5*2^23 + sum(al*a) as float bit patterns, and
+                    // their fp32 difference is sumi exactly (both lie in [2^23, 2^24): Sterbenz).
+                    const uint32_t ah[4] = {prmt(a.lut[2], a.lut[3], xf0), prmt(a.lut[2], a.lut[3], xf8),
+                                            prmt(a.lut[2], a.lut[3], hi16(xf0)), prmt(a.lut[2], a.lut[3], hi16(xf8))};
+                    const uint32_t al[4] = {prmt(a.lut[0], a.lut[1], x0), prmt(a.lut[0], a.lut[1], x8),
+                                            prmt(a.lut[0], a.lut[1], hi16(x0)), prmt(a.lut[0], a.lut[1], hi16(x8))};
+                    int dd[4] = {kMagicI, kMagicI, kMagicI, kMagicI};
+                    int dl[4] = {kMagicI, kMagicI, kMagicI, kMagicI};
+                    mma_s8(dd, ah, bf.x, bf.y);
+                    mma_s8(dl, al, bf.x, bf.y);
                     const float f0 = __shfl_sync(0xFFFFFFFFu, fq0[ib & 1], 4 * g + (ib >> 1));
                     const float f8 = __shfl_sync(0xFFFFFFFFu, fq8[ib & 1], 4 * g + (ib >> 1));
-                    const int s0 = dd[0], s1 = dd[1], s2 = dd[2], s3 = dd[3];
                     if constexpr (kDebug) {
+                        const int s0 = dd[0] - dl[0], s1 = dd[1] - dl[1], s2 = dd[2] - dl[2], s3 = dd[3] - dl[3];
                         const int64_t r0w = t * 16 + g, r8w = r0w + 8;
                         const int sbg = p * pk * 16 + sbl;
                         if (2 * c < B && r0w < a.N) a.sumi[((int64_t)(2 * c) * a.N + r0w) * nsb + sbg] = s0;
@@ -270,11 +312,13 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                         if (2 * c + 1 < B && r8w < a.N) a.sumi[((int64_t)(2 * c + 1) * a.N + r8w) * nsb + sbg] = s3;
                     }
                     // acc += (f * dx) * sumi, as one rounding of the product f*dx and one fused add.
-                    float c0, c1, c2, c3;
+                    float c0, c1, c2, c3, v0, v1, v2, v3;
+                    sub2(v0, v1, __int_as_float(dd[0]), __int_as_float(dd[1]), __int_as_float(dl[0]), __int_as_float(dl[1]));
+                    sub2(v2, v3, __int_as_float(dd[2]), __int_as_float(dd[3]), __int_as_float(dl[2]), __int_as_float(dl[3]));
                     mul2(c0, c1, f0, f0, dx.x, dx.y);
                     mul2(c2, c3, f8, f8, dx.x, dx.y);
-                    fma2(acc[0], acc[1], c0, c1, (float)s0, (float)s1);
-                    fma2(acc[2], acc[3], c2, c3, (float)s2, (float)s3);
+                    fma2(acc[0], acc[1], c0, c1, v0, v1);
+                    fma2(acc[2], acc[3], c2, c3, v2, v3);
                 }
             }
         }
