@@ -34,6 +34,18 @@ extern "C" {
 int iq4xs_dec_residual_rmsnorm_q8(float* x, const float* delta, const float* w, int64_t D, int64_t T, float eps,
                                   void* q8, float* h_out, unsigned flags, cudaStream_t stream);
 
+/* Residual + RMSNorm fused into the batch-1 decode GEMV that consumes it:
+ *   v = x + delta (delta may be null), h = (v * rsqrt(mean(v^2) + eps)) * w, Y[n] = sum_k W[n][k] q8(h)[k]
+ * where q8(h) are the Q8_1 blocks iq4xs_q8_1_quantize would make of h (every CTA of the GEMV builds
+ * them in its shared memory; the weight copies start before the kernel waits for x).  If x_out is
+ * not null, v is also written there (it must not be x or delta; a decoder alternates two residual
+ * buffers).  x, delta, w and x_out 16-byte aligned.  K <= 20480 and the bulk-copy GEMV (K/256 even, W 16-byte aligned), otherwise
+ * IQ4XS_ERR_NOT_SUPPORTED.  workspace >= iq4xs_gemv_q8_workspace_bytes(K, N, 1).
+ * IQ4XS_FLAG_PDL: W is not written by the preceding kernel (programmatic dependent launch). */
+int iq4xs_dec_rmsnorm_gemv(const void* W, const float* x, const float* delta, const float* w, float eps, float* x_out,
+                           float* Y, int64_t K, int64_t N, void* workspace, size_t workspace_bytes, unsigned flags,
+                           cudaStream_t stream);
+
 /* Attention of one new token at position *pos (a device int64, so a captured graph can advance it):
  *   qkv      fp32 [q_heads + 2*kv_heads][head_dim]: the token's q heads, then k heads, then v heads
  *   k_cache, v_cache  f16 [kv_heads][max_seq][head_dim] (16-byte aligned)

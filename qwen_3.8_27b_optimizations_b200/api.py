@@ -71,6 +71,7 @@ DECODER_SIGNATURES = {
     "iq4xs_dec_attention_decode_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp,
                                            C.c_uint, _vp]),
     "iq4xs_dec_swiglu_q8": (_i, [_vp, _i64, _i64, _vp, C.c_uint, _vp]),
+    "iq4xs_dec_rmsnorm_gemv": (_i, [_vp, _vp, _vp, _vp, _f, _vp, _vp, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
 }
 
 _lib = None
@@ -394,3 +395,18 @@ def dec_swiglu_q8(gu, F: int, q8=None, flags: int = 0, stream=None):
     q8 = _q8_out(T, F, gu.device, q8)
     _check("iq4xs_dec_swiglu_q8", lib().iq4xs_dec_swiglu_q8(_ptr(gu), F, T, _ptr(q8), flags, _stream(stream)))
     return q8
+
+
+def dec_rmsnorm_gemv(W, x, w, eps: float, N: int, delta=None, x_out=None, out=None, flags: int = 0, stream=None,
+                     workspace=None):
+    """Y [1][N] = W . q8(rmsnorm(x + delta) * w) in one kernel (batch 1); x + delta also goes to x_out
+    when given (a buffer other than x and delta)."""
+    torch = _torch()
+    K = x.shape[-1]
+    Y = out if out is not None else torch.empty((1, N), dtype=torch.float32, device=x.device)
+    ws = workspace if workspace is not None else _workspace(gemv_q8_workspace_bytes(K, N, 1), x.device)
+    _check("iq4xs_dec_rmsnorm_gemv", lib().iq4xs_dec_rmsnorm_gemv(
+        _ptr(W), _ptr(x), _ptr(delta) if delta is not None else None, _ptr(w), eps,
+        _ptr(x_out) if x_out is not None else None, _ptr(Y), K, N, _ptr(ws), ws.numel() * ws.element_size(), flags,
+        _stream(stream)))
+    return Y

@@ -58,18 +58,124 @@ __device__ __forceinline__ bool wait_sleep_or_abort(uint64_t* bar, uint32_t pari
 // sum in shared memory and the last of the KW warps (shared-memory ticket) adds them in kw order:
 // deterministic.
 struct RowSmem {
-    uint32_t bar_off, abort_off, part_off, cnt_off, ring_off, total;
+    uint32_t bar_off, abort_off, red_off, part_off, cnt_off, q8_off, ring_off, total;
 };
 
-__host__ __device__ inline RowSmem gemv_row_smem(int B, int R, int KW, int stages, int64_t stage_bytes) {
+// q8_bytes: Q8_1 activations built in shared memory from an fp32 source (0 for kActQ8).
+__host__ __device__ inline RowSmem gemv_row_smem(int B, int R, int KW, int stages, int64_t stage_bytes,
+                                                 uint32_t q8_bytes = 0) {
     RowSmem L;
     L.bar_off = 0;
     L.abort_off = 2 * kMaxStages * 8;
-    L.part_off = L.abort_off + 16;
+    L.red_off = L.abort_off + 16;  // 32 floats: per-warp sums of squares of the RMSNorm source
+    L.part_off = L.red_off + 128;
     L.cnt_off = L.part_off + (uint32_t)kMaxStages * R * KW * B * 4;
-    L.ring_off = (L.cnt_off + (uint32_t)kMaxStages * R * 4 + 127) & ~127u;
+    L.q8_off = (L.cnt_off + (uint32_t)kMaxStages * R * 4 + 15) & ~15u;
+    L.ring_off = (L.q8_off + q8_bytes + 127) & ~127u;
     L.total = L.ring_off + (uint32_t)(stages * stage_bytes);
     return L;
+}
+
+// Consumer warps (warp index cw of ncw) build the Q8_1 activations of an fp32 source in shared
+// memory, four blocks (128 values, one float4 per lane) at a time with q8_1_quad_store; each warp
+// issues the loads of a batch of quads (kActQ / kActQF) before using any (one round trip per batch).
+// kActNorm (batch 1): v = x (+ delta) (CTA 0 also writes v to x_out), the sum of v^2 per lane, per
+// warp (xor butterfly) and then over warps in warp order (the same order in every CTA),
+// r = rsqrt(mean + eps), h = (v * r) * w.  The first batch of v and w stays in registers for the
+// second pass; later batches (K > 6144) are re-read.  Ends with a barrier of the consumer warps
+// (named barrier `bar_id`).
+constexpr int kActQ = 4;    // kActNorm: quads per warp per batch (v and w of the first batch stay in registers)
+constexpr int kActQF = 12;  // kActF32: quads per warp per batch (one batch up to K = 18432 at batch 1)
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+__device__ __forceinline__ float4 add4_rn(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
+__device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K, uint8_t* q8s, float* red, int cw,
+                                             int ncw, int lane, int bar_id) {
+    const int nq = B * K / 128;
+    const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (act.mode == kActNorm) {
+        float4 v0[kActQ], w0[kActQ];
+        float ss = 0.0f;
+        for (int base = cw; base < nq; base += ncw * kActQ) {
+            float4 xa[kActQ], da[kActQ];
+#pragma unroll
+            for (int i = 0; i < kActQ; ++i) {
+                const int qd = base + i * ncw;
+                xa[i] = da[i] = zero4;
+                if (qd < nq) {
+                    xa[i] = ldg4(act.x + qd * 128 + 4 * lane);
+                    if (act.delta) da[i] = ldg4(act.delta + qd * 128 + 4 * lane);
+                    if (base == cw) w0[i] = ldg4(act.w + qd * 128 + 4 * lane);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kActQ; ++i) {
+                const int qd = base + i * ncw;
+                if (qd >= nq) continue;
+                const float4 v = act.delta ? add4_rn(xa[i], da[i]) : xa[i];
+                if (act.x_out && blockIdx.x == 0) *reinterpret_cast<float4*>(act.x_out + qd * 128 + 4 * lane) = v;
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+                if (base == cw) v0[i] = v;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+        if (lane == 0) red[cw] = ss;
+        named_barrier(bar_id, ncw * 32);
+        float tot = 0.0f;
+        for (int i = 0; i < ncw; ++i) tot += red[i];
+        const float r = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), act.eps));
+        for (int base = cw; base < nq; base += ncw * kActQ) {
+            float4 va[kActQ], wa[kActQ];
+#pragma unroll
+            for (int i = 0; i < kActQ; ++i) {
+                const int qd = base + i * ncw;
+                va[i] = wa[i] = zero4;
+                if (qd >= nq) continue;
+                if (base == cw) {
+                    va[i] = v0[i];
+                    wa[i] = w0[i];
+                } else {
+                    va[i] = ldg4(act.x + qd * 128 + 4 * lane);
+                    if (act.delta) va[i] = add4_rn(va[i], ldg4(act.delta + qd * 128 + 4 * lane));
+                    wa[i] = ldg4(act.w + qd * 128 + 4 * lane);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kActQ; ++i) {
+                const int qd = base + i * ncw;
+                if (qd >= nq) continue;
+                float4 h;
+                h.x = __fmul_rn(__fmul_rn(va[i].x, r), wa[i].x);
+                h.y = __fmul_rn(__fmul_rn(va[i].y, r), wa[i].y);
+                h.z = __fmul_rn(__fmul_rn(va[i].z, r), wa[i].z);
+                h.w = __fmul_rn(__fmul_rn(va[i].w, r), wa[i].w);
+                q8_1_quad_store(h, q8s + (size_t)qd * 4 * kQ8Bytes, lane);
+            }
+        }
+    } else {
+        for (int base = cw; base < nq; base += ncw * kActQF) {
+            float4 xa[kActQF];
+#pragma unroll
+            for (int i = 0; i < kActQF; ++i) {
+                const int qd = base + i * ncw;
+                xa[i] = qd < nq ? ldg4(act.x + (int64_t)qd * 128 + 4 * lane) : zero4;
+            }
+#pragma unroll
+            for (int i = 0; i < kActQF; ++i) {
+                const int qd = base + i * ncw;
+                if (qd < nq) q8_1_quad_store(xa[i], q8s + (size_t)qd * 4 * kQ8Bytes, lane);
+            }
+        }
+    }
+    named_barrier(bar_id, ncw * 32);
 }
 
 // x >> 16 on the FMA pipe: one mul.hi.u32 by 2^16 (the integer ALU pipe is the busier one).
@@ -98,7 +204,9 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
     const int R = a.rows_per_stage, KW = a.kw;
     const int stages = a.stages;
     const int64_t stage_bytes = (int64_t)R * a.rb;
-    const RowSmem L = gemv_row_smem(B, R, KW, stages, stage_bytes);
+    const bool smem_act = a.act.mode != kActQ8;
+    const RowSmem L = gemv_row_smem(B, R, KW, stages, stage_bytes,
+                                    smem_act ? (uint32_t)(B * (a.K / kQK8) * kQ8Bytes) : 0u);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     uint64_t* empty = full + kMaxStages;
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.abort_off);
@@ -159,6 +267,8 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
     const uint32_t off_q = off_h + 8 + 16 * ib;
 
     grid_dependency_wait();
+    if (smem_act)
+        build_act_q8(a.act, B, a.K, smem + L.q8_off, reinterpret_cast<float*>(smem + L.red_off), cw, NCW, lane, 1);
     uint32_t alo[SPL][B][4], ahi[SPL][B][4];
     float dx[SPL][B];
 #pragma unroll
@@ -167,10 +277,16 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
 #pragma unroll
         for (int t = 0; t < B; ++t) {
             if (!kTail || sb < nsb) {
-                const uint32_t* q = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)t * nsb + sb) * kQ8Bytes);
                 uint32_t w[9];
+                if (smem_act) {
+                    const uint32_t* q = reinterpret_cast<const uint32_t*>(smem + L.q8_off + ((size_t)t * nsb + sb) * kQ8Bytes);
 #pragma unroll
-                for (int j = 0; j < 9; ++j) w[j] = __ldg(q + j);
+                    for (int j = 0; j < 9; ++j) w[j] = q[j];
+                } else {
+                    const uint32_t* q = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)t * nsb + sb) * kQ8Bytes);
+#pragma unroll
+                    for (int j = 0; j < 9; ++j) w[j] = __ldg(q + j);
+                }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     alo[i][t][j] = act_perm_lo(w[1 + j], w[5 + j]);
@@ -334,7 +450,6 @@ __global__ void __launch_bounds__(256) gemv_iq4xs_q8_generic_kernel(const GemvAr
 // --------------------------------------------------------------------------------------------
 // Host-side launch helpers.
 namespace {
-constexpr int kNCW = 8, kRPL = 2, kKC = 4;
 
 int g_num_sms[64];
 int g_max_smem[64];
@@ -371,9 +486,11 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     int kw = 1;
     while (kw < 4 && (nsb + 32 * kw - 1) / (32 * kw) > spl_max) kw *= 2;
     const int spl = (nsb + 32 * kw - 1) / (32 * kw);
-    if (spl > spl_max)  // K too long for register-resident activations: tensor-core kernel
+    if (spl > spl_max) {  // K too long for register-resident activations: tensor-core kernel
+        if (a.act.mode == kActNorm) return cudaErrorNotSupported;
         return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.tickets, a.partials, a.partial_bytes, a.K, a.N,
-                               B, stream, pdl, sms, smem_optin, a.err, a.lut);
+                               B, stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
+    }
     const bool tail = (nsb != 32 * kw * spl);
     const int R = (NCW / kw) * RPW;
     a.kw = kw;
@@ -382,12 +499,13 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     // At most ~110 KB of stages (two of them always): deeper rings did not stream faster, and a CTA
     // that leaves half the shared memory free lets the next kernel's CTA start on the same SM.
     constexpr int64_t kRowSmemTarget = 110000;
+    const uint32_t q8b = a.act.mode != kActQ8 ? (uint32_t)(B * nsb * kQ8Bytes) : 0u;
     int stages = kMaxStages;
-    while (stages > 2 && ((int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes).total > smem_optin ||
-                          (int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes).total > kRowSmemTarget))
+    while (stages > 2 && ((int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes, q8b).total > smem_optin ||
+                          (int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes, q8b).total > kRowSmemTarget + q8b))
         --stages;
     a.stages = stages;
-    const RowSmem L = gemv_row_smem(B, R, kw, stages, stage_bytes);
+    const RowSmem L = gemv_row_smem(B, R, kw, stages, stage_bytes, q8b);
     if ((int64_t)L.total > smem_optin || stage_bytes >= (1 << 20)) return cudaErrorInvalidConfiguration;
     void* kern = nullptr;
     switch (spl) {
@@ -437,8 +555,9 @@ cudaError_t dispatch(int B, GemvArgs a, cudaStream_t stream, bool pdl) {
     cudaGetDevice(&dev);
     int sms = 0, smem_optin = 0;
     device_limits(dev, &sms, &smem_optin);
-    const bool bulk_ok = (a.kb % 2 == 0) && ((reinterpret_cast<uintptr_t>(a.W) & 15u) == 0) && !a.force_generic;
+    const bool bulk_ok = gemv_bulk_path(a.W, a.K) && !a.force_generic;
     if (!bulk_ok) {
+        if (a.act.mode != kActQ8) return cudaErrorNotSupported;  // the generic kernel reads Q8_1 from global
         switch (B) {
 #define IQ4XS_GEN(BB) case BB: return launch_generic<BB, kDebug>(a, stream, pdl, sms);
             IQ4XS_GEN(1) IQ4XS_GEN(2) IQ4XS_GEN(3) IQ4XS_GEN(4) IQ4XS_GEN(5) IQ4XS_GEN(6) IQ4XS_GEN(7) IQ4XS_GEN(8)
@@ -447,10 +566,15 @@ cudaError_t dispatch(int B, GemvArgs a, cudaStream_t stream, bool pdl) {
         }
     }
     if (B == 1) return launch_rows<1, kDebug>(a, stream, pdl, sms, smem_optin);
+    if (a.act.mode == kActNorm) return cudaErrorNotSupported;
     return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.tickets, a.partials, a.partial_bytes, a.K, a.N, B,
-                           stream, pdl, sms, smem_optin, a.err, a.lut);
+                           stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
 }
 }  // namespace
+
+bool gemv_bulk_path(const uint8_t* W, int64_t K) {
+    return ((K / kQK) % 2 == 0) && ((reinterpret_cast<uintptr_t>(W) & 15u) == 0);
+}
 
 int device_sm_count() {
     int dev = 0, sms = 0, smem = 0;

@@ -207,17 +207,47 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
         float* dxw = reinterpret_cast<float*>(smem + L.dx_off);
         const int ch0 = nsubs[0] / kStageChunk, ch1 = nsubs[1] / kStageChunk;  // chunks per token
         const int nchunks = (ch0 + ch1) * B;
-        for (int q = cw; q < nchunks; q += kNCW) {
+        // fp32 source (batch <= 2): the fp32 values of all of this warp's chunks are requested first
+        constexpr int kF32Chunks = 3;  // >= 2 slots * 16 * pk(<= 5) / 8 * 2 tokens / kNCW
+        float4 xf[kF32Chunks][2];
+        if (a.act.mode == kActF32) {
+#pragma unroll
+            for (int k = 0; k < kF32Chunks; ++k) {
+                const int q = cw + k * kNCW;
+                xf[k][0] = xf[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (q < nchunks) {
+                    const int n = q % B, r = q / B;
+                    const int slot = r < ch0 ? 0 : 1;
+                    const int sb = (pfirst + slot) * pk * 16 + (r - slot * ch0) * kStageChunk;
+                    const float4* xs = reinterpret_cast<const float4*>(a.act.x + (int64_t)n * a.K + (int64_t)sb * kQK8) + lane;
+                    xf[k][0] = __ldg(xs);
+                    xf[k][1] = __ldg(xs + 32);
+                }
+            }
+        }
+        for (int q = cw, kq = 0; q < nchunks; q += kNCW, ++kq) {
             const int n = q % B, r = q / B;
             const int slot = r < ch0 ? 0 : 1;
             const int sbl0 = (r - slot * ch0) * kStageChunk;
             const int sb = (pfirst + slot) * pk * 16 + sbl0;
-            const uint32_t* src = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb) * kQ8Bytes);
-            const uint32_t v0 = __ldg(src + lane), v1 = __ldg(src + 32 + lane);
-            const uint32_t v2 = lane < kChunkWords - 64 ? __ldg(src + 64 + lane) : 0u;
-            scr[lane] = v0;
-            scr[32 + lane] = v1;
-            if (lane < kChunkWords - 64) scr[64 + lane] = v2;
+            if (a.act.mode == kActF32) {  // quantise the chunk's 8 blocks from fp32 into the scratch
+                float4 x0 = xf[0][0], x1 = xf[0][1];
+#pragma unroll
+                for (int k = 1; k < kF32Chunks; ++k)
+                    if (kq == k) {
+                        x0 = xf[k][0];
+                        x1 = xf[k][1];
+                    }
+                q8_1_quad_store(x0, reinterpret_cast<uint8_t*>(scr), lane);
+                q8_1_quad_store(x1, reinterpret_cast<uint8_t*>(scr) + 4 * kQ8Bytes, lane);
+            } else {
+                const uint32_t* src = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb) * kQ8Bytes);
+                const uint32_t v0 = __ldg(src + lane), v1 = __ldg(src + 32 + lane);
+                const uint32_t v2 = lane < kChunkWords - 64 ? __ldg(src + 64 + lane) : 0u;
+                scr[lane] = v0;
+                scr[32 + lane] = v1;
+                if (lane < kChunkWords - 64) scr[64 + lane] = v2;
+            }
             __syncwarp();
             const int bq = lane >> 2, j = lane & 3;
             const uint32_t* blk = scr + bq * (kQ8Bytes / 4);
@@ -226,7 +256,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
             if (j == 0) dxw[(slot * pk * 16 + sbl) * 8 + n] = f16_bits_to_f32(blk[0]);
             __syncwarp();
         }
-        if (B < 8) {
+        if constexpr (B < 8) {
             const int zitems = (nsubs[0] + nsubs[1]) * (8 - B);
             for (int e = ctid; e < zitems; e += nct) {
                 const int n = B + e % (8 - B), sbg = e / (8 - B);
@@ -461,7 +491,8 @@ static cudaError_t launch_mma_b(const CUtensorMap& map, GemvMmaArgs a, int smem,
 
 cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32_t* sumi, uint32_t* tickets,
                             float* partials, size_t partial_bytes, int64_t K, int64_t N, int B, cudaStream_t stream,
-                            bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4]) {
+                            bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4],
+                            const ActSource* act) {
     if (B < 1 || B > 8 || K % 512 != 0 || (reinterpret_cast<uintptr_t>(W) & 15u)) return cudaErrorInvalidValue;
     EncodeTiledFn enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
@@ -503,6 +534,11 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     a.partial = partials;
     a.tile_cnt = tickets;
     for (int i = 0; i < 4; ++i) a.lut[i] = lut[i];
+    a.act.mode = kActQ8;
+    if (act && act->mode != kActQ8) {
+        if (act->mode != kActF32) return cudaErrorNotSupported;
+        a.act = *act;
+    }
     const int64_t U = T * parts;
     // A CTA holds the activations of at most two parts: its unit range must not exceed T units.
     int64_t grid64 = std::min<int64_t>(sms, U);

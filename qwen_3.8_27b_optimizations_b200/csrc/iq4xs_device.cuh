@@ -86,6 +86,35 @@ __device__ __forceinline__ void q8_1_block_store(float x, uint8_t* out, int lane
         *reinterpret_cast<uint32_t*>(out) = (uint32_t)f32_to_f16_trunc(d) | ((uint32_t)f32_to_f16_trunc(sum) << 16);
 }
 
+// Four consecutive Q8_1 blocks (144 bytes at `out`, 4-byte aligned) from 128 values held as one
+// float4 per lane (lane l: values 4l..4l+3; lanes 8j..8j+7 form block j).  amax (exact in any order),
+// d = amax/127 and q = (int8)roundf(x/d) are those of q8_1_block_store, so the quants and d are
+// identical; the block sum (the upper half of ds, which no IQ4_XS dot reads) is added in a
+// different order and may differ in its last bit.
+__device__ __forceinline__ void q8_1_quad_store(float4 v, uint8_t* out, int lane) {
+    const unsigned full = 0xFFFFFFFFu;
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    float sum = (v.x + v.y) + (v.z + v.w);
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(full, amax, off));
+        sum += __shfl_xor_sync(full, sum, off);
+    }
+    const float d = amax / 127.0f;
+    int q0 = 0, q1 = 0, q2 = 0, q3 = 0;
+    if (amax != 0.0f) {
+        q0 = (int)roundf(v.x / d);
+        q1 = (int)roundf(v.y / d);
+        q2 = (int)roundf(v.z / d);
+        q3 = (int)roundf(v.w / d);
+    }
+    uint8_t* blk = out + (lane >> 3) * 36;
+    *reinterpret_cast<uint32_t*>(blk + 4 + 4 * (lane & 7)) =
+        ((uint32_t)q0 & 0xFFu) | (((uint32_t)q1 & 0xFFu) << 8) | (((uint32_t)q2 & 0xFFu) << 16) | ((uint32_t)q3 << 24);
+    if ((lane & 7) == 0)
+        *reinterpret_cast<uint32_t*>(blk) = (uint32_t)f32_to_f16_trunc(d) | ((uint32_t)f32_to_f16_trunc(sum) << 16);
+}
+
 // ------------------------------------------------------------------------------ byte permute
 // prmt.b32 default mode: bytes {b,a} numbered 0..7 (a = 0..3); selector nibble i: bits 2:0
 // pick the source byte, bit 3 replicates that byte's sign bit over the output byte.

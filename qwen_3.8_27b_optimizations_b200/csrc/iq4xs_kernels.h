@@ -7,6 +7,23 @@
 
 namespace iq4xs {
 
+// Where a GEMV's Q8_1 activations come from.  The fp32 sources are quantised (and, for kActNorm,
+// normalised) by every CTA into its own shared memory at kernel start, while the weight copies
+// are already in flight; the bytes equal those of the standalone quantizer on the same fp32 values.
+enum ActMode : int {
+    kActQ8 = 0,    // q8: Q8_1 blocks [B][K/32] in global memory
+    kActF32 = 1,   // x: fp32 [B][K]
+    kActNorm = 2,  // batch 1: h = rmsnorm(x + delta) * w, from fp32 x [K] (+ delta [K]), weight w [K]
+};
+struct ActSource {
+    int mode;
+    const float* x;
+    const float* delta;  // kActNorm: may be null
+    const float* w;      // kActNorm
+    float* x_out;        // kActNorm: x + delta is written here by CTA 0 (may be null; must not alias x)
+    float eps;
+};
+
 struct GemvArgs {
     const uint8_t* W;    // IQ4_XS rows [N][K/256][136]
     const uint8_t* q8;   // Q8_1 blocks [B][K/32][36]
@@ -27,6 +44,7 @@ struct GemvArgs {
     uint32_t* tickets;   // tensor-core kernel: per-tile tickets (zero between calls)
     float* partials;     // tensor-core kernel: cross-CTA partial sums
     size_t partial_bytes;
+    ActSource act;       // activation source (kActQ8: `q8` above)
 };
 
 struct GemvMmaArgs {
@@ -43,6 +61,7 @@ struct GemvMmaArgs {
     int parts;
     int stages;
     uint32_t lut[4];
+    ActSource act;       // kActQ8 or kActF32
 };
 
 // Tensor-core GEMV (batch 1..8).  Workspace = [tickets: kTicketBytes, zero between calls][partials].
@@ -52,8 +71,12 @@ size_t gemv_mma_partial_bytes_for(int64_t K, int64_t N, int B, int sms, int smem
 int device_smem_optin();
 cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32_t* sumi, uint32_t* tickets,
                             float* partials, size_t partial_bytes, int64_t K, int64_t N, int B, cudaStream_t stream,
-                            bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4]);
+                            bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4],
+                            const ActSource* act = nullptr);
 int device_sm_count();
+// True when launch_gemv_q8 runs the bulk-copy kernels for this matrix (the fused fp32 activation
+// sources need them; the generic kernel reads Q8_1 from global memory).
+bool gemv_bulk_path(const uint8_t* W, int64_t K);
 
 // Tensor-core prefill GEMM (gemm.cu).  Y[m][n] at y + m*ldy_m + n*ldy_n.
 struct GemmArgs {

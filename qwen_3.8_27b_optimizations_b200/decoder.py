@@ -17,9 +17,11 @@ does not depend on P.
 
 The decode step (one token) is captured in a CUDA graph and replayed, the position and the token
 living in device tensors, so generating N tokens issues no host work per token.  With the CUDA
-kernels, a decode layer is four Q8_1-input GEMVs and three fused kernels (include/iq4xs_decoder.h):
-residual+RMSNorm->Q8_1, RoPE+KV-append+attention->Q8_1, SwiGLU->Q8_1; each GEMV is launched as a
-programmatic dependent of the kernel before it, so its weight stream overlaps that kernel.  The
+kernels, a decode layer is six kernels (include/iq4xs_decoder.h): residual + RMSNorm fused into the
+q|k|v and gate|up GEMVs (each CTA normalises and quantises the activations in its shared memory),
+RoPE + KV-append + attention -> Q8_1, the o_proj GEMV, SwiGLU -> Q8_1 and the down_proj GEMV; each is
+launched as a programmatic dependent of the kernel before it, so the GEMVs' weight streams start
+while it finishes.  The
 prompt (prefill) runs the same model with torch ops around the tensor-core GEMM.
 """
 from __future__ import annotations
@@ -207,6 +209,7 @@ class TPDecoder:
             D = cfg.hidden
             q8 = lambda K: torch.empty((1, K // 32 * 36), dtype=torch.uint8, device=dev)
             self._dec = dict(x=torch.empty((1, D), dtype=torch.float32, device=dev),
+                             x2=torch.empty((1, D), dtype=torch.float32, device=dev),
                              h=torch.empty((1, D), dtype=torch.float32, device=dev),
                              q8d=q8(D), q8a=q8(self.hq * cfg.head_dim), q8f=q8(self.F),
                              qkv=torch.empty((1, self.nqkv), dtype=torch.float32, device=dev),
@@ -222,21 +225,26 @@ class TPDecoder:
         b = self._decode_buffers()
         D, hd = cfg.hidden, cfg.head_dim
         OV, PDL = api.FLAG_OVERLAP_PRECEDING, api.FLAG_PDL
-        xs = b["x"]
-        xs.copy_(x)
+        cur, nxt = b["x"], b["x2"]  # the residual stream: the fused GEMVs write x + delta to the other one
+        cur.copy_(x)
         delta = None
+
+        def norm_gemv(W, w, N, out):
+            nonlocal cur, nxt
+            api.dec_rmsnorm_gemv(W, cur, w, cfg.eps, N, delta=delta, x_out=nxt if delta is not None else None,
+                                 out=out, flags=PDL)
+            if delta is not None:
+                cur, nxt = nxt, cur
+
         for l, L in enumerate(self.layers):
-            api.dec_residual_rmsnorm_q8(xs, L["an"], cfg.eps, delta=delta, q8=b["q8d"], flags=PDL)
-            api.gemv_q8_ex(L["wqkv"], b["q8d"], D, self.nqkv, 1, out=b["qkv"], flags=OV)
+            norm_gemv(L["wqkv"], L["an"], self.nqkv, b["qkv"])
             api.dec_attention_decode_q8(b["qkv"], self.cache[l, 0], self.cache[l, 1], self.cos, self.sin, self._pos,
                                         self.hq, self.hkv, q8=b["q8a"], flags=PDL)
-            self._allreduce(api.gemv_q8_ex(L["wo"], b["q8a"], self.hq * hd, D, 1, out=b["o"], flags=OV))
-            api.dec_residual_rmsnorm_q8(xs, L["fn"], cfg.eps, delta=b["o"], q8=b["q8d"], flags=PDL)
-            api.gemv_q8_ex(L["wgu"], b["q8d"], D, 2 * self.F, 1, out=b["gu"], flags=OV)
+            delta = self._allreduce(api.gemv_q8_ex(L["wo"], b["q8a"], self.hq * hd, D, 1, out=b["o"], flags=OV))
+            norm_gemv(L["wgu"], L["fn"], 2 * self.F, b["gu"])
             api.dec_swiglu_q8(b["gu"], self.F, q8=b["q8f"], flags=PDL)
-            self._allreduce(api.gemv_q8_ex(L["wd"], b["q8f"], self.F, D, 1, out=b["d"], flags=OV))
-            delta = b["d"]
-        api.dec_residual_rmsnorm_q8(xs, self.final_norm, cfg.eps, delta=delta, h_out=b["h"], want_q8=False,
+            delta = self._allreduce(api.gemv_q8_ex(L["wd"], b["q8f"], self.F, D, 1, out=b["d"], flags=OV))
+        api.dec_residual_rmsnorm_q8(cur, self.final_norm, cfg.eps, delta=delta, h_out=b["h"], want_q8=False,
                                     flags=PDL)
         return b["h"]
 

@@ -67,6 +67,10 @@ def test_decoder_op_validation(pkg):
     # swiglu: F % 32
     assert L.iq4xs_dec_swiglu_q8(FAKE, 100, 1, FAKE, 0, None) == 2
     assert L.iq4xs_dec_swiglu_q8(None, 128, 1, FAKE, 0, None) == 1
+    # fused norm GEMV: x_out aliasing x, K too long, misaligned W
+    assert L.iq4xs_dec_rmsnorm_gemv(FAKE, FAKE, None, FAKE, 1e-6, FAKE, FAKE, 5120, 64, FAKE, 1 << 30, 0, None) == 1
+    assert L.iq4xs_dec_rmsnorm_gemv(FAKE, FAKE, None, FAKE, 1e-6, None, FAKE, 25600, 64, FAKE, 1 << 30, 0, None) == 7
+    assert L.iq4xs_dec_rmsnorm_gemv(FAKE + 4, FAKE, None, FAKE, 1e-6, None, FAKE, 5120, 64, FAKE, 1 << 30, 0, None) == 3
     # gemv_q8_ex shares gemv_q8's checks
     assert L.iq4xs_gemv_q8_ex(FAKE, FAKE, FAKE, 500, 64, 1, FAKE, 1 << 30, 1, None) == 2
 

@@ -119,3 +119,52 @@ def test_gemv_q8_ex_matches_gemv_q8(pkg):
     y1 = pkg.api.gemv_q8_ex(W, q8, K, N, B, flags=pkg.api.FLAG_OVERLAP_PRECEDING)
     torch.cuda.synchronize()
     assert torch.equal(y0, y1)
+
+
+@pytest.mark.parametrize("N,K", [(4096, 5120), (10240, 5120), (1024, 8192), (5120, 17408), (64, 25600)])
+@pytest.mark.parametrize("B", [1, 2, 5, 8])
+def test_gemv_f32_entry_equals_quantize_then_gemv(pkg, N, K, B):
+    """The fp32 entry quantises inside the GEMV kernel (every CTA into its shared memory): the result
+    equals the standalone quantizer followed by the Q8_1 GEMV bit for bit."""
+    W = pkg.api.random_weights(N, K, seed=N + K)
+    X = torch.randn((B, K), generator=_gen(B + K), device="cuda")
+    y_fused = pkg.api.gemv(W, X, N)
+    y_ref = pkg.api.gemv_q8(W, pkg.q8_1_quantize(X), K, N, B)
+    torch.cuda.synchronize()
+    assert torch.equal(y_fused, y_ref)
+    assert pkg.device_error() == 0
+
+
+@pytest.mark.parametrize("N", [10240, 2048])
+@pytest.mark.parametrize("with_delta", [True, False])
+def test_rmsnorm_gemv(pkg, N, with_delta):
+    """Residual + RMSNorm fused into the GEMV against the standalone norm kernel + Q8_1 GEMV: the
+    residual output is exact, the GEMV output agrees up to rare Q8_1 rounding flips (the sum of
+    squares is reduced in a different order)."""
+    K, eps = 5120, 1e-6
+    g = _gen(N)
+    W = pkg.api.random_weights(N, K, seed=77)
+    x = torch.randn((1, K), generator=g, device="cuda")
+    delta = torch.randn((1, K), generator=g, device="cuda") * 0.3 if with_delta else None
+    w = 1.0 + 0.02 * torch.randn(K, generator=g, device="cuda")
+    x_out = torch.full_like(x, float("nan"))
+    y = pkg.api.dec_rmsnorm_gemv(W, x, w, eps, N, delta=delta, x_out=x_out if with_delta else None)
+    xr = x.clone()
+    q8, _ = pkg.api.dec_residual_rmsnorm_q8(xr, w, eps, delta=delta)
+    y_ref = pkg.api.gemv_q8(W, q8, K, N, 1)
+    torch.cuda.synchronize()
+    if with_delta:
+        assert torch.equal(x_out, x + delta)
+    cos = torch.nn.functional.cosine_similarity(y.double(), y_ref.double(), dim=-1).item()
+    assert cos >= 0.999999
+    assert (y - y_ref).abs().max().item() <= 2e-3 * y_ref.abs().max().item()
+    assert pkg.device_error() == 0
+
+
+def test_rmsnorm_gemv_rejects_aliased_output(pkg):
+    K, N = 5120, 256
+    W = pkg.api.random_weights(N, K, seed=1)
+    x = torch.randn((1, K), device="cuda")
+    w = torch.ones(K, device="cuda")
+    with pytest.raises(pkg.IQ4XSError):
+        pkg.api.dec_rmsnorm_gemv(W, x, w, 1e-6, N, delta=x.clone(), x_out=x)
