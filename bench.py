@@ -149,15 +149,19 @@ SHARDED = [("lm_head", 152064, 5120), ("gate_up", 34816, 5120)]
 
 def sharded_sweep(P, dev, stream, rank: int, world: int, barrier, reps: int = 5):
     """lm_head and gate|up split by output rows over the ranks, GEMV at batch 1
-    and GEMM at M = 2048, each call followed by the all-gather of the output slices (NCCL).  Time per
-    call = max over ranks of the CUDA-event time of `reps` calls."""
+    and GEMM at M = 2048, each call followed by the all-gather of the output slices (GEMV: the NVLink
+    peer-memory pull kernel; GEMM: NCCL).  Time per call = max over ranks of the CUDA-event time of
+    `reps` calls."""
     import torch
     import torch.distributed as dist
     out = []
+    peers = None
+    if world > 1:
+        peers = P.peer.PeerGroup(max(P.sharded.max_shard_rows(N, world) for _, N, _ in SHARDED), areas=2)
     for name, N, K in SHARDED:
         r0, r1 = P.sharded.shard_rows(N, world, rank)
         W = P.random_weights(r1 - r0, K, seed=5000 + N + rank)
-        S = P.sharded.RowShardedIQ4XS(W, N, K, rank=rank, world=world) if world > 1 else \
+        S = P.sharded.RowShardedIQ4XS(W, N, K, rank=rank, world=world, peers=peers) if world > 1 else \
             P.sharded.RowShardedIQ4XS(W, N, K, rank=0, world=1)
         for op, M in (("gemv", 1), ("gemm", 2048)):
             X = P.fill_normal(M * K, seed=31 + M).view(M, K)
@@ -187,6 +191,8 @@ def sharded_sweep(P, dev, stream, rank: int, world: int, barrier, reps: int = 5)
             del X
         del S, W
         torch.cuda.empty_cache()
+    if peers is not None:
+        peers.close()
     return out
 
 
@@ -633,8 +639,9 @@ def main():
                              "kernel": "gemm_iq4xs_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators)"},
                 "per_shape": gemm_per},
             "decoder": decoder,
-            "sharded": {"what": "row-sharded over the ranks (strong scaling), NCCL all-gather of the outputs, "
-                                "time = max over ranks", "results": sharded},
+            "sharded": {"what": "row-sharded over the ranks (strong scaling), all-gather of the outputs (GEMV: "
+                                "NVLink peer-memory pull kernel, GEMM: NCCL), time = max over ranks",
+                        "results": sharded},
             "gpu_launches": args.steps * launches_per_step,
             "gpu_launches_per_step": launches_per_step,
             "clocks": clocks,

@@ -5,5 +5,6 @@ __graft_entry__.py, bench.py) under the module name ``iq4xs_b200``.
 """
 from .api import *  # noqa: F401,F403
 from .api import lib, LIB_PATH, SIGNATURES, IQ4XSError  # noqa: F401
+from . import peer  # noqa: F401,E402  (collectives over NVLink peer memory)
 from . import sharded  # noqa: F401,E402  (row-sharded multi-GPU matmuls)
 from . import decoder  # noqa: F401,E402  (synthetic tensor-parallel decoder)

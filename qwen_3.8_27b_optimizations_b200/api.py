@@ -74,6 +74,18 @@ DECODER_SIGNATURES = {
     "iq4xs_dec_rmsnorm_gemv": (_i, [_vp, _vp, _vp, _vp, _f, _vp, _vp, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
 }
 
+# include/iq4xs_peer.h (collectives over NVLink peer memory)
+PEER_SIGNATURES = {
+    "iq4xs_peer_alloc": (_i, [_sz, C.POINTER(_vp)]),
+    "iq4xs_peer_free": (_i, [_vp]),
+    "iq4xs_ipc_handle": (_i, [_vp, _vp]),
+    "iq4xs_ipc_open": (_i, [_vp, C.POINTER(_vp)]),
+    "iq4xs_ipc_close": (_i, [_vp]),
+    "iq4xs_peer_collective": (_i, [C.POINTER(_vp), C.POINTER(_vp), _vp, _vp, _i, _i, _i, _i64, _vp, C.c_uint32, _vp]),
+}
+IPC_HANDLE_BYTES = 64
+MAX_PEERS = 8
+
 _lib = None
 
 
@@ -91,7 +103,7 @@ def lib():
         if not LIB_PATH.exists():
             raise ImportError(f"{LIB_PATH} is missing; build it with __graft_entry__.build()")
         L = C.CDLL(str(LIB_PATH))
-        for name, (res, args) in {**SIGNATURES, **BENCH_SIGNATURES, **DECODER_SIGNATURES}.items():
+        for name, (res, args) in {**SIGNATURES, **BENCH_SIGNATURES, **DECODER_SIGNATURES, **PEER_SIGNATURES}.items():
             fn = getattr(L, name)
             fn.restype = res
             fn.argtypes = args
@@ -410,3 +422,40 @@ def dec_rmsnorm_gemv(W, x, w, eps: float, N: int, delta=None, x_out=None, out=No
         _ptr(x_out) if x_out is not None else None, _ptr(Y), K, N, _ptr(ws), ws.numel() * ws.element_size(), flags,
         _stream(stream)))
     return Y
+
+
+# ----------------------------------------------------------------------------- peer memory (iq4xs_peer.h)
+def peer_alloc(nbytes: int) -> int:
+    p = C.c_void_p()
+    _check("iq4xs_peer_alloc", lib().iq4xs_peer_alloc(nbytes, C.byref(p)))
+    return int(p.value)
+
+
+def peer_free(ptr: int) -> None:
+    _check("iq4xs_peer_free", lib().iq4xs_peer_free(ptr))
+
+
+def ipc_handle(ptr: int) -> bytes:
+    buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+    _check("iq4xs_ipc_handle", lib().iq4xs_ipc_handle(ptr, buf))
+    return bytes(buf.raw)
+
+
+def ipc_open(handle: bytes) -> int:
+    p = C.c_void_p()
+    buf = C.create_string_buffer(handle, IPC_HANDLE_BYTES)
+    _check("iq4xs_ipc_open", lib().iq4xs_ipc_open(buf, C.byref(p)))
+    return int(p.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check("iq4xs_ipc_close", lib().iq4xs_ipc_close(ptr))
+
+
+def peer_collective(src, rflags, flags: int, counter: int, rank: int, world: int, gather: bool, n: int, out: int,
+                    spin_limit: int = 0, stream=None) -> None:
+    """src / rflags: per-rank device addresses (this rank's view); see include/iq4xs_peer.h."""
+    arr = C.c_void_p * world
+    _check("iq4xs_peer_collective", lib().iq4xs_peer_collective(
+        arr(*src), arr(*rflags), flags, counter, rank, world, 1 if gather else 0, n, out, spin_limit,
+        _stream(stream)))

@@ -32,6 +32,7 @@ enum DeviceError : uint32_t {
     kDevErrDrainWait = 3,   // copies still in flight after an error
     kDevErrMmaWait = 4,     // tensor-core pipeline barrier timed out
     kDevErrPosition = 5,    // decode attention: the device-side position is outside the KV cache
+    kDevErrPeerWait = 6,    // peer collective: a peer's flag did not arrive within the spin limit
 };
 
 // Spin limit for every mbarrier wait (each try_wait already suspends for a while in hardware);

@@ -59,7 +59,8 @@ class TPDecoder:
 
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, group=None, seed: int = 0,
                  device="cuda", matmul: Optional[Callable] = None, gen_weights: Optional[Callable] = None,
-                 gen_normal: Optional[Callable] = None, fused_decode: Optional[bool] = None):
+                 gen_normal: Optional[Callable] = None, fused_decode: Optional[bool] = None,
+                 peer_collectives: Optional[bool] = None):
         import torch
         from . import sharded
         self.torch = torch
@@ -118,9 +119,18 @@ class TPDecoder:
         self.final_norm = self.gen_normal(D, s + 2, 1.0, cfg.std).to(self.device)
         lm = self.gen_weights(cfg.vocab, D, s + 3)
         r0, r1 = sharded.shard_rows(cfg.vocab, world, rank)
+        # decode-step collectives over NVLink peer memory (areas: 0 o_proj, 1 down_proj, 2 lm_head)
+        if peer_collectives is None:
+            peer_collectives = self.fused_decode and world > 1
+        self.peers = None
+        if peer_collectives and world > 1:
+            from .peer import PeerGroup
+            lm_pad = sharded.max_shard_rows(cfg.vocab, world)
+            self.peers = PeerGroup(max(D, 8 * lm_pad), areas=3, group=group, device=self.device)
         self.lm_head = sharded.RowShardedIQ4XS(lm[r0:r1].contiguous(), cfg.vocab, D, group=group, rank=rank,
                                                world=world, local_gemv=self._lm_local if matmul else None,
-                                               local_gemm=self._lm_local_t if matmul else None)
+                                               local_gemm=self._lm_local_t if matmul else None, peers=self.peers,
+                                               peer_areas=(2,))
         del lm
         self.cache = torch.zeros((cfg.layers, 2, self.hkv, cfg.max_seq, hd), dtype=torch.float16, device=self.device)
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
@@ -240,13 +250,24 @@ class TPDecoder:
             norm_gemv(L["wqkv"], L["an"], self.nqkv, b["qkv"])
             api.dec_attention_decode_q8(b["qkv"], self.cache[l, 0], self.cache[l, 1], self.cos, self.sin, self._pos,
                                         self.hq, self.hkv, q8=b["q8a"], flags=PDL)
-            delta = self._allreduce(api.gemv_q8_ex(L["wo"], b["q8a"], self.hq * hd, D, 1, out=b["o"], flags=OV))
+            delta = self._reduce_gemv(L["wo"], b["q8a"], self.hq * hd, b["o"], 0)
             norm_gemv(L["wgu"], L["fn"], 2 * self.F, b["gu"])
             api.dec_swiglu_q8(b["gu"], self.F, q8=b["q8f"], flags=PDL)
-            delta = self._allreduce(api.gemv_q8_ex(L["wd"], b["q8f"], self.F, D, 1, out=b["d"], flags=OV))
+            delta = self._reduce_gemv(L["wd"], b["q8f"], self.F, b["d"], 1)
         api.dec_residual_rmsnorm_q8(cur, self.final_norm, cfg.eps, delta=delta, h_out=b["h"], want_q8=False,
                                     flags=PDL)
         return b["h"]
+
+    def _reduce_gemv(self, W, q8, K, out, area):
+        """out [1][hidden] = the row-parallel GEMV's partial sums, summed over the ranks: over NVLink
+        peer memory (the GEMV writes into this rank's area, the pull kernel sums in rank order) or
+        with an NCCL all-reduce."""
+        api, D = self._api, self.cfg.hidden
+        if self.peers is None:
+            return self._allreduce(api.gemv_q8_ex(W, q8, K, D, 1, out=out, flags=api.FLAG_OVERLAP_PRECEDING))
+        api.gemv_q8_ex(W, q8, K, D, 1, out=self.peers.area(area, D).view(1, D), flags=api.FLAG_OVERLAP_PRECEDING)
+        self.peers.allreduce(area, D, out)
+        return out
 
     def logits(self, h):
         """h [T][hidden] -> logits [T][vocab] (row-sharded lm_head + all-gather); the result may be a
@@ -313,5 +334,9 @@ class TPDecoder:
         return out.tolist()
 
     def release(self):
-        """Drop the captured graph (before destroying the process group)."""
+        """Drop the captured graph and the peer-memory buffers (before destroying the process group)."""
         self.graph = None
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
+            self.lm_head.peers = None

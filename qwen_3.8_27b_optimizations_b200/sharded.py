@@ -11,6 +11,10 @@ and 8 ranks) gather without padding; otherwise slices are padded to the largest 
 
 The local compute goes through the C ABI (iq4xs_gemv_f32 / iq4xs_gemm_strided).  `local_gemv` /
 `local_gemm` replace it only in tests that run the host logic on CPU ranks (gloo).
+
+With a `peers` group (peer.PeerGroup) the GEMV (decode-size outputs) writes its slice straight into
+this rank's peer-memory area and the all-gather is the NVLink pull kernel of csrc/peer.cu instead of
+NCCL; the GEMM output (tens to hundreds of MB) always goes through NCCL.
 """
 from __future__ import annotations
 
@@ -41,7 +45,8 @@ class RowShardedIQ4XS:
     """
 
     def __init__(self, W_local, N: int, K: int, group=None, rank: Optional[int] = None, world: Optional[int] = None,
-                 local_gemv: Optional[Callable] = None, local_gemm: Optional[Callable] = None):
+                 local_gemv: Optional[Callable] = None, local_gemm: Optional[Callable] = None, peers=None,
+                 peer_areas=(0, 1)):
         import torch.distributed as dist
         self.dist = dist
         self.group = group
@@ -57,6 +62,9 @@ class RowShardedIQ4XS:
         self._gemv = local_gemv
         self._gemm = local_gemm
         self._bufs = {}
+        self.peers = peers if (peers is not None and self.world > 1) else None
+        self.peer_areas = tuple(peer_areas)  # used in turn: consecutive collectives need different areas
+        self._area_i = 0
         self._pkg = None
         if local_gemv is None or local_gemm is None:
             from . import api as _api  # the CUDA path; raises if the library is missing
@@ -95,6 +103,8 @@ class RowShardedIQ4XS:
         import torch
         X = X if X.dim() == 2 else X[None]
         B = X.shape[0]
+        if self.peers is not None:
+            return self._gemv_peer(X, B)
         loc = self._buf(("gemv_loc", B), (B, self.pad), X.device)
         if self.rows == self.pad:
             self._local_gemv(X, loc)
@@ -105,6 +115,20 @@ class RowShardedIQ4XS:
             return loc[:, :self.N]
         gathered = self._buf(("gemv_all", B), (self.world * B, self.pad), X.device)
         self.dist.all_gather_into_tensor(gathered, loc, group=self.group)
+        return self._assemble_bn(gathered.view(self.world, B, self.pad), B)
+
+    def _gemv_peer(self, X, B):
+        import torch
+        area = self.peer_areas[self._area_i % len(self.peer_areas)]
+        self._area_i += 1
+        loc = self.peers.area(area, B * self.pad).view(B, self.pad)
+        if self.rows == self.pad:
+            self._local_gemv(X, loc)
+        else:
+            tmp = self._buf(("gemv_tmp", B), (B, self.rows), X.device)
+            loc[:, :self.rows] = self._local_gemv(X, tmp)
+        gathered = self._buf(("gemv_all", B), (self.world * B, self.pad), X.device)
+        self.peers.allgather(area, B * self.pad, gathered)
         return self._assemble_bn(gathered.view(self.world, B, self.pad), B)
 
     def gemm_nm(self, X):

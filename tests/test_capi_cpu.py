@@ -10,6 +10,7 @@ from conftest import ROOT
 HEADER = ROOT / "include" / "iq4xs.h"
 BENCH_HEADER = ROOT / "include" / "iq4xs_bench.h"
 DECODER_HEADER = ROOT / "include" / "iq4xs_decoder.h"
+PEER_HEADER = ROOT / "include" / "iq4xs_peer.h"
 
 
 def declared_functions(header=HEADER):
@@ -35,16 +36,17 @@ def test_python_signatures_cover_header(pkg):
     assert set(pkg.SIGNATURES) == set(declared_functions())
     assert set(pkg.api.BENCH_SIGNATURES) == set(declared_functions(BENCH_HEADER))
     assert set(pkg.api.DECODER_SIGNATURES) == set(declared_functions(DECODER_HEADER))
+    assert set(pkg.api.PEER_SIGNATURES) == set(declared_functions(PEER_HEADER))
 
 
 def test_every_header_is_covered():
     assert sorted(p.name for p in (ROOT / "include").glob("*.h")) == sorted(
-        p.name for p in (HEADER, BENCH_HEADER, DECODER_HEADER))
+        p.name for p in (HEADER, BENCH_HEADER, DECODER_HEADER, PEER_HEADER))
 
 
 def test_bench_header_symbols_exported(pkg):
     L = pkg.lib()
-    for name in declared_functions(BENCH_HEADER) + declared_functions(DECODER_HEADER):
+    for name in declared_functions(BENCH_HEADER) + declared_functions(DECODER_HEADER) + declared_functions(PEER_HEADER):
         assert hasattr(L, name), name
 
 
@@ -110,3 +112,18 @@ def test_ggml_can_handle(pkg):
     assert not pkg.custom_gemv_iq4xs_can_handle(4096, 4096, 9)
     assert not pkg.custom_gemv_iq4xs_can_handle(4000, 4096, 1)
     assert not pkg.custom_gemv_iq4xs_can_handle(4096, 4096, 1, 12)  # another ggml type
+
+
+def test_peer_validation(pkg):
+    import ctypes as C
+    L = pkg.lib()
+    arr = C.c_void_p * 2
+    ok = arr(FAKE, FAKE)
+    assert L.iq4xs_peer_collective(ok, ok, FAKE, FAKE, 0, 9, 0, 64, FAKE, 0, None) == 1      # world > 8
+    assert L.iq4xs_peer_collective(ok, ok, FAKE, FAKE, 2, 2, 0, 64, FAKE, 0, None) == 1      # rank >= world
+    assert L.iq4xs_peer_collective(arr(FAKE, None), ok, FAKE, FAKE, 0, 2, 0, 64, FAKE, 0, None) == 1
+    assert L.iq4xs_peer_collective(ok, ok, FAKE, FAKE + 4, 0, 2, 0, 64, FAKE, 0, None) == 3  # counter alignment
+    assert L.iq4xs_peer_collective(ok, ok, FAKE, FAKE, 0, 2, 0, 0, FAKE, 0, None) == 1       # n <= 0
+    assert L.iq4xs_peer_collective(ok, ok, FAKE, FAKE, 0, 2, 0, 66, FAKE, 0, None) == 2      # n % 4
+    assert L.iq4xs_peer_alloc(0, C.byref(C.c_void_p())) == 1
+    assert L.iq4xs_ipc_open(None, C.byref(C.c_void_p())) == 1

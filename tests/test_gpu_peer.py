@@ -1,0 +1,139 @@
+"""Collectives over NVLink peer memory (csrc/peer.cu, peer.PeerGroup) on 2 GPUs (skipped on a
+1-GPU box): all-reduce and all-gather against NCCL on the same data, bit-exact (the all-reduce adds
+the ranks in rank order, as NCCL does for 2 ranks), repeated calls with alternating areas, the same
+collectives replayed from a CUDA graph, the row-sharded GEMV with the peer all-gather against the
+single-GPU kernel, and the tensor-parallel decoder with peer collectives against the same model
+with NCCL all-reduces.  NVLS is off; no multicast memory is used."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import sys
+    from datetime import timedelta
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root))
+    sys.path.insert(0, str(root / "tests"))
+    import torch.distributed as dist
+    from conftest import load_pkg
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    res = {}
+    try:
+        P = load_pkg()
+        dev = torch.device("cuda", rank)
+        g = P.peer.PeerGroup(1 << 16, areas=3)
+        # all-reduce / all-gather against NCCL, several rounds (the epoch counter advances)
+        ok_ar, ok_ag = True, True
+        for it in range(6):
+            n = [5120, 1000, 65536][it % 3]
+            area = it % 2
+            x = torch.randn(n, generator=torch.Generator(device=dev).manual_seed(100 * it + rank), device=dev)
+            g.area(area, n).copy_(x)
+            out = torch.empty(n, device=dev)
+            g.allreduce(area, n, out)
+            ref = x.clone()
+            dist.all_reduce(ref)
+            ok_ar &= bool(torch.equal(out, ref))
+            area = (it + 1) % 2
+            g.area(area, n).copy_(x)
+            outg = torch.empty(world * n, device=dev)
+            g.allgather(area, n, outg)
+            refg = torch.empty(world * n, device=dev)
+            dist.all_gather_into_tensor(refg, x)
+            ok_ag &= bool(torch.equal(outg, refg))
+        res["allreduce"], res["allgather"] = ok_ar, ok_ag
+        # replayed from a CUDA graph: two collectives per replay, alternating areas
+        n = 4096
+        out0, out1 = torch.empty(n, device=dev), torch.empty(n, device=dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                g.allreduce(0, n, out0)
+                g.allreduce(1, n, out1)
+        torch.cuda.current_stream().wait_stream(s)
+        ok_graph = True
+        for it in range(5):
+            a0 = torch.full((n,), float(it + 1 + rank), device=dev)
+            a1 = torch.full((n,), float(10 * it - rank), device=dev)
+            g.area(0, n).copy_(a0)
+            g.area(1, n).copy_(a1)
+            gr.replay()
+            torch.cuda.synchronize()
+            exp0 = sum(float(it + 1 + r) for r in range(world))
+            exp1 = sum(float(10 * it - r) for r in range(world))
+            ok_graph &= bool((out0 == exp0).all()) and bool((out1 == exp1).all())
+        del gr
+        res["graph"] = ok_graph
+        # row-sharded GEMV with the peer all-gather against the full-matrix kernel
+        N, K = 6144, 5120
+        W = P.random_weights(N, K, seed=77)
+        r0, r1 = P.sharded.shard_rows(N, world, rank)
+        S = P.sharded.RowShardedIQ4XS(W[r0:r1].contiguous(), N, K, peers=g)
+        ok_sh = True
+        for B in (1, 1, 3):
+            X = P.fill_normal(B * K, seed=5 + B).view(B, K)
+            Y = S.gemv(X)
+            Yf = P.gemv(W, X, N) if B == 1 else torch.cat([P.gemv(W[a:b].contiguous(), X, b - a) for a, b in
+                                                           (P.sharded.shard_rows(N, world, r) for r in range(world))], 1)
+            ok_sh &= bool(torch.equal(Y, Yf))
+        res["sharded"] = ok_sh
+        torch.cuda.synchronize()
+        g.close()
+        # decoder, tensor parallel: peer collectives vs NCCL all-reduces (same model, same prompt)
+        dec = P.decoder
+        cfg = dec.DecoderConfig(layers=2, hidden=1024, heads=8, kv_heads=2, head_dim=128, ffn=2048, vocab=3072,
+                                max_seq=40)
+        prompt = torch.randint(0, cfg.vocab, (12,), generator=torch.Generator().manual_seed(3)).to(dev)
+        lg = {}
+        for use_peer in (True, False):
+            m = dec.TPDecoder(cfg, rank=rank, world=world, seed=4, peer_collectives=use_peer)
+            m.prefill(prompt)
+            toks = m.decode(5, use_graph=True)
+            lg[use_peer] = (toks, m._last_logits.clone())
+            m.release()
+            del m
+        res["decoder_tokens"] = lg[True][0] == lg[False][0]
+        a, b = lg[True][1].double(), lg[False][1].double()
+        res["decoder_logits"] = bool((a - b).abs().max() <= 1e-3 * b.abs().max())
+        torch.cuda.synchronize()
+        q.put((rank, res, P.device_error()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_collectives_2gpu():
+    world = 2
+    ctx = mp.get_context("spawn")
+    qq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, qq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    out = [qq.get(timeout=5) for _ in range(world)]
+    for rank, res, err in out:
+        assert all(res.values()), (rank, res)
+        assert err == 0
