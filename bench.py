@@ -556,7 +556,7 @@ def main():
     maxN = max(N for _, N, _ in SHAPES)
     hx = torch.empty(max(BATCHES) * maxK, dtype=torch.float32).pin_memory()
     hx.normal_()
-    hy = torch.empty(max(BATCHES) * maxN, dtype=torch.float32).pin_memory()
+    hy = torch.empty(2 * max(BATCHES) * maxN, dtype=torch.float32).pin_memory()  # one result per slot
     dx = torch.empty(max(BATCHES) * maxK, dtype=torch.float32, device=dev)
     dy = torch.empty(max(BATCHES) * maxN, dtype=torch.float32, device=dev)
     ems = C.c_float(0.0)
@@ -630,7 +630,8 @@ def main():
                          "per_launch": per},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "custom_gemv_iq4xs_dispatch_batched from a C++ host loop, pinned host x/y"},
+                    "path": "custom_gemv_iq4xs_dispatch_batched from a C++ host loop, pinned host x/y, "
+                            "uploads and downloads on two copy streams overlapping the neighbouring GEMVs"},
             "gemm": None if gemm_tops is None else {
                 "metric": "IQ4_XS prefill GEMM TOPS (2*M*N*K / time, Q8_1 quantisation included)",
                 "value": round(gemm_tops, 1), "unit": "TOPS", "tokens": GEMM_TOKENS,

@@ -17,11 +17,14 @@ extern "C" {
 #endif
 
 /* Runs `steps` passes; one pass = for every batch size b in batches[0..nbatch) and every matrix i:
- *   cudaMemcpyAsync(dev_x <- host_x, b*K[i] floats), custom_gemv_iq4xs_dispatch_batched(W[i], dev_x,
- *   dev_y, K[i], N[i], b), cudaMemcpyAsync(host_y <- dev_y, b*N[i] floats).
- * host_x / host_y must be pinned and large enough for the largest b*K / b*N.  *ms = elapsed
- * device time between events recorded on `stream` before the first and after the last pass,
- * with the stream synchronised at the end.  Returns 0 or the first failing cudaError_t. */
+ *   cudaMemcpyAsync(dev x <- host_x, b*K[i] floats), custom_gemv_iq4xs_dispatch_batched(W[i], dev x,
+ *   dev y, K[i], N[i], b) on `stream`, cudaMemcpyAsync(host y <- dev y, b*N[i] floats).
+ * The uploads and downloads run on two copy streams of the driver and overlap the neighbouring
+ * GEMVs (two device slots: the caller's dev_x / dev_y and a second pair the driver allocates before
+ * the timed region).  host_x must be pinned and hold the largest b*K floats; host_y pinned and hold
+ * twice the largest b*N (one result per slot).  *ms = elapsed device time between events recorded
+ * on `stream` before the first upload and after the last download.  Returns 0 or the first failing
+ * cudaError_t. */
 int iq4xs_bench_e2e_gemv(const void* const* W, const int64_t* K, const int64_t* N, int nmat,
                          const int64_t* batches, int nbatch, const float* host_x, float* host_y,
                          float* dev_x, float* dev_y, int steps, cudaStream_t stream, float* ms);

@@ -405,8 +405,7 @@ cudaError_t launch_attention_g(const float* qkv, __half* kc, __half* vc, const f
                                uint32_t* err, cudaStream_t stream, bool pdl) {
     const size_t smem = attention_decode_smem(max_seq, G);
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(attention_decode_q8_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(attention_decode_q8_kernel<G>), (int)smem);
         if (e != cudaSuccess) return e;
     }
     cudaLaunchAttribute attr[1];

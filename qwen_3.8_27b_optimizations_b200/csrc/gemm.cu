@@ -609,7 +609,7 @@ cudaError_t launch_gemm(const uint8_t* W, const float* X, float* Y, int64_t K, i
     const int sms = device_sm_count() > 0 ? device_sm_count() : 148;
     const int grid = (int)std::min<int64_t>(T, sms);
 
-    e = cudaFuncSetAttribute(gemm_iq4xs_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    e = ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_iq4xs_tc_kernel), (int)kSmemBytes);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);

@@ -19,6 +19,10 @@
 //    fp32 expression; per-row sums are reduced over the 8 sub-block lanes with xor shuffles.
 //  * every mbarrier wait is bounded; a timeout records a device error code and the kernel
 //    drains its in-flight copies and returns.
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "iq4xs_device.cuh"
 #include "iq4xs_kernels.h"
 
@@ -517,7 +521,7 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
         default: break;
     }
     if (!kern) return cudaErrorInvalidConfiguration;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    cudaError_t e = ensure_dynamic_smem(kern, (int)L.total);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)imin64((int64_t)sms, a.N));
@@ -574,6 +578,22 @@ cudaError_t dispatch(int B, GemvArgs a, cudaStream_t stream, bool pdl) {
 
 bool gemv_bulk_path(const uint8_t* W, int64_t K) {
     return ((K / kQK) % 2 == 0) && ((reinterpret_cast<uintptr_t>(W) & 15u) == 0);
+}
+
+cudaError_t ensure_dynamic_smem(const void* kern, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<int, const void*>, int> done;  // (device, kernel) -> bytes allowed
+    int dev = 0, sms = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    device_limits(dev, &sms, &optin);
+    if (bytes > optin) return cudaErrorInvalidValue;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(dev, kern);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    if (e == cudaSuccess) done[key] = optin;
+    return e;
 }
 
 int device_sm_count() {

@@ -474,7 +474,7 @@ size_t gemv_mma_partial_bytes_for(int64_t K, int64_t N, int B, int sms, int smem
 template <int B, bool kDebug>
 static cudaError_t launch_mma_b(const CUtensorMap& map, GemvMmaArgs a, int smem, cudaStream_t stream, bool pdl, int grid) {
     auto kern = gemv_iq4xs_q8_mma_kernel<B, kDebug>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);

@@ -114,6 +114,10 @@ cudaError_t launch_dequantize(const uint8_t* W, float* out, int64_t K, int64_t N
 
 uint32_t* device_error_word();  // per-device error word (current device)
 
+// cudaFuncAttributeMaxDynamicSharedMemorySize for `kern` on the current device, set at most once per
+// (device, kernel) to the device's opt-in maximum: a launch does not pay a runtime call for it.
+cudaError_t ensure_dynamic_smem(const void* kern, int bytes);
+
 // Decoder step operations (decode_ops.cu).
 cudaError_t launch_residual_rmsnorm_q8(float* x, const float* delta, const float* w, int D, int T, float eps,
                                        uint8_t* q8, float* h_out, cudaStream_t stream, bool pdl);

@@ -32,9 +32,7 @@ __global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restr
 cudaError_t launch_q8_1_quantize(const float* X, uint8_t* q8, int64_t K, int64_t M, int64_t stride_m,
                                  int64_t stride_k, cudaStream_t stream, bool signal_dependents, bool pdl) {
     const int64_t total = (K / kQK8) * M;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = device_sm_count();
     const int64_t grid = std::min<int64_t>((total + 7) / 8, (int64_t)sms * 16);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
