@@ -252,13 +252,10 @@ int iq4xs_gemv_f32_ex(const void* W, const float* X, float* Y, int64_t K, int64_
     const bool overlap = (flags & IQ4XS_FLAG_OVERLAP_PRECEDING) != 0;
     GemvArgs a = make_gemv_args(W, q8, Y, K, N);
     attach_workspace(a, workspace, iq4xs_q8_1_bytes(K, B), K, N, B);
-    const bool fuse = (B == 2 || (B == 1 && K <= 6144)) && aligned(X, 16) &&
-                      gemv_bulk_path(static_cast<const uint8_t*>(W), K);
-    if (fuse) {
-        // One launch: every CTA quantises X into its own shared memory while its weight copies fly.
-        // Measured on B200: faster than the separate quantizer for batch 2 and for batch 1 up to
-        // K = 5120; for longer batch-1 rows and batches >= 3 the redundant per-CTA quantisation
-        // costs more than the PDL-chained quantizer launch it saves.
+    if (aligned(X, 16) && gemv_bulk_path(static_cast<const uint8_t*>(W), K)) {
+        // The kernel launchers quantise X inside the GEMV (every CTA into its shared memory, while
+        // its weight copies fly) when the per-CTA share is small, and otherwise launch the standalone
+        // quantizer into the workspace's Q8_1 area first (see launch_rows / launch_gemv_mma).
         a.act.mode = kActF32;
         a.act.x = X;
         return status_from(launch_gemv_q8(a, (int)B, stream, overlap));

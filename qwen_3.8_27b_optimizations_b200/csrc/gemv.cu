@@ -475,6 +475,9 @@ void device_limits(int dev, int* sms, int* smem_optin) {
 // Row-stage kernel configuration for batch B: 16 consumer warps, one row each per stage; KW warps
 // per row so that a lane holds at most SPLMAX(B) sub-blocks of activations in registers.
 constexpr int kRowNCW = 12, kRowRPW = 2;
+// fp32 sources are quantised inside the row kernel up to this K (every CTA quantises all of K; beyond
+// it the standalone quantizer launch is cheaper, measured on B200 at K = 8192 and 17408)
+constexpr int kRowFusedMaxK = 6144;
 
 template <int B, int SPL, bool kDebug>
 void* rows_kernel_ptr(bool tail) {
@@ -494,6 +497,13 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
         if (a.act.mode == kActNorm) return cudaErrorNotSupported;
         return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.tickets, a.partials, a.partial_bytes, a.K, a.N,
                                B, stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
+    }
+    if (a.act.mode == kActF32 && a.K > kRowFusedMaxK) {
+        // every CTA would quantise all of K: the standalone quantizer (programmatic launch) is cheaper
+        cudaError_t eq = launch_q8_1_quantize(a.act.x, const_cast<uint8_t*>(a.q8), a.K, B, a.K, 1, stream, true, pdl);
+        if (eq != cudaSuccess) return eq;
+        a.act.mode = kActQ8;
+        pdl = true;
     }
     const bool tail = (nsb != 32 * kw * spl);
     const int R = (NCW / kw) * RPW;

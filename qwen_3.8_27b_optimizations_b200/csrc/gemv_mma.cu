@@ -43,6 +43,8 @@ struct MmaSmem {
 };
 
 constexpr int kStageChunk = 8;                      // Q8_1 blocks per coalesced staging chunk
+constexpr int kF32MaxPkB = 12;  // fp32 sources are quantised in the kernel while pk * B <= this
+                                // (= the chunks a warp holds in registers while staging, see below)
 constexpr int kChunkWords = kStageChunk * kQ8Bytes / 4;  // 72
 
 // act: per staged part (up to 2) and sub-block: 32 lanes x uint2 (B fragment words) = 256 B;
@@ -208,7 +210,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
         const int ch0 = nsubs[0] / kStageChunk, ch1 = nsubs[1] / kStageChunk;  // chunks per token
         const int nchunks = (ch0 + ch1) * B;
         // fp32 source (batch <= 2): the fp32 values of all of this warp's chunks are requested first
-        constexpr int kF32Chunks = 3;  // >= 2 slots * 16 * pk(<= 5) / 8 * 2 tokens / kNCW
+        constexpr int kF32Chunks = 3;  // >= 2 slots * (16 * pk / 8) * B / kNCW for pk * B <= kF32MaxPkB
         float4 xf[kF32Chunks][2];
         if (a.act.mode == kActF32) {
 #pragma unroll
@@ -537,7 +539,16 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     a.act.mode = kActQ8;
     if (act && act->mode != kActQ8) {
         if (act->mode != kActF32) return cudaErrorNotSupported;
-        a.act = *act;
+        if (pk * B <= kF32MaxPkB) {
+            a.act = *act;  // every CTA quantises the <= 2 parts it touches while staging them
+        } else {
+            // Quantising 16*pk*B blocks per CTA would cost more than one more launch: the standalone
+            // quantizer writes the Q8_1 area (q8) and the GEMV waits for it (programmatic launch).
+            if (!q8) return cudaErrorInvalidValue;
+            cudaError_t eq = launch_q8_1_quantize(act->x, const_cast<uint8_t*>(q8), K, B, K, 1, stream, true, pdl);
+            if (eq != cudaSuccess) return eq;
+            pdl = true;
+        }
     }
     const int64_t U = T * parts;
     // A CTA holds the activations of at most two parts: its unit range must not exceed T units.
