@@ -202,13 +202,15 @@ __device__ __forceinline__ void lut_word(const uint32_t (&tab)[4], uint32_t x, u
     l1 = prmt(tab[0], tab[1], hi16_fma(x));
 }
 
-template <int B, int SPL, int RPW, int NCW, bool kTail, bool kDebug>
+// kSmemAct: the activations come from an fp32 source built into shared memory (build_act_q8); the
+// Q8_1-input instances do not carry that code (it costs instruction-cache misses in the hot loop).
+template <int B, int SPL, int RPW, int NCW, bool kTail, bool kDebug, bool kSmemAct>
 __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int R = a.rows_per_stage, KW = a.kw;
     const int stages = a.stages;
     const int64_t stage_bytes = (int64_t)R * a.rb;
-    const bool smem_act = a.act.mode != kActQ8;
+    constexpr bool smem_act = kSmemAct;
     const RowSmem L = gemv_row_smem(B, R, KW, stages, stage_bytes,
                                     smem_act ? (uint32_t)(B * (a.K / kQK8) * kQ8Bytes) : 0u);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
@@ -271,7 +273,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
     const uint32_t off_q = off_h + 8 + 16 * ib;
 
     grid_dependency_wait();
-    if (smem_act)
+    if constexpr (smem_act)
         build_act_q8(a.act, B, a.K, smem + L.q8_off, reinterpret_cast<float*>(smem + L.red_off), cw, NCW, lane, 1);
     uint32_t alo[SPL][B][4], ahi[SPL][B][4];
     float dx[SPL][B];
@@ -282,7 +284,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
         for (int t = 0; t < B; ++t) {
             if (!kTail || sb < nsb) {
                 uint32_t w[9];
-                if (smem_act) {
+                if constexpr (smem_act) {
                     const uint32_t* q = reinterpret_cast<const uint32_t*>(smem + L.q8_off + ((size_t)t * nsb + sb) * kQ8Bytes);
 #pragma unroll
                     for (int j = 0; j < 9; ++j) w[j] = q[j];
@@ -480,9 +482,17 @@ constexpr int kRowNCW = 12, kRowRPW = 2;
 constexpr int kRowFusedMaxK = 6144;
 
 template <int B, int SPL, bool kDebug>
-void* rows_kernel_ptr(bool tail) {
-    return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, kDebug>
-                : (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, false, kDebug>;
+void* rows_kernel_ptr(bool tail, bool smem_act) {
+    if constexpr (kDebug) {  // the debug path reads Q8_1 from global memory only
+        return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, true, false>
+                    : (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, false, true, false>;
+    } else {
+        if (smem_act)
+            return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, false, true>
+                        : (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, false, false, true>;
+        return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, false, false>
+                    : (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, false, false, false>;
+    }
 }
 
 template <int B, bool kDebug>
@@ -522,12 +532,13 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     const RowSmem L = gemv_row_smem(B, R, kw, stages, stage_bytes, q8b);
     if ((int64_t)L.total > smem_optin || stage_bytes >= (1 << 20)) return cudaErrorInvalidConfiguration;
     void* kern = nullptr;
+    const bool sa = a.act.mode != kActQ8;
     switch (spl) {
-        case 1: kern = rows_kernel_ptr<B, 1, kDebug>(tail); break;
-        case 2: kern = rows_kernel_ptr<B, 2, kDebug>(tail); break;
-        case 3: kern = B == 1 ? rows_kernel_ptr<1, 3, kDebug>(tail) : nullptr; break;
-        case 4: kern = B == 1 ? rows_kernel_ptr<1, 4, kDebug>(tail) : nullptr; break;
-        case 5: kern = B == 1 ? rows_kernel_ptr<1, 5, kDebug>(tail) : nullptr; break;
+        case 1: kern = rows_kernel_ptr<B, 1, kDebug>(tail, sa); break;
+        case 2: kern = rows_kernel_ptr<B, 2, kDebug>(tail, sa); break;
+        case 3: kern = B == 1 ? rows_kernel_ptr<1, 3, kDebug>(tail, sa) : nullptr; break;
+        case 4: kern = B == 1 ? rows_kernel_ptr<1, 4, kDebug>(tail, sa) : nullptr; break;
+        case 5: kern = B == 1 ? rows_kernel_ptr<1, 5, kDebug>(tail, sa) : nullptr; break;
         default: break;
     }
     if (!kern) return cudaErrorInvalidConfiguration;

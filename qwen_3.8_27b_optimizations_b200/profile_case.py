@@ -3,6 +3,13 @@ ncu captures.
 
     python qwen_3.8_27b_optimizations_b200/profile_case.py --N 69632 --K 5120 --B 1 --launches 3
     python qwen_3.8_27b_optimizations_b200/profile_case.py --N 17408 --K 5120 --M 2048
+    python qwen_3.8_27b_optimizations_b200/profile_case.py --op attention --pos 512
+    python qwen_3.8_27b_optimizations_b200/profile_case.py --op sweep
+
+--op attention: the decoder's decode attention kernel (64 query / 8 KV heads of 128, KV cache of
+640 positions, the token at --pos).  --op sweep: one step of the benchmark's decode GEMV sweep
+(q, k, v, o, gate|up, down at batch 1, 2, 4, 8 through the fp32 entry point), launched eagerly so
+that a profiler lists every kernel.
 
 Weights are synthetic IQ4_XS (N(0, 0.02) quantised on the device), activations N(0, 1), quantised
 to Q8_1 once up front, so the launches of interest are `--launches` GEMV kernels after `--warmup`
@@ -35,8 +42,14 @@ def main() -> int:
     ap.add_argument("--M", type=int, default=0, help="tokens: run the prefill GEMM instead of the GEMV")
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--op", default="gemv", choices=["gemv", "attention", "sweep"])
+    ap.add_argument("--pos", type=int, default=512)
     args = ap.parse_args()
     P = _load_pkg()
+    if args.op == "attention":
+        return attention_case(P, args.pos, args.launches, args.warmup)
+    if args.op == "sweep":
+        return sweep_case(P, args.launches, args.warmup)
     N, K, B = args.N, args.K, args.B
     W = P.random_weights(N, K, seed=7)
     if args.M:
@@ -81,6 +94,60 @@ def gemm_case(P, W, N, K, M, launches, warmup):
     us = e0.elapsed_time(e1) * 1e3 / max(launches, 1)
     ops = 2 * M * N * K
     print(json.dumps({"N": N, "K": K, "M": M, "us_per_call": round(us, 2), "tops": round(ops / (us * 1e-6) / 1e12, 1)}))
+    return 0
+
+
+def attention_case(P, pos, launches, warmup):
+    hq, hkv, hd, max_seq = 64, 8, 128, 640
+    g = torch.Generator(device="cuda").manual_seed(3)
+    qkv = torch.randn((1, (hq + 2 * hkv) * hd), generator=g, device="cuda")
+    kc = torch.randn((hkv, max_seq, hd), generator=g, device="cuda").half()
+    vc = torch.randn((hkv, max_seq, hd), generator=g, device="cuda").half()
+    inv = 1.0 / (1.0e6 ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
+    ang = torch.arange(max_seq, dtype=torch.float64)[:, None] * inv[None, :]
+    cos, sin = torch.cos(ang).float().cuda(), torch.sin(ang).float().cuda()
+    p = torch.tensor([pos], dtype=torch.long, device="cuda")
+    q8 = torch.empty((1, hq * hd // 32 * 36), dtype=torch.uint8, device="cuda")
+    run = lambda: P.dec_attention_decode_q8(qkv, kc, vc, cos, sin, p, hq, hkv, q8=q8)
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(launches):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    if P.device_error():
+        raise RuntimeError(f"device error word {P.device_error()}")
+    kv_bytes = 2 * hkv * (pos + 1) * hd * 2
+    print(json.dumps({"op": "attention", "pos": pos, "us_per_launch": round(e0.elapsed_time(e1) * 1e3 / max(launches, 1), 2),
+                      "kv_bytes": kv_bytes}))
+    return 0
+
+
+def sweep_case(P, steps, warmup):
+    shapes = [(8192, 5120), (1024, 5120), (1024, 5120), (5120, 8192), (34816, 5120), (5120, 17408)]
+    Ws = [P.random_weights(N, K, seed=i) for i, (N, K) in enumerate(shapes)]
+    Xs = {B: P.fill_normal(B * 17408, seed=B) for B in (1, 2, 4, 8)}
+    Ys = {B: torch.empty(B * 34816, dtype=torch.float32, device="cuda") for B in (1, 2, 4, 8)}
+
+    def step():
+        for B in (1, 2, 4, 8):
+            for W, (N, K) in zip(Ws, shapes):
+                P.gemv(W, Xs[B][:B * K].view(B, K), N, out=Ys[B][:B * N].view(B, N), flags=P.FLAG_OVERLAP_PRECEDING)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if P.device_error():
+        raise RuntimeError(f"device error word {P.device_error()}")
+    print(json.dumps({"op": "sweep", "us_per_step_eager": round(e0.elapsed_time(e1) * 1e3 / max(steps, 1), 1)}))
     return 0
 
 
