@@ -129,7 +129,9 @@ __device__ __forceinline__ bool wait_sleep(uint64_t* bar, uint32_t parity, volat
 }
 }  // namespace
 
-template <int B, bool kDebug>
+// kF32: the activations are quantised from fp32 while staging (batch <= 2 and small parts); the
+// Q8_1-input instances do not carry that code.
+template <int B, bool kDebug, bool kF32>
 __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
     gemv_iq4xs_q8_mma_kernel(const __grid_constant__ CUtensorMap tmap, const GemvMmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -212,7 +214,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
         // fp32 source (batch <= 2): the fp32 values of all of this warp's chunks are requested first
         constexpr int kF32Chunks = 3;  // >= 2 slots * (16 * pk / 8) * B / kNCW for pk * B <= kF32MaxPkB
         float4 xf[kF32Chunks][2];
-        if (a.act.mode == kActF32) {
+        if constexpr (kF32) {
 #pragma unroll
             for (int k = 0; k < kF32Chunks; ++k) {
                 const int q = cw + k * kNCW;
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
             const int slot = r < ch0 ? 0 : 1;
             const int sbl0 = (r - slot * ch0) * kStageChunk;
             const int sb = (pfirst + slot) * pk * 16 + sbl0;
-            if (a.act.mode == kActF32) {  // quantise the chunk's 8 blocks from fp32 into the scratch
+            if constexpr (kF32) {  // quantise the chunk's 8 blocks from fp32 into the scratch
                 float4 x0 = xf[0][0], x1 = xf[0][1];
 #pragma unroll
                 for (int k = 1; k < kF32Chunks; ++k)
@@ -475,7 +477,9 @@ size_t gemv_mma_partial_bytes_for(int64_t K, int64_t N, int B, int sms, int smem
 
 template <int B, bool kDebug>
 static cudaError_t launch_mma_b(const CUtensorMap& map, GemvMmaArgs a, int smem, cudaStream_t stream, bool pdl, int grid) {
-    auto kern = gemv_iq4xs_q8_mma_kernel<B, kDebug>;
+    constexpr bool kF32Ok = !kDebug && B <= kF32MaxPkB;
+    auto kern = (kF32Ok && a.act.mode == kActF32) ? gemv_iq4xs_q8_mma_kernel<B, kDebug, kF32Ok>
+                                                   : gemv_iq4xs_q8_mma_kernel<B, kDebug, false>;
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
