@@ -97,11 +97,12 @@ __device__ __forceinline__ float4 add4_rn(float4 a, float4 b) {
     return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
 }
 
+template <int kAct>
 __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K, uint8_t* q8s, float* red, int cw,
                                              int ncw, int lane, int bar_id) {
     const int nq = B * K / 128;
     const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (act.mode == kActNorm) {
+    if constexpr (kAct == kActNorm) {
         float4 v0[kActQ], w0[kActQ];
         float ss = 0.0f;
         for (int base = cw; base < nq; base += ncw * kActQ) {
@@ -202,15 +203,16 @@ __device__ __forceinline__ void lut_word(const uint32_t (&tab)[4], uint32_t x, u
     l1 = prmt(tab[0], tab[1], hi16_fma(x));
 }
 
-// kSmemAct: the activations come from an fp32 source built into shared memory (build_act_q8); the
-// Q8_1-input instances do not carry that code (it costs instruction-cache misses in the hot loop).
-template <int B, int SPL, int RPW, int NCW, bool kTail, bool kDebug, bool kSmemAct>
+// kAct: where the activations come from (ActMode).  kActF32 / kActNorm build them into shared memory
+// (build_act_q8); each instance carries only its own prologue (code size costs instruction-cache
+// misses in the hot loop).
+template <int B, int SPL, int RPW, int NCW, bool kTail, bool kDebug, int kAct>
 __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int R = a.rows_per_stage, KW = a.kw;
     const int stages = a.stages;
     const int64_t stage_bytes = (int64_t)R * a.rb;
-    constexpr bool smem_act = kSmemAct;
+    constexpr bool smem_act = kAct != kActQ8;
     const RowSmem L = gemv_row_smem(B, R, KW, stages, stage_bytes,
                                     smem_act ? (uint32_t)(B * (a.K / kQK8) * kQ8Bytes) : 0u);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
@@ -274,7 +276,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
 
     grid_dependency_wait();
     if constexpr (smem_act)
-        build_act_q8(a.act, B, a.K, smem + L.q8_off, reinterpret_cast<float*>(smem + L.red_off), cw, NCW, lane, 1);
+        build_act_q8<kAct>(a.act, B, a.K, smem + L.q8_off, reinterpret_cast<float*>(smem + L.red_off), cw, NCW, lane, 1);
     uint32_t alo[SPL][B][4], ahi[SPL][B][4];
     float dx[SPL][B];
 #pragma unroll
@@ -481,17 +483,20 @@ constexpr int kRowNCW = 12, kRowRPW = 2;
 // it the standalone quantizer launch is cheaper, measured on B200 at K = 8192 and 17408)
 constexpr int kRowFusedMaxK = 6144;
 
+template <int B, int SPL, bool kDebug, int kAct>
+void* rows_kernel_ptr_t(bool tail) {
+    return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, kDebug, kAct>
+                : (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, false, kDebug, kAct>;
+}
+
 template <int B, int SPL, bool kDebug>
-void* rows_kernel_ptr(bool tail, bool smem_act) {
+void* rows_kernel_ptr(bool tail, int mode) {
     if constexpr (kDebug) {  // the debug path reads Q8_1 from global memory only
-        return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, true, false>
-                    : (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, false, true, false>;
+        return rows_kernel_ptr_t<B, SPL, true, kActQ8>(tail);
     } else {
-        if (smem_act)
-            return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, false, true>
-                        : (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, false, false, true>;
-        return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, false, false>
-                    : (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, false, false, false>;
+        if (mode == kActNorm) return rows_kernel_ptr_t<B, SPL, false, kActNorm>(tail);
+        if (mode == kActF32) return rows_kernel_ptr_t<B, SPL, false, kActF32>(tail);
+        return rows_kernel_ptr_t<B, SPL, false, kActQ8>(tail);
     }
 }
 
@@ -532,7 +537,7 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     const RowSmem L = gemv_row_smem(B, R, kw, stages, stage_bytes, q8b);
     if ((int64_t)L.total > smem_optin || stage_bytes >= (1 << 20)) return cudaErrorInvalidConfiguration;
     void* kern = nullptr;
-    const bool sa = a.act.mode != kActQ8;
+    const int sa = a.act.mode;
     switch (spl) {
         case 1: kern = rows_kernel_ptr<B, 1, kDebug>(tail, sa); break;
         case 2: kern = rows_kernel_ptr<B, 2, kDebug>(tail, sa); break;
