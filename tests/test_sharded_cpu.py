@@ -93,3 +93,76 @@ def test_shard_rows_properties():
             sizes = [b - a for a, b in rs]
             assert max(sizes) - min(sizes) <= 16
     assert sh.shard_rows(152064, 8, 3) == (57024, 76032)
+
+
+class _FakePeers:
+    """peer.PeerGroup's interface on CPU ranks: the areas are local tensors and the all-gather is
+    gloo's, so the row-sharded GEMV's peer path (area alternation, padded slices, assembly) runs
+    here; the NVLink kernel itself is covered on 2 GPUs by test_gpu_peer.py."""
+
+    def __init__(self, area_floats, areas, world):
+        self.bufs = [torch.zeros(area_floats) for _ in range(areas)]
+        self.world = world
+        self.used = []
+
+    def area(self, i, n):
+        self.used.append(i)
+        return self.bufs[i][:n]
+
+    def allgather(self, i, n, out):
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(out.view(-1)[:self.world * n], self.bufs[i][:n].contiguous())
+        return out
+
+
+def _peer_worker(rank, world, port, N, K, B, q):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root))
+    sys.path.insert(0, str(root / "tests"))
+    import torch.distributed as dist
+    from conftest import load_pkg
+    from oracle import oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        sh = load_pkg().sharded
+        W = O.random_blocks(K, N, 4321)
+        r0, r1 = sh.shard_rows(N, world, rank)
+
+        def gemv_fn(Wl, X):
+            Xn = X.numpy()
+            Y64, _ = O.matmul_q8(Wl.numpy(), O.quantize_q8_1(Xn), K, Wl.shape[0], Xn.shape[0])
+            return torch.from_numpy(Y64.astype(np.float32))
+
+        peers = _FakePeers(B * sh.max_shard_rows(N, world), 2, world)
+        S = sh.RowShardedIQ4XS(torch.from_numpy(W[r0:r1].copy()), N, K, local_gemv=gemv_fn, local_gemm=gemv_fn,
+                               peers=peers)
+        ok = True
+        for it in range(3):
+            X = torch.from_numpy(O.normal(B * K, 70 + it).reshape(B, K))
+            Y = S.gemv(X)
+            full, _ = O.matmul_q8(W, O.quantize_q8_1(X.numpy()), K, N, B)
+            ok &= tuple(Y.shape) == (B, N) and np.array_equal(Y.numpy(), full.astype(np.float32))
+        q.put((rank, ok, peers.used))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,N", [(2, 96), (3, 200)])
+def test_row_sharded_peer_path_gloo(world, N):
+    K, B = 512, 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, N, K, B, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = sorted(q.get(timeout=5) for _ in range(world))
+    assert all(ok for _, ok, _ in res), res
+    assert all(used == [0, 1, 0] for _, _, used in res)  # consecutive collectives alternate areas
