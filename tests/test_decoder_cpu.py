@@ -17,12 +17,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def tiny_cfg(dec):
-    return dec.DecoderConfig(layers=2, hidden=512, heads=8, kv_heads=2, head_dim=128, ffn=1024, vocab=1000,
-                             max_seq=40)
+def tiny_cfg(dec, heads=8, kv_heads=2, ffn=1024):
+    return dec.DecoderConfig(layers=2, hidden=512, heads=heads, kv_heads=kv_heads, head_dim=128, ffn=ffn,
+                             vocab=1000, max_seq=40)
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, cfg_kw=None):
     import sys
     from pathlib import Path
     root = Path(__file__).resolve().parents[1]
@@ -49,7 +49,7 @@ def _worker(rank, world, port, q):
         def gen_normal(n, s, mean, std):
             return torch.from_numpy(O.normal(n, s, mean, std))
 
-        m = dec.TPDecoder(tiny_cfg(dec), rank=rank, world=world, seed=3, device="cpu", matmul=matmul,
+        m = dec.TPDecoder(tiny_cfg(dec, **(cfg_kw or {})), rank=rank, world=world, seed=3, device="cpu", matmul=matmul,
                           gen_weights=gen_weights, gen_normal=gen_normal)
         prompt = torch.from_numpy(np.random.default_rng(7).integers(0, 1000, 12)).long()
         first, lg = m.prefill(prompt)
@@ -59,11 +59,11 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def _run(world):
+def _run(world, cfg_kw=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, cfg_kw)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -80,3 +80,14 @@ def test_tp2_matches_tp1():
         assert np.max(np.abs(lg - one[2])) <= 1e-3 * np.max(np.abs(one[2]))
         assert toks[:4] == one[1][:4], (toks, one[1])
     assert two[0][1] == two[1][1]      # both ranks hold the same tokens
+
+
+def test_tp4_matches_tp1():
+    """Four ranks: one KV head and four query heads each, an FFN of 5 super-block pairs split
+    unevenly (2/1/1/1), the lm_head over 4 shards."""
+    kw = dict(heads=16, kv_heads=4, ffn=2560)
+    one = _run(1, kw)[0]
+    four = _run(4, kw)
+    for rank, toks, lg, last in four:
+        assert np.max(np.abs(lg - one[2])) <= 1e-3 * np.max(np.abs(one[2]))
+        assert toks[:4] == one[1][:4]
