@@ -166,6 +166,8 @@ def sharded_sweep(P, dev, stream, rank: int, world: int, barrier, reps: int = 5)
         for op, M in (("gemv", 1), ("gemm", 2048)):
             X = P.fill_normal(M * K, seed=31 + M).view(M, K)
             fn = (lambda: S.gemv(X)) if op == "gemv" else (lambda: S.gemm_nm(X))
+            torch.cuda.synchronize()
+            barrier()  # the first collective of a call waits for every rank
             with torch.cuda.stream(stream):
                 for _ in range(3):
                     fn()

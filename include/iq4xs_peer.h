@@ -20,7 +20,7 @@
  * src[q] and rflags[q] are rank q's data area and flag array as mapped on this rank (src[rank],
  * rflags[rank] this rank's own).  n % 4 == 0; src[q] and out 16-byte aligned.  Every rank must issue the same collectives in the same order;
  * consecutive collectives must use different data areas (alternate two).  A wait that exceeds
- * spin_limit polls (0: about a second) records device error 6 (iq4xs_device_error) and returns.
+ * spin_limit polls (0: a few seconds) records device error 6 (iq4xs_device_error) and returns.
  * Graph-capture safe.
  */
 #ifndef IQ4XS_PEER_H

@@ -182,7 +182,7 @@ int iq4xs_peer_collective(const float* const* src, uint32_t* const* rflags, uint
     a.rank = rank;
     a.world = world;
     a.gather = gather ? 1 : 0;
-    a.spin_limit = spin_limit ? spin_limit : (1u << 21);
+    a.spin_limit = spin_limit ? spin_limit : (1u << 24);  // a few seconds: ranks may arrive skewed
     a.err = device_error_word();
     if (!a.err) return IQ4XS_ERR_CUDA;
     const int64_t total4 = (gather ? n * world : n) / 4;
