@@ -555,12 +555,13 @@ def main():
     Ks = (C.c_int64 * len(SHAPES))(*[K for _, _, K in SHAPES])
     Ns = (C.c_int64 * len(SHAPES))(*[N for _, N, _ in SHAPES])
     Bs = (C.c_int64 * len(BATCHES))(*BATCHES)
-    maxN = max(N for _, N, _ in SHAPES)
-    hx = torch.empty(max(BATCHES) * maxK, dtype=torch.float32).pin_memory()
+    nx = int(L.iq4xs_bench_e2e_floats(Ks, len(SHAPES), Bs, len(BATCHES)))  # one pass's inputs, concatenated
+    ny = int(L.iq4xs_bench_e2e_floats(Ns, len(SHAPES), Bs, len(BATCHES)))  # one pass's results
+    hx = torch.empty(nx, dtype=torch.float32).pin_memory()
     hx.normal_()
-    hy = torch.empty(2 * max(BATCHES) * maxN, dtype=torch.float32).pin_memory()  # one result per slot
-    dx = torch.empty(max(BATCHES) * maxK, dtype=torch.float32, device=dev)
-    dy = torch.empty(max(BATCHES) * maxN, dtype=torch.float32, device=dev)
+    hy = torch.empty(ny, dtype=torch.float32).pin_memory()
+    dx = torch.empty(nx, dtype=torch.float32, device=dev)
+    dy = torch.empty(ny, dtype=torch.float32, device=dev)
     ems = C.c_float(0.0)
     rc = L.iq4xs_bench_e2e_gemv(wptrs, Ks, Ns, len(SHAPES), Bs, len(BATCHES), hx.data_ptr(), hy.data_ptr(),
                                 dx.data_ptr(), dy.data_ptr(), max(args.warmup, 3), stream.cuda_stream, C.byref(ems))
@@ -575,8 +576,7 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_gbs = world * sb * e2e_steps / (float(t.item()) * 1e-3) / 1e9
-    h2d = sum(4 * B * K for B in BATCHES for _, _, K in SHAPES)
-    d2h = sum(4 * B * N for B in BATCHES for _, N, _ in SHAPES)
+    h2d, d2h = 4 * nx, 4 * ny  # the bytes of the two copies of every step
 
     gemm_per, gemm_tops, sharded, decoder = [], None, [], None
     bpeak, bpeak_kind = bf16_peak()
@@ -632,8 +632,9 @@ def main():
                          "per_launch": per},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "custom_gemv_iq4xs_dispatch_batched from a C++ host loop, pinned host x/y, "
-                            "uploads and downloads on two copy streams overlapping the neighbouring GEMVs"},
+                    "path": "custom_gemv_iq4xs_dispatch_batched from a C++ host loop, pinned host x/y: each step "
+                            "uploads its activations in one copy and downloads its results in one copy, on two copy "
+                            "streams overlapping the neighbouring steps' GEMVs"},
             "gemm": None if gemm_tops is None else {
                 "metric": "IQ4_XS prefill GEMM TOPS (2*M*N*K / time, Q8_1 quantisation included)",
                 "value": round(gemm_tops, 1), "unit": "TOPS", "tokens": GEMM_TOKENS,

@@ -16,15 +16,20 @@
 extern "C" {
 #endif
 
-/* Runs `steps` passes; one pass = for every batch size b in batches[0..nbatch) and every matrix i:
- *   cudaMemcpyAsync(dev x <- host_x, b*K[i] floats), custom_gemv_iq4xs_dispatch_batched(W[i], dev x,
- *   dev y, K[i], N[i], b) on `stream`, cudaMemcpyAsync(host y <- dev y, b*N[i] floats).
- * The uploads and downloads run on two copy streams of the driver and overlap the neighbouring
- * GEMVs (two device slots: the caller's dev_x / dev_y and a second pair the driver allocates before
- * the timed region).  host_x must be pinned and hold the largest b*K floats; host_y pinned and hold
- * twice the largest b*N (one result per slot).  *ms = elapsed device time between events recorded
- * on `stream` before the first upload and after the last download.  Returns 0 or the first failing
- * cudaError_t. */
+/* Floats of one pass's concatenated layout for row lengths L[0..nmat): the sum over every batch
+ * size b and matrix i of b*L[i] rounded up to a multiple of 64 (each call's segment starts on a
+ * 256-byte boundary).  L = K gives the input layout, L = N the output layout. */
+int64_t iq4xs_bench_e2e_floats(const int64_t* L, int nmat, const int64_t* batches, int nbatch);
+
+/* Runs `steps` passes; one pass = one cudaMemcpyAsync of the pass's inputs (dev x <- host_x, the
+ * input layout), then for every batch size b in batches[0..nbatch) and every matrix i
+ * custom_gemv_iq4xs_dispatch_batched(W[i], x segment, y segment, K[i], N[i], b) on `stream`, then
+ * one cudaMemcpyAsync of the pass's results (host_y <- dev y, the output layout).  The copies run on
+ * two copy streams of the driver and overlap the neighbouring passes' GEMVs (two device slots: the
+ * caller's dev_x / dev_y and a second pair the driver allocates before the timed region).  host_x /
+ * dev_x hold the input layout, host_y / dev_y the output layout; host buffers pinned.  *ms =
+ * elapsed device time between events recorded on `stream` before the first upload and after the
+ * last download.  Returns 0 or the first failing cudaError_t. */
 int iq4xs_bench_e2e_gemv(const void* const* W, const int64_t* K, const int64_t* N, int nmat,
                          const int64_t* batches, int nbatch, const float* host_x, float* host_y,
                          float* dev_x, float* dev_y, int steps, cudaStream_t stream, float* ms);

@@ -63,6 +63,7 @@ SIGNATURES = {
 # include/iq4xs_bench.h (measurement driver, not the matmul path)
 BENCH_SIGNATURES = {
     "iq4xs_bench_e2e_gemv": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i, _vp, C.POINTER(C.c_float)]),
+    "iq4xs_bench_e2e_floats": (_i64, [_vp, _i, _vp, _i]),
 }
 
 # include/iq4xs_decoder.h (the decoder-step operations around the GEMVs)

@@ -127,3 +127,13 @@ def test_peer_validation(pkg):
     assert L.iq4xs_peer_collective(ok, ok, FAKE, FAKE, 0, 2, 0, 66, FAKE, 0, None) == 2      # n % 4
     assert L.iq4xs_peer_alloc(0, C.byref(C.c_void_p())) == 1
     assert L.iq4xs_ipc_open(None, C.byref(C.c_void_p())) == 1
+
+
+def test_bench_pass_layout(pkg):
+    """The e2e driver's concatenated layout: every call's segment rounded up to 64 floats."""
+    import ctypes as C
+    L = pkg.lib()
+    lens = (C.c_int64 * 3)(5120, 100, 8)
+    bs = (C.c_int64 * 2)(1, 3)
+    want = sum((b * n + 63) // 64 * 64 for b in (1, 3) for n in (5120, 100, 8))
+    assert L.iq4xs_bench_e2e_floats(lens, 3, bs, 2) == want
