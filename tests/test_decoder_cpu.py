@@ -4,17 +4,9 @@ Matmuls are the FP64 oracle of the quantised pipeline (injected), weights are qu
 oracle; the test covers the head / FFN partition, the K-slicing of the row-parallel layers, the
 all-reduces, the KV cache and RoPE/attention indexing, and the sharded lm_head."""
 import os
-import socket
 
 import numpy as np
 import torch
-import torch.multiprocessing as mp
-
-
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
 
 
 def tiny_cfg(dec, heads=8, kv_heads=2, ffn=1024):
@@ -22,7 +14,7 @@ def tiny_cfg(dec, heads=8, kv_heads=2, ffn=1024):
                              vocab=1000, max_seq=40)
 
 
-def _worker(rank, world, port, q, cfg_kw=None):
+def _worker(rank, world, port, q, cfg_kw=None, exact=False):
     import sys
     from pathlib import Path
     root = Path(__file__).resolve().parents[1]
@@ -40,6 +32,8 @@ def _worker(rank, world, port, q, cfg_kw=None):
         def matmul(W, X, N):
             Xn = np.ascontiguousarray(X.numpy(), dtype=np.float32)
             K = Xn.shape[1]
+            if exact:  # unquantised activations, FP64 sums: no Q8_1 rounding flips between partitions
+                return torch.from_numpy(O.matmul_f64(W.numpy(), Xn, K, N, Xn.shape[0]))
             Y, _ = O.matmul_q8(W.numpy(), O.quantize_q8_1(Xn), K, N, Xn.shape[0])
             return torch.from_numpy(Y.astype(np.float32))
 
@@ -59,17 +53,11 @@ def _worker(rank, world, port, q, cfg_kw=None):
         dist.destroy_process_group()
 
 
-def _run(world, cfg_kw=None):
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, cfg_kw)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=600)
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    return sorted((q.get(timeout=5) for _ in range(world)), key=lambda r: r[0])
+def _run(world, cfg_kw=None, exact=False):
+    from conftest import run_ranks
+    out, codes = run_ranks(_worker, world, lambda r, port, q: (r, world, port, q, cfg_kw, exact))
+    assert all(c == 0 for c in codes), codes
+    return sorted(out, key=lambda r: r[0])
 
 
 def test_tp2_matches_tp1():
@@ -91,3 +79,19 @@ def test_tp4_matches_tp1():
     for rank, toks, lg, last in four:
         assert np.max(np.abs(lg - one[2])) <= 1e-3 * np.max(np.abs(one[2]))
         assert toks[:4] == one[1][:4]
+
+
+def test_tp8_matches_tp1():
+    """Eight ranks, as on a full 8-GPU box: one KV head and four query heads each, an FFN of 9
+    super-block pairs split 2/1/1/1/1/1/1/1, the lm_head over 8 shards.  The matmul is the unquantised
+    FP64 one, so the partitioning must reproduce TP=1 up to fp32 rounding of the partial sums (with
+    Q8_1 activations a partial sum that lands on the other side of a rounding boundary flips one
+    quant, and two layers amplify that to ~1e-2 of the largest logit)."""
+    kw = dict(heads=32, kv_heads=8, ffn=4608)
+    one = _run(1, kw, exact=True)[0]
+    eight = _run(8, kw, exact=True)
+    for rank, toks, lg, last in eight:
+        assert np.max(np.abs(lg - one[2])) <= 1e-5 * np.max(np.abs(one[2]))
+        assert np.max(np.abs(last - one[3])) <= 1e-5 * np.max(np.abs(one[3]))
+        assert toks == one[1]
+    assert all(r[1] == eight[0][1] for r in eight)

@@ -5,19 +5,11 @@ collectives replayed from a CUDA graph, the row-sharded GEMV with the peer all-g
 single-GPU kernel, and the tensor-parallel decoder with peer collectives against the same model
 with NCCL all-reduces.  NVLS is off; no multicast memory is used."""
 import os
-import socket
 
 import pytest
 import torch
-import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
-
-
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
 
 
 def _worker(rank, world, port, q):
@@ -124,16 +116,10 @@ def _worker(rank, world, port, q):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_peer_collectives_2gpu():
     world = 2
-    ctx = mp.get_context("spawn")
-    qq = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, qq)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    out = [qq.get(timeout=5) for _ in range(world)]
+    from conftest import run_ranks
+    out, codes = run_ranks(_worker, world, lambda r, port, q: (r, world, port, q), timeout=300)
+    assert all(c == 0 for c in codes), codes
+    assert len(out) == world
     for rank, res, err in out:
         assert all(res.values()), (rank, res)
         assert err == 0

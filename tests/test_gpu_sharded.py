@@ -2,20 +2,12 @@
 otherwise 1), against the single-GPU kernels on the full matrix: the GEMM and the batch-1 GEMV
 are per-row identical (bit-exact), batched GEMV partial sums may be split differently (tolerance)."""
 import os
-import socket
 
 import numpy as np
 import pytest
 import torch
-import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
-
-
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
 
 
 def _worker(rank, world, port, q):
@@ -63,16 +55,10 @@ def _worker(rank, world, port, q):
 
 def test_row_sharded_nccl():
     world = min(2, torch.cuda.device_count())
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    out = [q.get(timeout=5) for _ in range(world)]
+    from conftest import run_ranks
+    out, codes = run_ranks(_worker, world, lambda r, port, q: (r, world, port, q), timeout=300)
+    assert all(c == 0 for c in codes), codes
+    assert len(out) == world
     for rank, res, err in out:
         assert all(res), (rank, res)
         assert err == 0

@@ -5,18 +5,10 @@ padding of uneven shards and the assembly of the gathered output, not the CUDA k
 covered on the GPU by test_gpu_sharded.py).
 """
 import os
-import socket
 
 import numpy as np
 import pytest
 import torch
-import torch.multiprocessing as mp
-
-
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
 
 
 def _worker(rank, world, port, N, K, B, M, q):
@@ -61,16 +53,10 @@ def _worker(rank, world, port, N, K, B, M, q):
 @pytest.mark.parametrize("world,N", [(2, 96), (2, 100), (3, 200)])
 def test_row_sharded_gather_gloo(world, N):
     K, B, M = 512, 3, 5
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, N, K, B, M, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=240)
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    res = sorted(q.get(timeout=5) for _ in range(world))
+    from conftest import run_ranks
+    out, codes = run_ranks(_worker, world, lambda r, port, q: (r, world, port, N, K, B, M, q), timeout=240)
+    assert all(c == 0 for c in codes), codes
+    res = sorted(out)
     assert all(ok for _, ok, _ in res), res
     # the shards tile [0, N) with whole 16-row tiles
     bounds = [b for _, _, b in res]
@@ -154,15 +140,9 @@ def _peer_worker(rank, world, port, N, K, B, q):
 @pytest.mark.parametrize("world,N", [(2, 96), (3, 200)])
 def test_row_sharded_peer_path_gloo(world, N):
     K, B = 512, 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, N, K, B, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=240)
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    res = sorted(q.get(timeout=5) for _ in range(world))
+    from conftest import run_ranks
+    out, codes = run_ranks(_peer_worker, world, lambda r, port, q: (r, world, port, N, K, B, q), timeout=240)
+    assert all(c == 0 for c in codes), codes
+    res = sorted(out)
     assert all(ok for _, ok, _ in res), res
     assert all(used == [0, 1, 0] for _, _, used in res)  # consecutive collectives alternate areas
