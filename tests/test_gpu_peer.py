@@ -1,9 +1,10 @@
-"""Collectives over NVLink peer memory (csrc/peer.cu, peer.PeerGroup) on 2 GPUs (skipped on a
-1-GPU box): all-reduce and all-gather against NCCL on the same data, bit-exact (the all-reduce adds
-the ranks in rank order, as NCCL does for 2 ranks), repeated calls with alternating areas, the same
-collectives replayed from a CUDA graph, the row-sharded GEMV with the peer all-gather against the
-single-GPU kernel, and the tensor-parallel decoder with peer collectives against the same model
-with NCCL all-reduces.  NVLS is off; no multicast memory is used."""
+"""Collectives over NVLink peer memory (csrc/peer.cu, peer.PeerGroup) on 2, 4 and 8 GPUs (each
+skipped on a box with fewer): all-reduce and all-gather bit-exact against the rank-order sum and the
+concatenation of the ranks' inputs (and within fp32 rounding of NCCL's all-reduce), repeated calls
+with alternating areas, the same collectives replayed from a CUDA graph, the row-sharded GEMV with
+the peer all-gather against the single-GPU kernel, and the tensor-parallel decoder with peer
+collectives against the same model with NCCL all-reduces.  NVLS is off; no multicast memory is
+used."""
 import os
 
 import pytest
@@ -41,9 +42,14 @@ def _worker(rank, world, port, q):
             g.area(area, n).copy_(x)
             out = torch.empty(n, device=dev)
             g.allreduce(area, n, out)
-            ref = x.clone()
-            dist.all_reduce(ref)
-            ok_ar &= bool(torch.equal(out, ref))
+            parts = torch.empty(world * n, device=dev)
+            dist.all_gather_into_tensor(parts, x)
+            ref = parts[:n].clone()
+            for r in range(1, world):  # rank order, one rounded fp32 add per rank
+                ref += parts[r * n:(r + 1) * n]
+            nccl = x.clone()
+            dist.all_reduce(nccl)  # NCCL's order is its own beyond 2 ranks
+            ok_ar &= bool(torch.equal(out, ref)) and bool(torch.allclose(out, nccl, rtol=1e-5, atol=1e-5))
             area = (it + 1) % 2
             g.area(area, n).copy_(x)
             outg = torch.empty(world * n, device=dev)
@@ -93,8 +99,9 @@ def _worker(rank, world, port, q):
         g.close()
         # decoder, tensor parallel: peer collectives vs NCCL all-reduces (same model, same prompt)
         dec = P.decoder
-        cfg = dec.DecoderConfig(layers=2, hidden=1024, heads=8, kv_heads=2, head_dim=128, ffn=2048, vocab=3072,
-                                max_seq=40)
+        # one KV head group of 4 query heads and 2 FFN super-block pairs per rank
+        cfg = dec.DecoderConfig(layers=2, hidden=1024, heads=4 * world, kv_heads=world, head_dim=128,
+                                ffn=1024 * world, vocab=3072, max_seq=40)
         prompt = torch.randint(0, cfg.vocab, (12,), generator=torch.Generator().manual_seed(3)).to(dev)
         lg = {}
         for use_peer in (True, False):
@@ -104,22 +111,27 @@ def _worker(rank, world, port, q):
             lg[use_peer] = (toks, m._last_logits.clone())
             m.release()
             del m
-        res["decoder_tokens"] = lg[True][0] == lg[False][0]
         a, b = lg[True][1].double(), lg[False][1].double()
-        res["decoder_logits"] = bool((a - b).abs().max() <= 1e-3 * b.abs().max())
+        if world == 2:  # both collectives add the two ranks' partial sums with one rounded add
+            res["decoder_tokens"] = lg[True][0] == lg[False][0]
+            res["decoder_logits"] = bool((a - b).abs().max() <= 1e-3 * b.abs().max())
+        else:  # other summation orders flip the odd Q8_1 rounding of the next layer's activations
+            res["decoder_logits"] = bool((a - b).abs().max() <= 3e-2 * b.abs().max())
         torch.cuda.synchronize()
-        q.put((rank, res, P.device_error()))
+        q.put((rank, res, P.device_error(), lg[True][0]))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_peer_collectives_2gpu():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_collectives(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from conftest import run_ranks
     out, codes = run_ranks(_worker, world, lambda r, port, q: (r, world, port, q), timeout=300)
     assert all(c == 0 for c in codes), codes
     assert len(out) == world
-    for rank, res, err in out:
+    for rank, res, err, toks in out:
         assert all(res.values()), (rank, res)
         assert err == 0
+        assert toks == out[0][3]  # every rank holds the same tokens (identical all-reduce bits)
