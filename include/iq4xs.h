@@ -68,10 +68,10 @@ int iq4xs_q8_1_quantize(const float* X, void* q8, int64_t K, int64_t M, cudaStre
 size_t iq4xs_q8_1_bytes(int64_t K, int64_t M);
 
 /* ------------------------------------------------------------------------------------------ */
-/* Workspace of the GEMV entry points: zero-filled by the caller before its first use (e.g.
- * cudaMemset); every completed call leaves it ready for the next one, whatever the shapes.  After a
- * call reported IQ4XS_ERR_DEVICE_TIMEOUT, zero it again.  Calls that may overlap on the GPU must use
- * separate workspaces.  256-byte aligned. */
+/* Workspace of the GEMV entry points: the call's quantised activations and the partial sums of
+ * long rows split over CTAs.  It needs no initialisation and carries nothing from one call to the
+ * next.  Calls that may overlap on the GPU must use separate workspaces.  256-byte aligned; may be
+ * NULL when the matching *_workspace_bytes function returns 0. */
 
 /* Decode GEMV on pre-quantised activations, batch B = 1..8:
  *   Y[b][n] = sum_k W[n][k] * x_b[k]  with the reference's per-sub-block integer pipeline.
@@ -113,7 +113,7 @@ int iq4xs_gemv_f32_ex(const void* W, const float* X, float* Y, int64_t K, int64_
 /* iq4xs_gemv_f32 for callers that cannot allocate device memory where they call it (a ggml hook
  * inside a graph with a fixed memory plan, a runtime that forbids cudaMalloc after start-up because
  * it synchronises the device): no workspace argument, nothing allocated.  Its scratch (Q8_1
- * activations, tile tickets, partial sums) is one static 4 MiB device array per GPU, kept until the
+ * activations, partial sums) is one static 4 MiB device array per GPU, kept until the
  * process exits; shapes needing more are rejected with IQ4XS_ERR_WORKSPACE_TOO_SMALL.  All calls
  * share that array, so calls that overlap on the GPU race: serialise them on one stream.  The first
  * call on a device looks up the array's address; make it before any stream capture.

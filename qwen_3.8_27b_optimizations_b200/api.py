@@ -159,9 +159,8 @@ _ws_cache = {}
 
 
 def _workspace(nbytes: int, device, kind: str = "gemv"):
-    """A zero-initialised workspace cached per (device, kind).  GEMV workspaces hold tickets that
-    must stay zero between calls; the GEMM writes its quantised activations over the whole of its
-    own, so the two never share one."""
+    """A workspace cached per (device, kind); GEMV and GEMM workspaces have different layouts, so
+    the two never share one."""
     torch = _torch()
     key = (str(device), kind)
     ws = _ws_cache.get(key)

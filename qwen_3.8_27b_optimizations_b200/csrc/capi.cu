@@ -77,8 +77,8 @@ struct Ws {
     void* ptr = nullptr;
     size_t bytes = 0;
 };
-// One buffer per (device, stream, kind): a GEMV workspace keeps zero tickets between calls, the GEMM
-// overwrites all of its own with quantised activations, so the two kinds never share a buffer.
+// One buffer per (device, stream, kind): a GEMV and a GEMM queued on one stream use different
+// layouts of their workspace, so the two kinds never share a buffer.
 enum WsKind { kWsGemv = 0, kWsGemm = 1 };
 std::map<std::tuple<int, cudaStream_t, int>, Ws> g_ws;
 
@@ -107,15 +107,13 @@ cudaError_t internal_workspace(cudaStream_t stream, size_t bytes, void** out, Ws
     while (want < bytes) want <<= 1;
     e = cudaMalloc(&w.ptr, want);
     if (e != cudaSuccess) return e;
-    e = cudaMemset(w.ptr, 0, want);  // the ticket region must start at zero
-    if (e != cudaSuccess) return e;
     w.bytes = want;
     *out = w.ptr;
     return cudaSuccess;
 }
 
-// GEMV workspace: [tickets: kTicketBytes, must be zero before first use, left zero by every call]
-//                 [Q8_1 activations, f32 entry points only][cross-CTA partial sums]
+// GEMV workspace: [Q8_1 activations, f32 entry points only][partial sums of the K parts]; nothing in
+// it carries over from one call to the next.
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 size_t gemv_partials(int64_t K, int64_t N, int64_t B) {
@@ -124,8 +122,7 @@ size_t gemv_partials(int64_t K, int64_t N, int64_t B) {
 
 void attach_workspace(GemvArgs& a, void* ws, size_t q8_bytes, int64_t K, int64_t N, int64_t B) {
     uint8_t* base = static_cast<uint8_t*>(ws);
-    a.tickets = reinterpret_cast<uint32_t*>(base);
-    a.partials = reinterpret_cast<float*>(base + kTicketBytes + align256(q8_bytes));
+    a.partials = reinterpret_cast<float*>(base + align256(q8_bytes));
     a.partial_bytes = gemv_partials(K, N, B);
 }
 
@@ -190,12 +187,12 @@ int iq4xs_q8_1_quantize(const float* X, void* q8, int64_t K, int64_t M, cudaStre
 
 size_t iq4xs_gemv_q8_workspace_bytes(int64_t K, int64_t N, int64_t B) {
     if (K <= 0 || N <= 0 || B <= 0) return 0;
-    return kTicketBytes + gemv_partials(K, N, B);
+    return gemv_partials(K, N, B);
 }
 
 size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t N, int64_t B) {
     if (K <= 0 || N <= 0 || B <= 0) return 0;
-    return kTicketBytes + align256(iq4xs_q8_1_bytes(K, B)) + gemv_partials(K, N, B);
+    return align256(iq4xs_q8_1_bytes(K, B)) + gemv_partials(K, N, B);
 }
 
 int iq4xs_gemv_q8(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B, void* workspace,
@@ -203,8 +200,9 @@ int iq4xs_gemv_q8(const void* W, const void* q8, float* Y, int64_t K, int64_t N,
     int s = check_matrix(W, K, N);
     if (s) return s;
     if ((s = check_batch(B))) return s;
-    if (!q8 || !Y || !workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
-    if (workspace_bytes < iq4xs_gemv_q8_workspace_bytes(K, N, B)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    const size_t need = iq4xs_gemv_q8_workspace_bytes(K, N, B);
+    if (!q8 || !Y || (need && !workspace)) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < need) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
     if (!aligned(q8, 4) || !aligned(Y, 4) || !aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
     GemvArgs a = make_gemv_args(W, q8, Y, K, N);
     attach_workspace(a, workspace, 0, K, N, B);
@@ -216,8 +214,9 @@ int iq4xs_gemv_q8_ex(const void* W, const void* q8, float* Y, int64_t K, int64_t
     int s = check_matrix(W, K, N);
     if (s) return s;
     if ((s = check_batch(B))) return s;
-    if (!q8 || !Y || !workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
-    if (workspace_bytes < iq4xs_gemv_q8_workspace_bytes(K, N, B)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    const size_t need = iq4xs_gemv_q8_workspace_bytes(K, N, B);
+    if (!q8 || !Y || (need && !workspace)) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < need) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
     if (!aligned(q8, 4) || !aligned(Y, 4) || !aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
     GemvArgs a = make_gemv_args(W, q8, Y, K, N);
     attach_workspace(a, workspace, 0, K, N, B);
@@ -248,7 +247,7 @@ int iq4xs_gemv_f32_ex(const void* W, const float* X, float* Y, int64_t K, int64_
     if (!X || !Y || !workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
     if (workspace_bytes < iq4xs_gemv_workspace_bytes(K, N, B)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
     if (!aligned(X, 4) || !aligned(Y, 4) || !aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
-    uint8_t* q8 = static_cast<uint8_t*>(workspace) + kTicketBytes;
+    uint8_t* q8 = static_cast<uint8_t*>(workspace);
     const bool overlap = (flags & IQ4XS_FLAG_OVERLAP_PRECEDING) != 0;
     GemvArgs a = make_gemv_args(W, q8, Y, K, N);
     attach_workspace(a, workspace, iq4xs_q8_1_bytes(K, B), K, N, B);

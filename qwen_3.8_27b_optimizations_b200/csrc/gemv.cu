@@ -510,7 +510,7 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     const int spl = (nsb + 32 * kw - 1) / (32 * kw);
     if (spl > spl_max) {  // K too long for register-resident activations: tensor-core kernel
         if (a.act.mode == kActNorm) return cudaErrorNotSupported;
-        return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.tickets, a.partials, a.partial_bytes, a.K, a.N,
+        return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.partials, a.partial_bytes, a.K, a.N,
                                B, stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
     }
     if (a.act.mode == kActF32 && a.K > kRowFusedMaxK) {
@@ -597,7 +597,7 @@ cudaError_t dispatch(int B, GemvArgs a, cudaStream_t stream, bool pdl) {
     }
     if (B == 1) return launch_rows<1, kDebug>(a, stream, pdl, sms, smem_optin);
     if (a.act.mode == kActNorm) return cudaErrorNotSupported;
-    return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.tickets, a.partials, a.partial_bytes, a.K, a.N, B,
+    return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.partials, a.partial_bytes, a.K, a.N, B,
                            stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
 }
 }  // namespace

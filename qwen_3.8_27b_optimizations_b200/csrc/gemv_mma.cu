@@ -438,7 +438,7 @@ int mma_stages(int pk, int smem_optin) {
 
 // Part size: odd number of pairs pk <= 5 (odd: conflict-free fragment loads).  A unit runs on one
 // warp pair: cost of the busiest pair = units per pair x (pk + overhead); the overhead of a unit (stage
-// latency, stores, ticket) is 0.75 pairs with one stage per warp and 0.35 once the ring holds at
+// latency, stores) is 0.75 pairs with one stage per warp and 0.35 once the ring holds at
 // least 1.5 stages per warp (the next unit's copy overlaps the current one).
 int choose_pk(int pairs, int64_t tiles, int ctas, int smem_optin) {
     if (ctas < 1) ctas = 1;
@@ -495,8 +495,8 @@ static cudaError_t launch_mma_b(const CUtensorMap& map, GemvMmaArgs a, int smem,
     return cudaLaunchKernelEx(&cfg, kern, map, a);
 }
 
-cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32_t* sumi, uint32_t* tickets,
-                            float* partials, size_t partial_bytes, int64_t K, int64_t N, int B, cudaStream_t stream,
+cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32_t* sumi, float* partials,
+                            size_t partial_bytes, int64_t K, int64_t N, int B, cudaStream_t stream,
                             bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4],
                             const ActSource* act) {
     if (B < 1 || B > 8 || K % 512 != 0 || (reinterpret_cast<uintptr_t>(W) & 15u)) return cudaErrorInvalidValue;
@@ -507,9 +507,8 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     const int pk = choose_pk(pairs, T, sms, smem_optin);
     const int stages = mma_stages(pk, smem_optin);
     const int parts = (pairs + pk - 1) / pk;
-    if (parts > 1 && y) {  // partial sums and per-tile tickets (the debug path writes neither)
-        if (!tickets || !partials || partial_bytes < (size_t)parts * B * N * sizeof(float)) return cudaErrorInvalidValue;
-        if (T > (int64_t)(kTicketBytes / sizeof(uint32_t))) return cudaErrorInvalidValue;
+    if (parts > 1 && y) {  // partial sums of the parts (the debug path writes none)
+        if (!partials || partial_bytes < (size_t)parts * B * N * sizeof(float)) return cudaErrorInvalidValue;
     }
     const MmaSmem L = mma_smem(pk, stages);
     if ((int)L.total > smem_optin) return cudaErrorInvalidConfiguration;
@@ -538,7 +537,6 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     a.parts = parts;
     a.stages = stages;
     a.partial = partials;
-    a.tile_cnt = tickets;
     for (int i = 0; i < 4; ++i) a.lut[i] = lut[i];
     a.act.mode = kActQ8;
     if (act && act->mode != kActQ8) {

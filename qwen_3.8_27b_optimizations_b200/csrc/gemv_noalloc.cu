@@ -3,8 +3,8 @@
 // Who needs this: callers that cannot allocate device memory at the point where they run the
 // matmul -- a ggml backend hook called from inside a graph whose memory plan is fixed up front, a
 // runtime that forbids cudaMalloc after start-up because it synchronises the device, or code that
-// owns no allocator at all.  They pass only inputs and outputs; the Q8_1 activations, the per-tile
-// tickets and the cross-CTA partial sums live in one file-scope static device array instead.
+// owns no allocator at all.  They pass only inputs and outputs; the Q8_1 activations and the
+// partial sums of the K parts live in one file-scope static device array instead.
 //
 // Limits and rules:
 //  * the array is kNoAllocScratchBytes (4 MiB) on every GPU that loads the library, held until the
@@ -15,8 +15,8 @@
 //    threads) race and give wrong results -- serialise them on one stream;
 //  * the first call on a device looks up the array's device address (cudaGetSymbolAddress); make
 //    that first call before any stream capture;
-//  * nothing here calls cudaMalloc, cudaFree or an allocating library routine; the ticket words
-//    that must start at zero are cleared with cudaMemsetAsync on the caller's stream.
+//  * nothing here calls cudaMalloc, cudaFree, a memset or an allocating library routine: the array
+//    needs no initialisation, each call writes what it reads.
 #include <mutex>
 
 #include "../../include/iq4xs.h"
@@ -68,23 +68,17 @@ extern "C" int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, i
         (reinterpret_cast<uintptr_t>(Y) & 3u))
         return IQ4XS_ERR_MISALIGNED;
 
-    // Scratch layout: [tickets][Q8_1 activations][partial sums], as the workspace of iq4xs_gemv_f32.
+    // Scratch layout: [Q8_1 activations][partial sums], as the workspace of iq4xs_gemv_f32.
     const size_t q8_bytes = (size_t)(K / kQK8) * (size_t)B * kQ8Bytes;
     const size_t partials = gemv_mma_partial_bytes_for(K, N, (int)B, device_sm_count(), device_smem_optin());
-    const size_t need = kTicketBytes + align_up256(q8_bytes) + partials;
+    const size_t need = align_up256(q8_bytes) + partials;
     if (need > kNoAllocScratchBytes) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
 
     void* scratch = nullptr;
     if (scratch_address(&scratch) != cudaSuccess) return IQ4XS_ERR_CUDA;
     uint8_t* base = static_cast<uint8_t*>(scratch);
-    uint32_t* tickets = reinterpret_cast<uint32_t*>(base);
-    uint8_t* q8 = base + kTicketBytes;
-    float* part = reinterpret_cast<float*>(base + kTicketBytes + align_up256(q8_bytes));
-
-    // The tickets of the tiles this call can touch must start at zero, whatever an earlier call left.
-    const size_t ticket_bytes = (size_t)((N + 15) / 16) * sizeof(uint32_t);
-    if (cudaMemsetAsync(tickets, 0, ticket_bytes < kTicketBytes ? ticket_bytes : kTicketBytes, stream) != cudaSuccess)
-        return IQ4XS_ERR_CUDA;
+    uint8_t* q8 = base;
+    float* part = reinterpret_cast<float*>(base + align_up256(q8_bytes));
     if (launch_q8_1_quantize(X, q8, K, B, K, 1, stream, true, false) != cudaSuccess) return IQ4XS_ERR_CUDA;
 
     GemvArgs a = {};
@@ -100,8 +94,7 @@ extern "C" int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, i
     a.lut[1] = kNegLo1;
     a.lut[2] = kPosHi0;
     a.lut[3] = kPosHi1;
-    a.tickets = tickets;
     a.partials = part;
-    a.partial_bytes = kNoAllocScratchBytes - kTicketBytes - align_up256(q8_bytes);
+    a.partial_bytes = kNoAllocScratchBytes - align_up256(q8_bytes);
     return launch_gemv_q8(a, (int)B, stream, true) == cudaSuccess ? IQ4XS_OK : IQ4XS_ERR_CUDA;
 }

@@ -41,7 +41,6 @@ struct GemvArgs {
     int kw;              // row kernel: warps per row (set by the launcher)
     int rows_per_stage;  // row kernel: rows per stage (set by the launcher)
     uint32_t lut[4];     // codebook prmt tables {neg_lo0, neg_lo1, pos_hi0, pos_hi1} (read from the param bank)
-    uint32_t* tickets;   // tensor-core kernel: per-tile tickets (zero between calls)
     float* partials;     // tensor-core kernel: cross-CTA partial sums
     size_t partial_bytes;
     ActSource act;       // activation source (kActQ8: `q8` above)
@@ -51,7 +50,6 @@ struct GemvMmaArgs {
     const uint8_t* q8;   // Q8_1 blocks [B][K/32][36]
     float* y;            // [B][N]; nullptr: debug sums only
     float* partial;      // [parts][B][N] when parts > 1
-    uint32_t* tile_cnt;  // [ceil(N/16)] tickets, zero between calls
     int32_t* sumi;       // debug only
     uint32_t* err;
     int64_t N;
@@ -64,14 +62,12 @@ struct GemvMmaArgs {
     ActSource act;       // kActQ8 or kActF32
 };
 
-// Tensor-core GEMV (batch 1..8).  Workspace = [tickets: kTicketBytes, zero between calls][partials].
-constexpr size_t kTicketBytes = 64 * 1024;  // one uint32 per 16-row tile: N <= 262144
+// Tensor-core GEMV (batch 1..8).  Workspace = the partial sums of the K parts (none with one part).
 size_t gemv_mma_partial_bytes(int64_t K, int64_t N, int B);
 size_t gemv_mma_partial_bytes_for(int64_t K, int64_t N, int B, int sms, int smem_optin);
 int device_smem_optin();
-cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32_t* sumi, uint32_t* tickets,
-                            float* partials, size_t partial_bytes, int64_t K, int64_t N, int B, cudaStream_t stream,
-                            bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4],
+cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32_t* sumi, float* partials,
+                            size_t partial_bytes, int64_t K, int64_t N, int B, cudaStream_t stream, bool pdl, int sms, int smem_optin, uint32_t* err, const uint32_t lut[4],
                             const ActSource* act = nullptr);
 int device_sm_count();
 // True when launch_gemv_q8 runs the bulk-copy kernels for this matrix (the fused fp32 activation

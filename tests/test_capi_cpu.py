@@ -96,10 +96,13 @@ def test_validation_before_any_launch(pkg):
     assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 9, FAKE, big, None) == 2      # batch > 8
     assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 0, FAKE, big, None) == 2      # batch < 1
     assert L.iq4xs_gemv_q8(FAKE + 4, FAKE, FAKE, 512, 64, 1, FAKE, big, None) == 3  # W not 8-byte aligned
-    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 512, 64, 1, FAKE, 0, None) == 4        # no workspace room
+    need_q8 = L.iq4xs_gemv_q8_workspace_bytes(5120, 1024, 2)  # K split over CTAs: partial sums
+    assert need_q8 > 0
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 5120, 1024, 2, FAKE, need_q8 - 1, None) == 4  # no room
+    assert L.iq4xs_gemv_q8(FAKE, FAKE, FAKE, 5120, 1024, 2, None, need_q8, None) == 1      # no workspace
     assert L.iq4xs_q8_1_quantize(None, FAKE, 512, 1, None) == 1
     need = L.iq4xs_gemv_workspace_bytes(512, 64, 2)
-    assert need >= 64 * 1024 + 2 * 16 * 36
+    assert need >= 2 * 16 * 36  # the Q8_1 activations at least
     assert L.iq4xs_gemv_f32(FAKE, FAKE, FAKE, 512, 64, 2, FAKE, need - 1, None) == 4
     assert L.iq4xs_q8_1_quantize(FAKE, FAKE, 100, 1, None) == 2
     assert L.iq4xs_q8_1_bytes(5120, 3) == 3 * 160 * 36
