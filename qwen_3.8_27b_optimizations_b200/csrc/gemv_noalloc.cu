@@ -79,7 +79,6 @@ extern "C" int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, i
     uint8_t* base = static_cast<uint8_t*>(scratch);
     uint8_t* q8 = base;
     float* part = reinterpret_cast<float*>(base + align_up256(q8_bytes));
-    if (launch_q8_1_quantize(X, q8, K, B, K, 1, stream, true, false) != cudaSuccess) return IQ4XS_ERR_CUDA;
 
     GemvArgs a = {};
     a.W = static_cast<const uint8_t*>(W);
@@ -96,5 +95,13 @@ extern "C" int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, i
     a.lut[3] = kPosHi1;
     a.partials = part;
     a.partial_bytes = kNoAllocScratchBytes - align_up256(q8_bytes);
+    // The same activation policy as iq4xs_gemv_f32: from a 16-byte aligned X the GEMV launchers
+    // quantise inside the kernel where that pays and otherwise run the standalone quantizer into q8.
+    if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0 && gemv_bulk_path(a.W, K)) {
+        a.act.mode = kActF32;
+        a.act.x = X;
+        return launch_gemv_q8(a, (int)B, stream, false) == cudaSuccess ? IQ4XS_OK : IQ4XS_ERR_CUDA;
+    }
+    if (launch_q8_1_quantize(X, q8, K, B, K, 1, stream, true, false) != cudaSuccess) return IQ4XS_ERR_CUDA;
     return launch_gemv_q8(a, (int)B, stream, true) == cudaSuccess ? IQ4XS_OK : IQ4XS_ERR_CUDA;
 }

@@ -3,8 +3,8 @@
 Such callers (a ggml hook inside a graph whose memory is planned ahead, a runtime that forbids
 cudaMalloc once serving because it synchronises the device) pass only inputs and outputs; the
 entry point keeps its scratch in a static 4 MiB device array.  Checked here through the C ABI
-against the workspace entry point iq4xs_gemv_f32, on two calls in a row, with the tolerance the
-other GEMV tests use.  This file is named to run last.
+against the workspace entry point iq4xs_gemv_f32 (bit for bit) and the FP64 restatement (with the
+tolerance the other GEMV tests use), on two calls in a row.  This file is named to run last.
 """
 import numpy as np
 import pytest
@@ -39,7 +39,7 @@ def test_noalloc_matches_workspace_entry_point(pkg, O, N, K, B):
         T64, TA = torch_ref.matmul_q8(W, q8, K)
         tol = O.tolerance(T64.cpu().numpy(), TA.cpu().numpy(), K // 32, REL)
         y, yr = Y.cpu().numpy().astype(np.float64), Yref.cpu().numpy().astype(np.float64)
-        assert np.all(np.abs(y - yr) <= tol)
+        assert np.array_equal(y, yr)  # same kernels, same activation policy: the same bits
         assert np.all(np.abs(y - T64.cpu().numpy()) <= tol)
     assert pkg.device_error() == 0
 
