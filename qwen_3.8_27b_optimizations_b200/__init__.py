@@ -8,3 +8,4 @@ from .api import lib, LIB_PATH, SIGNATURES, IQ4XSError  # noqa: F401
 from . import peer  # noqa: F401,E402  (collectives over NVLink peer memory)
 from . import sharded  # noqa: F401,E402  (row-sharded multi-GPU matmuls)
 from . import decoder  # noqa: F401,E402  (synthetic tensor-parallel decoder)
+from . import gguf_weights  # noqa: F401,E402  (IQ4_XS matrices from / to GGUF files)
