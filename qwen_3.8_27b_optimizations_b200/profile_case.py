@@ -2,6 +2,7 @@
 ncu captures.
 
     python qwen_3.8_27b_optimizations_b200/profile_case.py --N 69632 --K 5120 --B 1 --launches 3
+    python qwen_3.8_27b_optimizations_b200/profile_case.py --N 69632 --K 5120 --B 2 --act f32
     python qwen_3.8_27b_optimizations_b200/profile_case.py --N 17408 --K 5120 --M 2048
     python qwen_3.8_27b_optimizations_b200/profile_case.py --op attention --pos 512
     python qwen_3.8_27b_optimizations_b200/profile_case.py --op sweep
@@ -12,8 +13,8 @@ ncu captures.
 that a profiler lists every kernel.
 
 Weights are synthetic IQ4_XS (N(0, 0.02) quantised on the device), activations N(0, 1), quantised
-to Q8_1 once up front, so the launches of interest are `--launches` GEMV kernels after `--warmup`
-untimed ones.  The default N (twice the gate|up projection) keeps the weights above the 126 MB L2.
+to Q8_1 once up front (or, with --act f32, passed as fp32 to the fp32 entry point), so the launches
+of interest are `--launches` GEMV kernels after `--warmup` untimed ones.  The default N (twice the gate|up projection) keeps the weights above the 126 MB L2.
 Prints one line with the event-timed average per launch (meaningless under a profiler).
 """
 from __future__ import annotations
@@ -44,6 +45,9 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--op", default="gemv", choices=["gemv", "attention", "sweep"])
     ap.add_argument("--pos", type=int, default=512)
+    ap.add_argument("--act", default="q8", choices=["q8", "f32"],
+                    help="GEMV activations: pre-quantised Q8_1, or fp32 through the fp32 entry point "
+                         "(quantised inside the GEMV kernel where the launch policy does that)")
     args = ap.parse_args()
     P = _load_pkg()
     if args.op == "attention":
@@ -58,20 +62,25 @@ def main() -> int:
     q8 = P.q8_1_quantize(X)
     ws = torch.zeros(P.gemv_q8_workspace_bytes(K, N, B), dtype=torch.uint8, device="cuda")
     Y = torch.empty((B, N), dtype=torch.float32, device="cuda")
+    if args.act == "f32":
+        ws = torch.zeros(P.gemv_workspace_bytes(K, N, B), dtype=torch.uint8, device="cuda")
+        run = lambda: P.gemv(W, X, N, workspace=ws, out=Y)
+    else:
+        run = lambda: P.gemv_q8(W, q8, K, N, B, out=Y, workspace=ws)
     for _ in range(args.warmup):
-        P.gemv_q8(W, q8, K, N, B, out=Y, workspace=ws)
+        run()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.launches):
-        P.gemv_q8(W, q8, K, N, B, out=Y, workspace=ws)
+        run()
     e1.record()
     torch.cuda.synchronize()
     if P.device_error():
         raise RuntimeError(f"device error word {P.device_error()}")
     us = e0.elapsed_time(e1) * 1e3 / max(args.launches, 1)
     nbytes = N * K * 17 // 32 + 4 * B * K + 4 * B * N
-    print(json.dumps({"N": N, "K": K, "B": B, "us_per_launch": round(us, 2),
+    print(json.dumps({"N": N, "K": K, "B": B, "act": args.act, "us_per_launch": round(us, 2),
                       "algorithmic_bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}))
     return 0
 
