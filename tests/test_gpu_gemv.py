@@ -116,6 +116,7 @@ SHAPES = {  # name: (N out, K in)
     "c1_4096": (4096, 4096),
     "q_proj": (8192, 5120), "k_proj": (1024, 5120), "o_proj": (5120, 8192),
     "gate": (17408, 5120), "gate_up": (34816, 5120), "down": (5120, 17408),
+    "lm_head": (152064, 5120),  # the row-sharded matrix of the multi-GPU config, whole
 }
 
 
