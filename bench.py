@@ -20,7 +20,8 @@ gemm   = prefill GEMM: the same layer shapes at M = 5
          (iq4xs_gemm: Q8_1 activation quantisation + the tensor-core GEMM per call), TOPS = 2*M*N*K /
          device time, against the measured dense bf16 tensor peak; reported beside the headline.
 --impl reference: the reference's own CPU path (kernels/matmul_iq4xs/ref_cpu.cpp, compiled unchanged
-         into oracle/_ref/) on the host cores, same metric on a bounded row sample.
+         into oracle/_ref/) on the host cores, same metric on a bounded row sample; where oracle/_ref
+         was not built, the oracle's C restatement of that loop (cpu_baseline.kind "port").
 """
 from __future__ import annotations
 
@@ -343,10 +344,11 @@ def cpu_sample_plan(rows_per_shape: int):
     return [(name, min(N, rows_per_shape), K) for name, N, K in SHAPES]
 
 
-def run_cpu_reference(threads: int, rows_per_shape: int, steps: int, warmup: int):
-    """The reference's gemv_iq4xs_cpu_ref (FP64, unquantised x) over a row sample of every shape,
-    every batch size (one call per token, as the reference's CPU path has no batch), row slices
-    spread over `threads` host threads.  Returns (GB/s, seconds per step, sample text)."""
+def run_cpu_reference(threads: int, rows_per_shape: int, steps: int, warmup: int, kind: str = "reference"):
+    """The reference's gemv_iq4xs_cpu_ref (FP64, unquantised x; kind "reference") or the oracle's C
+    restatement of it (kind "port", used where oracle/_ref was not built) over a row sample of every
+    shape, every batch size (one call per token, as the reference's CPU path has no batch), row
+    slices spread over `threads` host threads.  Returns (GB/s, seconds per step, sample text)."""
     import numpy as np
 
     sys.path.insert(0, str(ROOT))
@@ -365,7 +367,7 @@ def run_cpu_reference(threads: int, rows_per_shape: int, steps: int, warmup: int
             for name, n, K in plan:
                 W, xs, _, _ = mats[name]
                 for b in range(B):
-                    O.ref_gemv_threaded(W, xs[b], K, n, threads)
+                    O.ref_gemv_threaded(W, xs[b], K, n, threads, kind=kind)
 
     for _ in range(warmup):
         one_step()
@@ -374,8 +376,9 @@ def run_cpu_reference(threads: int, rows_per_shape: int, steps: int, warmup: int
         one_step()
     dt = (time.perf_counter() - t0) / max(steps, 1)
     nbytes = sum(gemv_bytes(n, K, B) for B in BATCHES for _, n, K in plan)
+    fn = "gemv_iq4xs_cpu_ref" if kind == "reference" else "or_matmul_f64 (C port of gemv_iq4xs_cpu_ref)"
     sample = (f"first {rows_per_shape} rows of each of the 6 shapes (all rows of k/v), batch 1/2/4/8 "
-              f"(one FP64 gemv_iq4xs_cpu_ref call per token), rows split over {threads} threads")
+              f"(one FP64 {fn} call per token), rows split over {threads} threads")
     return nbytes / dt / 1e9, dt, sample
 
 
@@ -384,11 +387,11 @@ def reference_arm(args, rank: int, world: int):
         return 0
     sys.path.insert(0, str(ROOT))
     from oracle import oracle as O
-    if not O.ref_available():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_cpu.so not built"}))
-        return 0
+    kind = O.cpu_gemv_kind()
     threads = O.host_threads()
-    gbs, dt, sample = run_cpu_reference(threads, args.cpu_rows, args.steps, args.warmup)
+    gbs, dt, sample = run_cpu_reference(threads, args.cpu_rows, args.steps, args.warmup, kind)
+    path = ("kernels/matmul_iq4xs/ref_cpu.cpp gemv_iq4xs_cpu_ref (unchanged)" if kind == "reference"
+            else "oracle/iq4xs_oracle.c or_matmul_f64 (restatement of ref_cpu.cpp:12-39)")
     line = {
         "impl": "reference",
         "metric": "IQ4_XS decode GEMV sweep HBM GB/s", "value": round(gbs, 3), "unit": "GB/s",
@@ -396,8 +399,8 @@ def reference_arm(args, rank: int, world: int):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (reference random-byte IQ4_XS blocks, N(0,1) activations)",
         "config": {"workload": "decode_gemv_sweep_27b_layers", "shapes": {n: [N, K] for n, N, K in SHAPES},
-                   "batches": BATCHES, "path": "kernels/matmul_iq4xs/ref_cpu.cpp gemv_iq4xs_cpu_ref (unchanged)"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference", "sample": sample},
+                   "batches": BATCHES, "path": path},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -600,10 +603,10 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, str(ROOT))
         from oracle import oracle as O
-        if O.ref_available():
-            threads = O.host_threads()
-            gbs, _, sample = run_cpu_reference(threads, args.cpu_rows, 2, 1)
-            cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference", "sample": sample}
+        kind = O.cpu_gemv_kind()
+        threads = O.host_threads()
+        gbs, _, sample = run_cpu_reference(threads, args.cpu_rows, 2, 1, kind)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample}
 
     for g in graphs:
         del g

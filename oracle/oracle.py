@@ -231,8 +231,16 @@ def _pool(threads: int):
     return _POOLS[threads]
 
 
-def ref_gemv_threaded(W: np.ndarray, x: np.ndarray, K: int, N: int, threads: int, y: np.ndarray = None) -> np.ndarray:
-    """The reference's gemv_iq4xs_cpu_ref over contiguous row slices on `threads` host threads of a
+def cpu_gemv_kind() -> str:
+    """Which CPU GEMV ref_gemv_threaded runs: "reference" (the reference's ref_cpu.cpp, built where
+    its tree exists) or "port" (or_matmul_f64, the C restatement of the same FP64 loop)."""
+    return "reference" if ref_available() else "port"
+
+
+def ref_gemv_threaded(W: np.ndarray, x: np.ndarray, K: int, N: int, threads: int, y: np.ndarray = None,
+                      kind: str = "reference") -> np.ndarray:
+    """The reference's gemv_iq4xs_cpu_ref (kind "reference") or its C restatement or_matmul_f64
+    (kind "port", ref_cpu.cpp:12-39) over contiguous row slices on `threads` host threads of a
     persistent pool (ctypes releases the GIL for the duration of each call)."""
     W = np.ascontiguousarray(W)
     x = np.ascontiguousarray(x, dtype=np.float32)
@@ -241,12 +249,19 @@ def ref_gemv_threaded(W: np.ndarray, x: np.ndarray, K: int, N: int, threads: int
     rb = K // QK_K * BLOCK_BYTES
     base_w, base_y = W.ctypes.data, y.ctypes.data
     bounds = np.linspace(0, N, threads + 1).astype(np.int64)
-    L = ref()
+    if kind == "reference":
+        fn = ref().ref_gemv_iq4xs_cpu_ref
+        call = lambda w, yy, n: fn(w, _p(x), yy, K, n)  # noqa: E731
+    elif kind == "port":
+        fn = lib().or_matmul_f64
+        call = lambda w, yy, n: fn(w, _p(x), yy, K, n, 1)  # noqa: E731  (M = 1: y is [1][n])
+    else:
+        raise ValueError(f"unknown CPU GEMV kind {kind!r}")
 
     def run(i):
         r0, r1 = int(bounds[i]), int(bounds[i + 1])
         if r1 > r0:
-            L.ref_gemv_iq4xs_cpu_ref(C.c_void_p(base_w + r0 * rb), _p(x), C.c_void_p(base_y + 4 * r0), K, r1 - r0)
+            call(C.c_void_p(base_w + r0 * rb), C.c_void_p(base_y + 4 * r0), r1 - r0)
 
     list(_pool(threads).map(run, range(threads)))
     return y

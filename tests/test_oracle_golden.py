@@ -67,3 +67,18 @@ def test_fp32_reference_order_close_to_fp64(O, golden):
     Y32 = O.matmul_q8_f32(golden[f"{name}/W"], golden[f"{name}/Q"], K, N, M)
     Y64, A = golden[f"{name}/Y64"], golden[f"{name}/A"]
     assert np.all(np.abs(Y32 - Y64) <= O.tolerance(Y64, A, K // 32))
+
+
+@pytest.mark.parametrize("kind", ["port", "reference"])
+def test_threaded_cpu_gemv_matches_reference_outputs(O, golden, kind):
+    # The CPU baseline's row-sliced GEMV (bench.py's reference arm) with either implementation
+    # reproduces gemv_iq4xs_cpu_ref's outputs bit for bit, whatever the slicing.
+    if kind == "reference" and not O.ref_available():
+        pytest.skip("oracle/_ref not built (reference tree absent)")
+    name = cases(golden)[0]
+    K, N, M = (int(v) for v in golden[f"{name}/shape"])
+    W, X, Yref = golden[f"{name}/W"], golden[f"{name}/X"].reshape(M, K), golden[f"{name}/Yref"]
+    for threads in (1, 3):
+        for m in range(M):
+            y = O.ref_gemv_threaded(W, X[m], K, N, threads, kind=kind)
+            assert np.array_equal(y, Yref[m])
