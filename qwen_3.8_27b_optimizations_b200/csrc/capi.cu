@@ -4,6 +4,7 @@
 // (kernels/matmul_iq4xs/impl_gemv_dp4a_gfx1100.hip:291-329, real_stock_dp4a_comparator.hip:266-315,
 // patches/0001-gfx1100-mul-mat-custom.patch:148-154,261-280): null pointers, K % 256, non-positive
 // sizes are rejected before any launch; nothing aborts; errors come back as status codes.
+#include <atomic>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -21,7 +22,9 @@ namespace {
 __device__ uint32_t g_device_error;
 
 constexpr int kMaxDevices = 64;
-uint32_t* g_err_ptr[kMaxDevices];
+// Device address of g_device_error per device, filled on first use; several host threads may
+// launch on one device at once, so the slots are atomics.
+std::atomic<uint32_t*> g_err_ptr[kMaxDevices];
 std::mutex g_mu;
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
@@ -32,12 +35,14 @@ int status_from(cudaError_t e) { return e == cudaSuccess ? IQ4XS_OK : IQ4XS_ERR_
 uint32_t* device_error_word() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-    if (!g_err_ptr[dev]) {
+    uint32_t* cur = g_err_ptr[dev].load(std::memory_order_acquire);
+    if (!cur) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
-        g_err_ptr[dev] = static_cast<uint32_t*>(p);
+        cur = static_cast<uint32_t*>(p);  // the same address whichever thread stores it
+        g_err_ptr[dev].store(cur, std::memory_order_release);
     }
-    return g_err_ptr[dev];
+    return cur;
 }
 
 namespace {
@@ -197,16 +202,7 @@ size_t iq4xs_gemv_workspace_bytes(int64_t K, int64_t N, int64_t B) {
 
 int iq4xs_gemv_q8(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B, void* workspace,
                   size_t workspace_bytes, cudaStream_t stream) {
-    int s = check_matrix(W, K, N);
-    if (s) return s;
-    if ((s = check_batch(B))) return s;
-    const size_t need = iq4xs_gemv_q8_workspace_bytes(K, N, B);
-    if (!q8 || !Y || (need && !workspace)) return IQ4XS_ERR_INVALID_ARGUMENT;
-    if (workspace_bytes < need) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
-    if (!aligned(q8, 4) || !aligned(Y, 4) || !aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
-    GemvArgs a = make_gemv_args(W, q8, Y, K, N);
-    attach_workspace(a, workspace, 0, K, N, B);
-    return status_from(launch_gemv_q8(a, (int)B, stream, false));
+    return iq4xs_gemv_q8_ex(W, q8, Y, K, N, B, workspace, workspace_bytes, 0u, stream);
 }
 
 int iq4xs_gemv_q8_ex(const void* W, const void* q8, float* Y, int64_t K, int64_t N, int64_t B, void* workspace,
@@ -270,6 +266,7 @@ int iq4xs_debug_subblock_dots(const void* W, const void* q8, int32_t* S, int64_t
     if (s) return s;
     if ((s = check_batch(B))) return s;
     if (!q8 || !S) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (!aligned(q8, 4) || !aligned(S, 4)) return IQ4XS_ERR_MISALIGNED;
     GemvArgs a = make_gemv_args(W, q8, nullptr, K, N);  // sums only, no y
     a.sumi = S;
     return status_from(launch_gemv_q8_debug(a, (int)B, stream));
@@ -291,6 +288,7 @@ int iq4xs_dequantize(const void* W, float* out, int64_t K, int64_t N, cudaStream
     int s = check_matrix(W, K, N);
     if (s) return s;
     if (!out) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (!aligned(out, 4)) return IQ4XS_ERR_MISALIGNED;
     return status_from(launch_dequantize(static_cast<const uint8_t*>(W), out, K, N, stream));
 }
 
