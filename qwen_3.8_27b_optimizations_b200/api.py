@@ -207,7 +207,7 @@ FLAG_OVERLAP_PRECEDING = 1
 
 def gemv(W, X, N: int, workspace=None, out=None, stream=None, flags: int = 0):
     """Y [B][N] = W . X^T for fp32 activations X [B][K] (quantised on the fly into the workspace).
-    The workspace must be zero-filled before its first use (torch.zeros).  flags=FLAG_OVERLAP_PRECEDING
+    The workspace needs no initialisation (nothing in it carries over between calls).  flags=FLAG_OVERLAP_PRECEDING
     when W is not written by the preceding kernel on the stream."""
     torch = _torch()
     X = X.contiguous()

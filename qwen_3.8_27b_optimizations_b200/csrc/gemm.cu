@@ -542,14 +542,15 @@ typedef CUresult (*EncodeTiledFn2)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn2 encode_fn2() {
-    static EncodeTiledFn2 fn = nullptr;
-    if (!fn) {
+    // Function-local static: initialised once, thread-safe when several host threads launch at once.
+    static const EncodeTiledFn2 fn = []() -> EncodeTiledFn2 {
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn2>(p);
-    }
+            return reinterpret_cast<EncodeTiledFn2>(p);
+        return nullptr;
+    }();
     return fn;
 }
 

@@ -19,6 +19,7 @@
 //    fp32 expression; per-row sums are reduced over the 8 sub-block lanes with xor shuffles.
 //  * every mbarrier wait is bounded; a timeout records a device error code and the kernel
 //    drains its in-flight copies and returns.
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -459,8 +460,11 @@ __global__ void __launch_bounds__(256) gemv_iq4xs_q8_generic_kernel(const GemvAr
 // Host-side launch helpers.
 namespace {
 
-int g_num_sms[64];
-int g_max_smem[64];
+// Per-device cache of the two attributes.  Host threads may launch on one device concurrently: the
+// shared-memory limit is published before the SM count (release), and a reader that sees the SM
+// count (acquire) sees the limit too, so no caller reads a half-filled entry.
+std::atomic<int> g_num_sms[64];
+std::atomic<int> g_max_smem[64];
 
 void device_limits(int dev, int* sms, int* smem_optin) {
     if (dev < 0 || dev >= 64) {
@@ -468,12 +472,21 @@ void device_limits(int dev, int* sms, int* smem_optin) {
         cudaDeviceGetAttribute(smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         return;
     }
-    if (g_num_sms[dev] == 0) {
-        cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        cudaDeviceGetAttribute(&g_max_smem[dev], cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    int n = g_num_sms[dev].load(std::memory_order_acquire);
+    if (n == 0) {
+        int smem = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        *sms = n;
+        *smem_optin = smem;
+        if (n > 0 && smem > 0) {
+            g_max_smem[dev].store(smem, std::memory_order_relaxed);
+            g_num_sms[dev].store(n, std::memory_order_release);
+        }
+        return;
     }
-    *sms = g_num_sms[dev];
-    *smem_optin = g_max_smem[dev];
+    *sms = n;
+    *smem_optin = g_max_smem[dev].load(std::memory_order_relaxed);
 }
 
 // Row-stage kernel configuration for batch B: 16 consumer warps, one row each per stage; KW warps
