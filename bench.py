@@ -145,6 +145,66 @@ def gemm_sweep(P, weights, dev, stream, reps: int = 3):
     return per, tot_flops / (tot_ms * 1e-3) / 1e12
 
 
+def c1_gemv(P, dev, stream, copies: int = 16):
+    """one GEMV 4096 x 4096 at batch 1 through the fp32 entry point (Q8_1 of x
+    inside the call).  `copies` weight matrices (16 x 8.9 MB = 143 MB > L2) rotate through a captured
+    graph of `copies` calls, so every call streams its weights from HBM; per-call time = median of 3
+    replays / copies."""
+    import torch
+    N = K = 4096
+    Ws = [P.random_weights(N, K, seed=9100 + i) for i in range(copies)]
+    X = P.fill_normal(K, seed=9099).view(1, K)
+    Y = torch.empty((1, N), dtype=torch.float32, device=dev)
+    ws = torch.zeros(P.gemv_workspace_bytes(K, N, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(stream):
+        for W in Ws:
+            P.gemv(W, X, N, workspace=ws, out=Y, stream=stream, flags=P.FLAG_OVERLAP_PRECEDING)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for W in Ws:
+                P.gemv(W, X, N, workspace=ws, out=Y, stream=stream, flags=P.FLAG_OVERLAP_PRECEDING)
+        g.replay()
+        stream.synchronize()
+        ts = []
+        for _ in range(3):
+            a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            g.replay()
+            b0.record(stream)
+            stream.synchronize()
+            ts.append(a0.elapsed_time(b0) / copies)
+    del g
+    ms = statistics.median(ts)
+    nb = gemv_bytes(N, K, 1)
+    peak, peak_kind = hbm_peak()
+    gbs = nb / (ms * 1e-3) / 1e9
+    return {"config": "single IQ4_XS GEMV 4096 x 4096, batch 1 (BASELINE.json configs[0]), fp32 x quantised "
+                      "to Q8_1 inside the call", "us_per_call": round(ms * 1e3, 2), "GBs": round(gbs, 1),
+            "roofline": {"bound": "hbm", "peak": peak, "peak_kind": peak_kind, "frac": round(gbs / peak, 4)},
+            "l2": f"{copies} weight copies ({copies * nb / 1e6:.0f} MB) rotate"}
+
+
+def c1_cpu_reference(threads: int, kind: str, calls: int = 5):
+    """The reference's CPU GEMV (gemv_iq4xs_cpu_ref, or its C port where oracle/_ref is absent) on the
+    full 4096 x 4096 C1 matrix (reference random-byte blocks), all host threads, median of `calls`."""
+    import numpy as np
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    N = K = 4096
+    W = O.random_blocks(K, N, 4096)
+    x = np.random.default_rng(1).standard_normal(K).astype(np.float32)
+    O.ref_gemv_threaded(W, x, K, N, threads, kind=kind)
+    ts = []
+    for _ in range(calls):
+        t0 = time.perf_counter()
+        O.ref_gemv_threaded(W, x, K, N, threads, kind=kind)
+        ts.append(time.perf_counter() - t0)
+    dt = statistics.median(ts)
+    return {"us_per_call": round(dt * 1e6, 1), "GBs": round(gemv_bytes(N, K, 1) / dt / 1e9, 3), "cores": threads,
+            "kind": kind, "sample": f"all 4096 rows, median of {calls} calls"}
+
+
 SHARDED = [("lm_head", 152064, 5120), ("gate_up", 34816, 5120)]
 
 
@@ -202,10 +262,23 @@ def sharded_sweep(P, dev, stream, rank: int, world: int, barrier, reps: int = 5)
 DECODER_PROMPT, DECODER_STEPS = 512, 128
 
 
+PARITY_TOKEN = 12345  # the fixed input token of the decode step compared across TP degrees
+
+
+def decoder_parity_logits(m, prompt):
+    """Prefill logits of `prompt`, then the logits of one decode step (the fused decode kernels and, at
+    TP > 1, the peer collectives) on a fixed token; both flattened to float64 on the device."""
+    _, lg_pre = m.prefill(prompt)
+    m._tok.fill_(PARITY_TOKEN % m.cfg.vocab)
+    m._step()
+    return lg_pre.flatten().double(), m._last_logits.flatten().double().clone()
+
+
 def decoder_run(P, dev, rank: int, world: int, barrier):
     """the synthetic 64-layer decoder, tensor-parallel over the ranks: a
     512-token uniform random prompt (seed 7), then 128 greedy decode steps (CUDA-graph replay per
-    token).  Times are CUDA events on each rank, max over ranks."""
+    token).  Times are CUDA events on each rank, max over ranks.  Also returns the model's prefill
+    and fixed-token decode logits (untimed) for the multi-GPU parity check."""
     import torch
     import torch.distributed as dist
     cfg = P.decoder.DecoderConfig()
@@ -214,6 +287,7 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
     torch.cuda.synchronize()
     build_s = time.time() - t0
     prompt = torch.randint(0, cfg.vocab, (DECODER_PROMPT,), generator=torch.Generator().manual_seed(7)).to(dev)
+    logits = decoder_parity_logits(m, prompt)
     m.prefill(prompt)
     m.decode(4)                      # warm-up: eager steps and graph capture
     barrier()
@@ -237,7 +311,108 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
             "prefill_ms": round(pre_ms, 1), "prefill_tok_s": round(DECODER_PROMPT / (pre_ms * 1e-3), 1),
             "decode_ms": round(dec_ms, 1), "build_s": round(build_s, 1), "first_tokens": toks[:8],
             "model": "64 x (hidden 5120, 64x128 q heads, 8 kv heads, SwiGLU 17408), vocab 152064, IQ4_XS "
-                     "linear layers, fp32 norms, f16 embeddings and KV cache, random N(0, 0.02) init"}
+                     "linear layers, fp32 norms, f16 embeddings and KV cache, random N(0, 0.02) init"}, logits
+
+
+def logit_agreement(a, b) -> dict:
+    """a against the reference b (flat float64 tensors): cosine, max |a - b| / max |b|, same argmax, and
+    how many of b's top 5 are in a's top 5."""
+    import torch
+    cos = float(torch.dot(a, b) / (a.norm() * b.norm()))
+    rel = float((a - b).abs().max() / b.abs().max())
+    top_a, top_b = set(torch.topk(a, 5).indices.tolist()), set(torch.topk(b, 5).indices.tolist())
+    return {"cosine": round(cos, 9), "max_rel": float(f"{rel:.3g}"), "argmax_same": bool(a.argmax() == b.argmax()),
+            "top5_common": len(top_a & top_b)}
+
+
+def multi_gpu_parity(P, dev, rank: int, world: int, c5_logits) -> dict:
+    """N > 1, outside every timed region: multi-GPU results against single-GPU results that every rank
+    computes itself on the same inputs.
+      * row-sharded GEMV (peer-memory all-gather) and GEMM (NCCL all-gather) of gate|up 34816 x 5120:
+        batch 1 and the GEMM bit-exact against the full-matrix kernels (rows are independent, per-row
+        arithmetic identical); batch 3 bit-exact against the concatenated per-shard GEMVs and within
+        1e-5 (of max |y|) of the full-matrix GEMV (its K parts may be split differently);
+      * tensor-parallel decoders, prefill logits and the logits of one fused decode step on a fixed
+        token: a small 2-layer model with peer collectives against the same model with NCCL
+        all-reduces and against TP 1; the C5 dimensions at 2 layers, and the full 64-layer C5 model,
+        against TP 1 of the same weights.  Summation order differs between TP degrees (partial sums of
+        the row-parallel layers), which moves single Q8_1 roundings of the next layer's activations,
+        so decoder logits are compared by cosine (gates below), with max rel error and top-5 shown."""
+    import torch
+    res, ok = {}, True
+    # ---- row-sharded matmuls
+    N, K = 34816, 5120
+    W = P.random_weights(N, K, seed=777)
+    shards = [P.sharded.shard_rows(N, world, r) for r in range(world)]
+    r0, r1 = shards[rank]
+    peers = P.peer.PeerGroup(3 * P.sharded.max_shard_rows(N, world), areas=2)
+    S = P.sharded.RowShardedIQ4XS(W[r0:r1].contiguous(), N, K, peers=peers)
+    sh = {}
+    for B in (1, 3):
+        X = P.fill_normal(B * K, seed=5 + B).view(B, K)
+        Y = S.gemv(X).clone()
+        Yf = P.gemv(W, X, N)
+        if B == 1:
+            sh["gemv_b1_bitexact"] = bool(torch.equal(Y, Yf))
+        else:
+            Ycat = torch.cat([P.gemv(W[a:b].contiguous(), X, b - a) for a, b in shards], 1)
+            sh["gemv_b3_bitexact_vs_shards"] = bool(torch.equal(Y, Ycat))
+            rel = float((Y - Yf).abs().max() / Yf.abs().max())
+            sh["gemv_b3_max_rel_vs_full"] = float(f"{rel:.3g}")
+            sh["gemv_b3_within_1e-5"] = rel <= 1e-5
+    Xm = P.fill_normal(256 * K, seed=9).view(256, K)
+    sh["gemm_m256_bitexact"] = bool(torch.equal(S.gemm_nm(Xm), P.gemm(W, Xm, N).t()))
+    torch.cuda.synchronize()
+    peers.close()
+    del S, W
+    torch.cuda.empty_cache()
+    ok &= all(v for k, v in sh.items() if isinstance(v, bool))
+    res["sharded_gate_up"] = sh
+
+    def build(cfg, w, rk, **kw):
+        return P.decoder.TPDecoder(cfg, rank=rk, world=w, seed=4, **kw)
+
+    def run(cfg, w, rk, prompt, **kw):
+        m = build(cfg, w, rk, **kw)
+        out = decoder_parity_logits(m, prompt)
+        torch.cuda.synchronize()
+        m.release()
+        del m
+        torch.cuda.empty_cache()
+        return out
+
+    def agree(tag, a, b, gate):
+        nonlocal ok
+        d = {"prefill": logit_agreement(a[0], b[0]), "decode_step": logit_agreement(a[1], b[1]),
+             "gate_cosine": gate}
+        d["ok"] = d["prefill"]["cosine"] >= gate and d["decode_step"]["cosine"] >= gate
+        ok &= d["ok"]
+        res[tag] = d
+
+    # ---- small decoder: one KV head and 4 query heads per rank, two FFN super-block pairs per rank
+    small = P.decoder.DecoderConfig(layers=2, hidden=1024, heads=4 * world, kv_heads=world, head_dim=128,
+                                    ffn=1024 * world, vocab=3072, max_seq=40)
+    prompt = torch.randint(0, small.vocab, (12,), generator=torch.Generator().manual_seed(3)).to(dev)
+    peer_l = run(small, world, rank, prompt, peer_collectives=True)
+    nccl_l = run(small, world, rank, prompt, peer_collectives=False)
+    tp1_l = run(small, 1, 0, prompt)
+    agree("small_2layer_peer_vs_nccl", peer_l, nccl_l, 0.9999)
+    agree("small_2layer_tp_vs_tp1", peer_l, tp1_l, 0.9999)
+    # ---- C5 dimensions, 2 layers
+    c5_2 = P.decoder.DecoderConfig(layers=2)
+    prompt = torch.randint(0, c5_2.vocab, (DECODER_PROMPT,), generator=torch.Generator().manual_seed(7)).to(dev)
+    agree("c5_2layer_tp_vs_tp1", run(c5_2, world, rank, prompt), run(c5_2, 1, 0, prompt), 0.9999)
+    # ---- full C5 (64 layers): the timed model's logits against TP 1 of the same weights (seed 1)
+    if c5_logits is not None:
+        m = P.decoder.TPDecoder(P.decoder.DecoderConfig(), rank=0, world=1, seed=1)
+        tp1 = decoder_parity_logits(m, prompt)
+        torch.cuda.synchronize()
+        m.release()
+        del m
+        torch.cuda.empty_cache()
+        agree("c5_64layer_tp_vs_tp1", c5_logits, tp1, 0.99)
+    res["ok"] = bool(ok)
+    return res
 
 
 def ncu_traffic():
@@ -265,14 +440,18 @@ class ClockSampler:
         self._thread = None
         self._proc = None
 
+    def _bus_id(self):
+        """PCI bus id of the torch device: names the same physical GPU to NVML and nvidia-smi whatever
+        CUDA_VISIBLE_DEVICES or the enumeration order is."""
+        import torch
+        pr = torch.cuda.get_device_properties(self.idx)
+        return f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+
     def _nvml_handle(self):
         import pynvml
-        import torch
         pynvml.nvmlInit()
         try:
-            pr = torch.cuda.get_device_properties(self.idx)
-            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
-            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(self._bus_id())
         except Exception:
             return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.idx)
 
@@ -302,8 +481,12 @@ class ClockSampler:
             fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                       "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
             try:
+                try:
+                    gpu = self._bus_id()
+                except Exception:
+                    gpu = str(self.idx)
                 self._proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
-                                               "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                               "-lms", "200", "-i", gpu], stdout=subprocess.PIPE,
                                               stderr=subprocess.DEVNULL, text=True)
             except Exception:
                 self._proc = None
@@ -407,8 +590,104 @@ def reference_arm(args, rank: int, world: int):
     return 0
 
 
+# ----------------------------------------------------------------------------- single cases (profiling)
+def run_case(argv) -> int:
+    """`bench.py --case {gemv,gemm,attention,sweep} ...`: one small, self-ending case on cuda:0 for ncu
+    captures (never a bench number: it prints the event-timed average of `--launches` launches after
+    `--warmup` untimed ones, meaningless under a profiler).
+
+      --case gemv --N 69632 --K 5120 --B 8 [--act f32]   one GEMV shape (Q8_1 quantised once up front,
+                                                          or fp32 through the fp32 entry point)
+      --case gemm --N 17408 --K 5120 --M 2048             the prefill GEMM
+      --case attention --pos 512                          the decoder's decode attention (64 / 8 heads)
+      --case sweep                                        one benchmark sweep step, eager launches
+    The default N (twice the gate|up projection) keeps the weights above the 126 MB L2."""
+    import torch
+    ap = argparse.ArgumentParser(prog="bench.py --case")
+    ap.add_argument("--case", required=True, choices=["gemv", "gemm", "attention", "sweep"])
+    ap.add_argument("--N", type=int, default=69632)
+    ap.add_argument("--K", type=int, default=5120)
+    ap.add_argument("--B", type=int, default=1)
+    ap.add_argument("--M", type=int, default=2048)
+    ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--pos", type=int, default=512)
+    ap.add_argument("--act", default="q8", choices=["q8", "f32"])
+    a = ap.parse_args(argv)
+    P = load_pkg()
+    torch.cuda.set_device(0)
+
+    def timed(run, launches, warmup):
+        for _ in range(warmup):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(launches):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        if P.device_error():
+            raise RuntimeError(f"device error word {P.device_error()}")
+        return e0.elapsed_time(e1) * 1e3 / max(launches, 1)
+
+    if a.case == "attention":
+        hq, hkv, hd, max_seq = 64, 8, 128, 640
+        g = torch.Generator(device="cuda").manual_seed(3)
+        qkv = torch.randn((1, (hq + 2 * hkv) * hd), generator=g, device="cuda")
+        kc = torch.randn((hkv, max_seq, hd), generator=g, device="cuda").half()
+        vc = torch.randn((hkv, max_seq, hd), generator=g, device="cuda").half()
+        inv = 1.0 / (1.0e6 ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
+        ang = torch.arange(max_seq, dtype=torch.float64)[:, None] * inv[None, :]
+        cos, sin = torch.cos(ang).float().cuda(), torch.sin(ang).float().cuda()
+        p = torch.tensor([a.pos], dtype=torch.long, device="cuda")
+        q8 = torch.empty((1, hq * hd // 32 * 36), dtype=torch.uint8, device="cuda")
+        us = timed(lambda: P.dec_attention_decode_q8(qkv, kc, vc, cos, sin, p, hq, hkv, q8=q8), a.launches, a.warmup)
+        print(json.dumps({"case": "attention", "pos": a.pos, "us_per_launch": round(us, 2),
+                          "kv_bytes": 2 * hkv * (a.pos + 1) * hd * 2}))
+        return 0
+    if a.case == "sweep":
+        Ws = [P.random_weights(N, K, seed=i) for i, (_, N, K) in enumerate(SHAPES)]
+        Xs = {B: P.fill_normal(B * 17408, seed=B) for B in BATCHES}
+        Ys = {B: torch.empty(B * 34816, dtype=torch.float32, device="cuda") for B in BATCHES}
+
+        def step():
+            for B in BATCHES:
+                for W, (_, N, K) in zip(Ws, SHAPES):
+                    P.gemv(W, Xs[B][:B * K].view(B, K), N, out=Ys[B][:B * N].view(B, N), flags=P.FLAG_OVERLAP_PRECEDING)
+        us = timed(step, a.launches, a.warmup)
+        print(json.dumps({"case": "sweep", "us_per_step_eager": round(us, 1)}))
+        return 0
+    N, K, B = a.N, a.K, a.B
+    W = P.random_weights(N, K, seed=7)
+    if a.case == "gemm":
+        X = P.fill_normal(a.M * K, seed=11).view(a.M, K)
+        ws = torch.zeros(P.gemm_workspace_bytes(K, a.M), dtype=torch.uint8, device="cuda")
+        Y = torch.empty((a.M, N), dtype=torch.float32, device="cuda")
+        us = timed(lambda: P.gemm(W, X, N, workspace=ws, out=Y), a.launches, a.warmup)
+        print(json.dumps({"case": "gemm", "N": N, "K": K, "M": a.M, "us_per_call": round(us, 2),
+                          "tops": round(2.0 * a.M * N * K / (us * 1e-6) / 1e12, 1)}))
+        return 0
+    X = P.fill_normal(B * K, seed=11).view(B, K)
+    Y = torch.empty((B, N), dtype=torch.float32, device="cuda")
+    if a.act == "f32":
+        ws = torch.zeros(P.gemv_workspace_bytes(K, N, B), dtype=torch.uint8, device="cuda")
+        run = lambda: P.gemv(W, X, N, workspace=ws, out=Y)
+    else:
+        q8 = P.q8_1_quantize(X)
+        ws = torch.zeros(max(P.gemv_q8_workspace_bytes(K, N, B), 1), dtype=torch.uint8, device="cuda")
+        run = lambda: P.gemv_q8(W, q8, K, N, B, out=Y, workspace=ws)
+    us = timed(run, a.launches, a.warmup)
+    nb = gemv_bytes(N, K, B)
+    print(json.dumps({"case": "gemv", "N": N, "K": K, "B": B, "act": a.act, "us_per_launch": round(us, 2),
+                      "algorithmic_bytes": nb, "gbs": round(nb / (us * 1e-6) / 1e9, 1)}))
+    return 0
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def main():
+    if "--case" in sys.argv[1:]:
+        return run_case(sys.argv[1:])
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=400)
@@ -583,6 +862,7 @@ def main():
 
     gemm_per, gemm_tops, sharded, decoder = [], None, [], None
     bpeak, bpeak_kind = bf16_peak()
+    c1 = c1_gemv(P, dev, stream)
     if args.extras == "all":
         # ---- prefill GEMM sweep (reported beside the headline)
         gemm_per, gemm_tops = gemm_sweep(P, weights, dev, stream)
@@ -591,7 +871,14 @@ def main():
         # ---- synthetic decoder, tensor-parallel over the ranks
         del weights
         torch.cuda.empty_cache()
-        decoder = decoder_run(P, dev, rank, world, barrier)
+        decoder, c5_logits = decoder_run(P, dev, rank, world, barrier)
+    parity = None
+    if world > 1:
+        # ---- multi-GPU results against single-GPU results (outside every timed region)
+        parity = multi_gpu_parity(P, dev, rank, world, c5_logits if args.extras == "all" else None)
+        flags = torch.tensor([1.0 if parity["ok"] else 0.0], dtype=torch.float64, device=dev)
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+        parity["ok_all_ranks"] = bool(flags.item() == 1.0)
 
     torch.cuda.synchronize()
     err = P.device_error()
@@ -607,6 +894,7 @@ def main():
         threads = O.host_threads()
         gbs, _, sample = run_cpu_reference(threads, args.cpu_rows, 2, 1, kind)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample}
+        c1["cpu_reference"] = c1_cpu_reference(threads, kind)
 
     for g in graphs:
         del g
@@ -645,6 +933,8 @@ def main():
                              "unit": "TFLOP/s", "frac": round(gemm_tops / bpeak, 4), "peak_kind": bpeak_kind,
                              "kernel": "gemm_iq4xs_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators)"},
                 "per_shape": gemm_per},
+            "c1": c1,
+            "parity": parity,
             "decoder": decoder,
             "sharded": {"what": "row-sharded over the ranks (strong scaling), all-gather of the outputs (GEMV: "
                                 "NVLink peer-memory pull kernel, GEMM: NCCL), time = max over ranks",
@@ -654,6 +944,8 @@ def main():
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    if parity is not None and not parity["ok_all_ranks"]:
+        return 3  # a multi-GPU result disagrees with the single-GPU one
     return 0
 
 

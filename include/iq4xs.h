@@ -126,9 +126,13 @@ int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, int64_t K, i
 /* ------------------------------------------------------------------------------------------ */
 /* Prefill GEMM (tensor cores): Y[M][N] = X[M][K] (fp32, quantised per 32-block with Q8_1
  * semantics inside the call) times W^T (IQ4_XS [N][K/256]), ggml layouts.  Same per-sub-block
- * arithmetic as the stock GEMM (real_stock_dp4a_comparator.hip:375-443).  K % 512 == 0 (whole
- * super-block pairs, the tensor-map granule); M, N >= 1.  The workspace holds the quantised
- * activations (iq4xs_gemm_workspace_bytes(K, M) bytes, 256-byte aligned, no zeroing needed).
+ * arithmetic as the stock GEMM (real_stock_dp4a_comparator.hip:375-443).  K % 256 == 0; M, N >= 1.
+ * K % 512 == 0 (whole super-block pairs, the tensor-map granule; W 16-byte aligned) runs the
+ * tensor-core kernel.  An odd K/256 gives rows no tensor map can address: those calls quantise X to
+ * Q8_1 in the workspace and run the direct-load GEMV kernel 8 tokens at a time (same arithmetic,
+ * much slower), for the ggml output layout only (Y [M][N]; other layouts: unsupported shape).
+ * The workspace holds the quantised activations (iq4xs_gemm_workspace_bytes(K, M) bytes, 256-byte
+ * aligned, no zeroing needed).
  * Replaces gemm_iq4xs_stock_dp4a_gpu / gemm_iq4xs_wmma_stream_gpu (which allocate per call). */
 size_t iq4xs_gemm_workspace_bytes(int64_t K, int64_t M);
 int iq4xs_gemm(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
@@ -188,7 +192,8 @@ cudaError_t quantize_row_q8_1_gpu(const float* x, void* y, int64_t K, cudaStream
 cudaError_t quantize_row_q8_1_batched_gpu(const float* X, void* Y, int64_t K, int64_t M, cudaStream_t stream);
 
 /* real_stock_dp4a_comparator.hip:505-548 and impl_gemm_wmma_stream.hip:321-350: playground layouts
- * X [K][M] (X[k*M+m]) and Y [N][M] (Y[n*M+m]); both run the tensor-core GEMM (K % 512 == 0). */
+ * X [K][M] (X[k*M+m]) and Y [N][M] (Y[n*M+m]); both run the tensor-core GEMM (K % 512 == 0; an odd
+ * K/256 is refused in this output layout). */
 cudaError_t gemm_iq4xs_stock_dp4a_gpu(const void* W, const float* X, float* Y, int64_t K, int64_t N,
                                       int64_t M, cudaStream_t stream);
 cudaError_t gemm_iq4xs_wmma_stream_gpu(const void* W, const float* X, float* Y, int64_t K, int64_t N,
@@ -200,7 +205,8 @@ cudaError_t gemm_iq4xs_wmma_stream_gpu(const void* W, const float* X, float* Y, 
  * GEMV handles M = 1..8 (the patch: M == 1 and three fixed shapes); the batched dispatch is the
  * M > 1 form of the same call.  Any non-success status lets the caller fall back to stock.
  * The GEMV dispatches treat W as static model weights (IQ4XS_FLAG_OVERLAP_PRECEDING).
- * GEMM can_handle: IQ4_XS, M >= 16 (the patch's gate), K % 512 == 0, N >= 1. */
+ * GEMM can_handle: IQ4_XS, M >= 16 (the patch's gate), K % 256 == 0, N >= 1 (patch:148-151; the
+ * patch's N % 16 gate is dropped: every N is served). */
 bool custom_gemv_iq4xs_can_handle(int64_t K, int64_t N, int64_t M, int type);
 cudaError_t custom_gemv_iq4xs_dispatch(const void* W, const float* x, float* y, int64_t K, int64_t N,
                                        cudaStream_t stream);

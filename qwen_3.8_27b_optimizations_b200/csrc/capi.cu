@@ -4,6 +4,7 @@
 // (kernels/matmul_iq4xs/impl_gemv_dp4a_gfx1100.hip:291-329, real_stock_dp4a_comparator.hip:266-315,
 // patches/0001-gfx1100-mul-mat-custom.patch:148-154,261-280): null pointers, K % 256, non-positive
 // sizes are rejected before any launch; nothing aborts; errors come back as status codes.
+#include <algorithm>
 #include <atomic>
 #include <cstring>
 #include <map>
@@ -293,14 +294,36 @@ int iq4xs_dequantize(const void* W, float* out, int64_t K, int64_t N, cudaStream
 }
 
 // ------------------------------------------------------------------------------ GEMM
+// K/256 odd: the rows are 8 mod 16 bytes long, which no tensor map can address, so the tensor-core
+// GEMM does not take them (the ggml hook accepts them all the same, patch:148-151).
+static bool gemm_odd_superblocks(int64_t K) { return (K / kQK) % 2 != 0; }
+
 static int check_gemm(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M) {
     int s = check_matrix(W, K, N);
     if (s) return s;
     if (!X || !Y) return IQ4XS_ERR_INVALID_ARGUMENT;
     if (M <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
-    if (K % 512 != 0 || M > ((int64_t)1 << 30) || N > ((int64_t)1 << 30) || K > ((int64_t)1 << 24))
-        return IQ4XS_ERR_UNSUPPORTED_SHAPE;
-    if (!aligned(W, 16) || !aligned(X, 4) || !aligned(Y, 4)) return IQ4XS_ERR_MISALIGNED;
+    if (M > ((int64_t)1 << 30) || N > ((int64_t)1 << 30) || K > ((int64_t)1 << 24)) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(X, 4) || !aligned(Y, 4)) return IQ4XS_ERR_MISALIGNED;
+    if (!gemm_odd_superblocks(K) && !aligned(W, 16)) return IQ4XS_ERR_MISALIGNED;
+    return IQ4XS_OK;
+}
+
+// Odd super-block count (ggml output layout only, Y [M][N]): the call's tokens are quantised to Q8_1
+// into the workspace (the same bytes as the GEMM's own quantiser), then the direct-load GEMV kernel
+// runs on them 8 tokens at a time -- the same per-sub-block arithmetic, the same fp32 term.
+static int gemm_odd_k(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M, int64_t xsm,
+                      int64_t xsk, void* workspace, cudaStream_t stream) {
+    uint8_t* q8 = static_cast<uint8_t*>(workspace);
+    cudaError_t e = launch_q8_1_quantize(X, q8, K, M, xsm, xsk, stream, true, false);
+    if (e != cudaSuccess) return IQ4XS_ERR_CUDA;
+    const int64_t blk = (K / kQK8) * kQ8Bytes;  // Q8_1 bytes of one token
+    for (int64_t m0 = 0; m0 < M; m0 += IQ4XS_MAX_GEMV_BATCH) {
+        const int64_t B = std::min<int64_t>(IQ4XS_MAX_GEMV_BATCH, M - m0);
+        GemvArgs a = make_gemv_args(W, q8 + m0 * blk, Y + m0 * N, K, N);
+        e = launch_gemv_q8(a, (int)B, stream, m0 == 0);  // the first waits for the quantiser (PDL)
+        if (e != cudaSuccess) return IQ4XS_ERR_CUDA;
+    }
     return IQ4XS_OK;
 }
 
@@ -312,6 +335,10 @@ static int gemm_strided(const void* W, const float* X, float* Y, int64_t K, int6
     if (!workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
     if (workspace_bytes < gemm_workspace_bytes(K, M)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
     if (!aligned(workspace, 256)) return IQ4XS_ERR_MISALIGNED;
+    if (gemm_odd_superblocks(K)) {
+        if (ysm != N || ysn != 1) return IQ4XS_ERR_UNSUPPORTED_SHAPE;  // only the ggml output layout
+        return gemm_odd_k(W, X, Y, K, N, M, xsm, xsk, workspace, stream);
+    }
     const uint32_t lut[4] = {kNegLo0, kNegLo1, kPosHi0, kPosHi1};
     return status_from(launch_gemm(static_cast<const uint8_t*>(W), X, Y, K, N, M, xsm, xsk, ysm, ysn, workspace, stream,
                                    device_error_word(), lut));
@@ -403,7 +430,7 @@ cudaError_t custom_gemv_iq4xs_dispatch_batched(const void* W, const float* x, fl
 bool custom_gemm_iq4xs_can_handle(int64_t K, int64_t N, int64_t M, int type) {
     if (type != IQ4XS_GGML_TYPE_IQ4_XS) return false;
     if (M < 16) return false;  // patch:149: smaller batches stay on the GEMV path
-    if (K <= 0 || N <= 0 || K % 512 != 0) return false;
+    if (K <= 0 || N <= 0 || K % kQK != 0) return false;  // patch:150 (the N % 16 gate is not needed)
     return true;
 }
 

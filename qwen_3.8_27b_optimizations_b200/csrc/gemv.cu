@@ -20,6 +20,7 @@
 //  * every mbarrier wait is bounded; a timeout records a device error code and the kernel
 //    drains its in-flight copies and returns.
 #include <atomic>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -243,6 +244,13 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
         // ------------------------------------------------------------------ producer: one copy per stage
         if (lane == 0) {
             const uint64_t policy = l2_policy_evict_first();
+            // Stages beyond the ring are prefetched into L2 `a.prefetch` stages ahead of their copy.
+            auto prefetch_tile = [&](int t) {
+                const int64_t row0 = r0 + (int64_t)t * R;
+                bulk_prefetch_l2(a.W + row0 * a.rb, (uint32_t)(imin64(R, r1 - row0) * a.rb));
+            };
+            const int pf0 = min(ntiles, stages + a.prefetch);
+            for (int t = stages; t < pf0; ++t) prefetch_tile(t);
             uint32_t it = 0;
             for (int t = 0; t < ntiles; ++t, ++it) {
                 const int s = (int)(it % stages);
@@ -252,6 +260,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
                 const uint32_t bytes = (uint32_t)(imin64(R, r1 - row0) * a.rb);
                 mbar_arrive_expect_tx(&full[s], bytes);
                 bulk_g2s_evict_first(ring + (size_t)s * stage_bytes, a.W + row0 * a.rb, bytes, &full[s], policy);
+                if (t >= stages && t + a.prefetch < ntiles) prefetch_tile(t + a.prefetch);
             }
             const uint32_t first = it > (uint32_t)stages ? it - stages : 0u;
             for (uint32_t j = first; j < it; ++j) {
@@ -496,6 +505,20 @@ constexpr int kRowNCW = 12, kRowRPW = 2;
 // it the standalone quantizer launch is cheaper, measured on B200 at K = 8192 and 17408)
 constexpr int kRowFusedMaxK = 6144;
 
+// Warps per row (kw) and sub-block slots per lane (spl) of the row kernel for K at batch B; false when
+// even four warps per row would need more than the lane's register budget (the launch then takes the
+// tensor-core kernel).
+bool row_split(int64_t K, int B, int* kw_out, int* spl_out) {
+    const int64_t nsb = K / kQK8;
+    const int spl_max = (B == 1) ? 5 : 2;
+    int kw = 1;
+    while (kw < 4 && (nsb + 32 * kw - 1) / (32 * kw) > spl_max) kw *= 2;
+    const int64_t spl = (nsb + 32 * kw - 1) / (32 * kw);
+    *kw_out = kw;
+    *spl_out = (int)(spl < 1 << 20 ? spl : 1 << 20);
+    return spl <= spl_max;
+}
+
 template <int B, int SPL, bool kDebug, int kAct>
 void* rows_kernel_ptr_t(bool tail) {
     return tail ? (void*)gemv_iq4xs_q8_rows_kernel<B, SPL, kRowRPW, kRowNCW, true, kDebug, kAct>
@@ -517,11 +540,8 @@ template <int B, bool kDebug>
 cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int smem_optin) {
     constexpr int NCW = kRowNCW, RPW = kRowRPW;
     const int nsb = a.K / kQK8;
-    const int spl_max = (B == 1) ? 5 : 2;
-    int kw = 1;
-    while (kw < 4 && (nsb + 32 * kw - 1) / (32 * kw) > spl_max) kw *= 2;
-    const int spl = (nsb + 32 * kw - 1) / (32 * kw);
-    if (spl > spl_max) {  // K too long for register-resident activations: tensor-core kernel
+    int kw = 1, spl = 1;
+    if (!row_split(a.K, B, &kw, &spl)) {  // K too long for register-resident activations: tensor-core kernel
         if (a.act.mode == kActNorm) return cudaErrorNotSupported;
         return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.partials, a.partial_bytes, a.K, a.N,
                                B, stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
@@ -547,6 +567,7 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
                           (int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes, q8b).total > kRowSmemTarget + q8b))
         --stages;
     a.stages = stages;
+    a.prefetch = gemv_prefetch_rows();
     const RowSmem L = gemv_row_smem(B, R, kw, stages, stage_bytes, q8b);
     if ((int64_t)L.total > smem_optin || stage_bytes >= (1 << 20)) return cudaErrorInvalidConfiguration;
     void* kern = nullptr;
@@ -615,8 +636,34 @@ cudaError_t dispatch(int B, GemvArgs a, cudaStream_t stream, bool pdl) {
 }
 }  // namespace
 
+namespace {
+int env_int(const char* name, int dflt) {
+    const char* v = std::getenv(name);
+    if (!v || !*v) return dflt;
+    const int x = std::atoi(v);
+    return x < 0 ? 0 : (x > 64 ? 64 : x);
+}
+}  // namespace
+
+int gemv_prefetch_rows() {
+    static const int v = env_int("IQ4XS_GEMV_PREFETCH_ROWS", 0);
+    return v;
+}
+
+int gemv_prefetch_mma() {
+    static const int v = env_int("IQ4XS_GEMV_PREFETCH_MMA", 0);
+    return v;
+}
+
 bool gemv_bulk_path(const uint8_t* W, int64_t K) {
     return ((K / kQK) % 2 == 0) && ((reinterpret_cast<uintptr_t>(W) & 15u) == 0);
+}
+
+bool gemv_takes_mma(const uint8_t* W, int64_t K, int B) {
+    if (!gemv_bulk_path(W, K)) return false;  // the direct-load kernel writes no partial sums
+    if (B > 1) return true;
+    int kw = 1, spl = 1;
+    return !row_split(K, 1, &kw, &spl);
 }
 
 cudaError_t ensure_dynamic_smem(const void* kern, int bytes) {

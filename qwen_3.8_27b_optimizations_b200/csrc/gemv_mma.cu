@@ -104,11 +104,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
-__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+// L2 prefetch of one tensor-map box (no shared-memory destination, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, int c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+// d = a*b + (c, c, c, c): every accumulator starts at the same value c.
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c));
 }
 
 __device__ __forceinline__ uint32_t hi16(uint32_t x) {
@@ -164,6 +171,15 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
         // ------------------------------------------------------------------ producer
         if (lane == 0) {
             const uint64_t policy = l2_policy_evict_first();
+            // The ring holds S units; units beyond it are prefetched into L2 `a.prefetch` units ahead of
+            // their TMA load, so the load is served from L2 when its stage frees up.
+            auto prefetch_unit = [&](int j) {
+                const int64_t u = u0 + j;
+                const int p = (int)(u / T);
+                tma_prefetch_2d(&tmap, p * pk * 34, (int)((u - (int64_t)p * T) * 16));
+            };
+            const int pf0 = min(nunits, S + a.prefetch);
+            for (int j = S; j < pf0; ++j) prefetch_unit(j);
             int it = 0;
             for (; it < nunits; ++it) {
                 const int s = it % S;
@@ -174,6 +190,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                 const int64_t t = u - (int64_t)p * T;
                 mbar_arrive_expect_tx(&full[s], stage_bytes);
                 tma_load_2d(ring + (size_t)s * stage_bytes, &tmap, p * pk * 34, (int)(t * 16), &full[s], policy);
+                if (it >= S && it + a.prefetch < nunits) prefetch_unit(it + a.prefetch);
             }
             const int first = it > S ? it - S : 0;
             for (int j = first; j < it; ++j) {
@@ -330,10 +347,9 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
                                             prmt(a.lut[2], a.lut[3], hi16(xf0)), prmt(a.lut[2], a.lut[3], hi16(xf8))};
                     const uint32_t al[4] = {prmt(a.lut[0], a.lut[1], x0), prmt(a.lut[0], a.lut[1], x8),
                                             prmt(a.lut[0], a.lut[1], hi16(x0)), prmt(a.lut[0], a.lut[1], hi16(x8))};
-                    int dd[4] = {kMagicI, kMagicI, kMagicI, kMagicI};
-                    int dl[4] = {kMagicI, kMagicI, kMagicI, kMagicI};
-                    mma_s8(dd, ah, bf.x, bf.y);
-                    mma_s8(dl, al, bf.x, bf.y);
+                    int dd[4], dl[4];
+                    mma_s8(dd, ah, bf.x, bf.y, kMagicI);
+                    mma_s8(dl, al, bf.x, bf.y, kMagicI);
                     const float f0 = __shfl_sync(0xFFFFFFFFu, fq0[ib & 1], 4 * g + (ib >> 1));
                     const float f8 = __shfl_sync(0xFFFFFFFFu, fq8[ib & 1], 4 * g + (ib >> 1));
                     if constexpr (kDebug) {
@@ -537,6 +553,7 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     a.pk = pk;
     a.parts = parts;
     a.stages = stages;
+    a.prefetch = gemv_prefetch_mma();
     a.partial = partials;
     for (int i = 0; i < 4; ++i) a.lut[i] = lut[i];
     a.act.mode = kActQ8;

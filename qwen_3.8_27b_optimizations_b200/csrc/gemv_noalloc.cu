@@ -69,8 +69,12 @@ extern "C" int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, i
         return IQ4XS_ERR_MISALIGNED;
 
     // Scratch layout: [Q8_1 activations][partial sums], as the workspace of iq4xs_gemv_f32.
+    // Partial sums exist only on the tensor-core path, with the part count its launcher picks for
+    // this device (the same SM count and shared-memory limit the launch below looks up).
     const size_t q8_bytes = (size_t)(K / kQK8) * (size_t)B * kQ8Bytes;
-    const size_t partials = gemv_mma_partial_bytes_for(K, N, (int)B, device_sm_count(), device_smem_optin());
+    const size_t partials = gemv_takes_mma(static_cast<const uint8_t*>(W), K, (int)B)
+                                ? gemv_mma_partial_bytes_for(K, N, (int)B, device_sm_count(), device_smem_optin())
+                                : 0;
     const size_t need = align_up256(q8_bytes) + partials;
     if (need > kNoAllocScratchBytes) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
 
@@ -94,7 +98,7 @@ extern "C" int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, i
     a.lut[2] = kPosHi0;
     a.lut[3] = kPosHi1;
     a.partials = part;
-    a.partial_bytes = kNoAllocScratchBytes - align_up256(q8_bytes);
+    a.partial_bytes = partials;  // the size checked above: a launcher that wanted more fails loudly
     // The same activation policy as iq4xs_gemv_f32: from a 16-byte aligned X the GEMV launchers
     // quantise inside the kernel where that pays and otherwise run the standalone quantizer into q8.
     if ((reinterpret_cast<uintptr_t>(X) & 15u) == 0 && gemv_bulk_path(a.W, K)) {

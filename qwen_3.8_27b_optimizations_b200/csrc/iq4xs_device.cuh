@@ -239,6 +239,12 @@ __device__ __forceinline__ void bulk_g2s_evict_first(void* dst, const void* src,
         : "memory");
 }
 
+// Prefetch `bytes` (a multiple of 16, src 16-byte aligned) of global memory into L2; no completion
+// tracking, nothing lands in shared memory.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -115,6 +115,13 @@ def test_ggml_can_handle(pkg):
     assert not pkg.custom_gemv_iq4xs_can_handle(4096, 4096, 9)
     assert not pkg.custom_gemv_iq4xs_can_handle(4000, 4096, 1)
     assert not pkg.custom_gemv_iq4xs_can_handle(4096, 4096, 1, 12)  # another ggml type
+    # GEMM hook: the patch's gate (patch:148-151) -- M >= 16 and K % 256 == 0, odd K/256 included
+    assert pkg.custom_gemm_iq4xs_can_handle(5120, 17408, 16)
+    assert pkg.custom_gemm_iq4xs_can_handle(2304, 5120, 512)
+    assert pkg.custom_gemm_iq4xs_can_handle(768, 1000, 64)
+    assert not pkg.custom_gemm_iq4xs_can_handle(5120, 17408, 15)
+    assert not pkg.custom_gemm_iq4xs_can_handle(1000, 4096, 64)
+    assert not pkg.custom_gemm_iq4xs_can_handle(5120, 4096, 64, 12)
 
 
 def test_peer_validation(pkg):

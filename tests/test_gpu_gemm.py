@@ -150,7 +150,8 @@ def test_reference_named_gemm_layouts(pkg, O):
     assert torch.equal(Y, ref)
     assert pkg.custom_gemm_iq4xs_can_handle(K, N, M)
     assert not pkg.custom_gemm_iq4xs_can_handle(K, N, 8)       # small batches stay on the GEMV
-    assert not pkg.custom_gemm_iq4xs_can_handle(768, N, M)     # odd super-block count
+    assert pkg.custom_gemm_iq4xs_can_handle(768, N, M)         # odd super-block count (patch:150)
+    assert not pkg.custom_gemm_iq4xs_can_handle(1000, N, M)    # not whole super-blocks
     assert not pkg.custom_gemm_iq4xs_can_handle(K, N, M, 2)    # not IQ4_XS
     no_device_error(pkg)
 
@@ -190,10 +191,36 @@ def test_gemm_invalid_arguments(pkg, O):
     ws = torch.zeros(pkg.gemm_workspace_bytes(K, M), dtype=torch.uint8, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
     nb = ws.numel()
-    assert L.iq4xs_gemm(W.data_ptr(), X.data_ptr(), Y.data_ptr(), 768, N, M, ws.data_ptr(), nb, s) == 2
+    assert L.iq4xs_gemm(W.data_ptr(), X.data_ptr(), Y.data_ptr(), 1000, N, M, ws.data_ptr(), nb, s) == 2
+    # odd K/256 runs in the ggml output layout only
+    assert L.iq4xs_gemm_strided(W.data_ptr(), X.data_ptr(), 768, 1, Y.data_ptr(), 1, M, 768, N, M, ws.data_ptr(),
+                                nb, s) == 2
     assert L.iq4xs_gemm(W.data_ptr(), X.data_ptr(), Y.data_ptr(), K, N, 0, ws.data_ptr(), nb, s) == 1
     assert L.iq4xs_gemm(None, X.data_ptr(), Y.data_ptr(), K, N, M, ws.data_ptr(), nb, s) == 1
     assert L.iq4xs_gemm(W.data_ptr(), X.data_ptr(), Y.data_ptr(), K, N, M, ws.data_ptr(), nb - 1, s) == 4
     assert L.iq4xs_gemm(W.data_ptr() + 8, X.data_ptr(), Y.data_ptr(), K, N - 1, M, ws.data_ptr(), nb, s) == 3
     assert L.iq4xs_gemm(W.data_ptr(), X.data_ptr(), Y.data_ptr(), K, N, M, ws.data_ptr(), nb, s) == 0
+    no_device_error(pkg)
+
+
+@pytest.mark.parametrize("K,N,M", [(768, 640, 16), (2304, 1000, 100), (1280, 272, 37)])
+def test_gemm_odd_superblock_count(pkg, O, K, N, M):
+    """K/256 odd (the patch's hook takes any K % 256 == 0, patch:148-151): the ggml dispatch and
+    iq4xs_gemm quantise to Q8_1 and run the direct-load kernel 8 tokens at a time; checked against
+    the C oracle of the quantised pipeline (tolerance) and the batched GEMV on the same tokens (bits)."""
+    W = dev(O.random_blocks(K, N, 777 + K))
+    X = O.normal(M * K, 31 + M).reshape(M, K)
+    Xd = dev(X)
+    assert pkg.custom_gemm_iq4xs_can_handle(K, N, M)
+    Y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    assert pkg.custom_gemm_iq4xs_dispatch(W, Xd, Y, K, N, M) == 0
+    Y2 = pkg.gemm(W, Xd, N)
+    torch.cuda.synchronize()
+    assert torch.equal(Y, Y2)
+    Q = O.quantize_q8_1(X)
+    Y64, A = O.matmul_q8(W.cpu().numpy(), Q, K, N, M)
+    check_close(O, Y.cpu().numpy(), Y64, A, K, f"odd K={K} N={N} M={M}")
+    for m0 in range(0, M, 8):  # the same bits as the GEMV entry point on each chunk of tokens
+        Yg = pkg.gemv(W, Xd[m0:m0 + 8].contiguous(), N)
+        assert torch.equal(Yg, Y[m0:m0 + 8])
     no_device_error(pkg)

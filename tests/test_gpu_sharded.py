@@ -1,5 +1,5 @@
-"""Row-sharded GEMV / GEMM through the CUDA path with NCCL (2 ranks when the box has 2 GPUs,
-otherwise 1), against the single-GPU kernels on the full matrix: the GEMM and the batch-1 GEMV
+"""Row-sharded GEMV / GEMM through the CUDA path with NCCL on 2 GPUs (skipped on a box with fewer),
+against the single-GPU kernels on the full matrix: the GEMM and the batch-1 GEMV
 are per-row identical (bit-exact), batched GEMV partial sums may be split differently (tolerance)."""
 import os
 
@@ -54,7 +54,9 @@ def _worker(rank, world, port, q):
 
 
 def test_row_sharded_nccl():
-    world = min(2, torch.cuda.device_count())
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
     from conftest import run_ranks
     out, codes = run_ranks(_worker, world, lambda r, port, q: (r, world, port, q), timeout=300)
     assert all(c == 0 for c in codes), codes

@@ -44,6 +44,40 @@ def test_noalloc_matches_workspace_entry_point(pkg, O, N, K, B):
     assert pkg.device_error() == 0
 
 
+def test_noalloc_batch1_long_rows_need_no_partials(pkg):
+    # Batch 1 with K <= 20480 runs the row kernel, which writes no partial sums: only the 18 KiB of
+    # Q8_1 activations count against the static scratch, so an lm_head-sized N is accepted.  (The
+    # tensor-core path at this shape would want ~4.3 MiB of partial sums.)
+    N, K, B = 152064, 16384, 1
+    W = pkg.random_weights(N, K, seed=5160)
+    ws = torch.zeros(pkg.gemv_workspace_bytes(K, N, B), dtype=torch.uint8, device="cuda")
+    for call in range(2):
+        X = pkg.fill_normal(B * K, seed=300 + call).view(B, K)
+        st, Y = call_noalloc(pkg, W, X, N)
+        assert st == 0, pkg.STATUS.get(st)
+        Yref = pkg.gemv(W, X, N, workspace=ws)
+        torch.cuda.synchronize()
+        assert torch.equal(Y, Yref)
+    assert pkg.device_error() == 0
+
+
+@pytest.mark.parametrize("N,K,B,x_offset", [(3000, 4096, 2, 1), (2048, 768, 3, 0), (1000, 2304, 1, 1)])
+def test_noalloc_fallback_paths(pkg, N, K, B, x_offset):
+    # The standalone quantizer into the static array, then the GEMV on those Q8_1 blocks: taken when X
+    # is not 16-byte aligned (x_offset = 1 float) or when K/256 is odd (the direct-load kernel).
+    W = pkg.random_weights(N, K, seed=5170 + K)
+    ws = torch.zeros(pkg.gemv_workspace_bytes(K, N, B), dtype=torch.uint8, device="cuda")
+    for call in range(2):
+        buf = pkg.fill_normal(B * K + 4, seed=400 + call)
+        X = buf[x_offset:x_offset + B * K].view(B, K)
+        st, Y = call_noalloc(pkg, W, X, N)
+        assert st == 0, pkg.STATUS.get(st)
+        Yref = pkg.gemv(W, X, N, workspace=ws)
+        torch.cuda.synchronize()
+        assert torch.equal(Y, Yref)
+    assert pkg.device_error() == 0
+
+
 def test_noalloc_rejects_oversized_scratch(pkg):
     # K = 524288 at batch 8 needs 4.5 MiB of Q8_1 activations alone, more than the 4 MiB of static
     # scratch: refused before any launch (W and X are full size all the same).
