@@ -601,10 +601,11 @@ def run_case(argv) -> int:
       --case gemm --N 17408 --K 5120 --M 2048             the prefill GEMM
       --case attention --pos 512                          the decoder's decode attention (64 / 8 heads)
       --case sweep                                        one benchmark sweep step, eager launches
+      --case grouped --B 8                                one grouped call over the six layer shapes
     The default N (twice the gate|up projection) keeps the weights above the 126 MB L2."""
     import torch
     ap = argparse.ArgumentParser(prog="bench.py --case")
-    ap.add_argument("--case", required=True, choices=["gemv", "gemm", "attention", "sweep"])
+    ap.add_argument("--case", required=True, choices=["gemv", "gemm", "attention", "sweep", "grouped"])
     ap.add_argument("--N", type=int, default=69632)
     ap.add_argument("--K", type=int, default=5120)
     ap.add_argument("--B", type=int, default=1)
@@ -657,6 +658,17 @@ def run_case(argv) -> int:
                     P.gemv(W, Xs[B][:B * K].view(B, K), N, out=Ys[B][:B * N].view(B, N), flags=P.FLAG_OVERLAP_PRECEDING)
         us = timed(step, a.launches, a.warmup)
         print(json.dumps({"case": "sweep", "us_per_step_eager": round(us, 1)}))
+        return 0
+    if a.case == "grouped":
+        B = a.B
+        Ws = [P.random_weights(N, K, seed=i) for i, (_, N, K) in enumerate(SHAPES)]
+        Xs = [P.fill_normal(B * K, seed=50 + i).view(B, K) for i, (_, N, K) in enumerate(SHAPES)]
+        Ys = [torch.empty((B, N), dtype=torch.float32, device="cuda") for _, N, K in SHAPES]
+        gws = torch.zeros(P.gemv_grouped_workspace_bytes([(K, N) for _, N, K in SHAPES], B), dtype=torch.uint8,
+                          device="cuda")
+        us = timed(lambda: P.gemv_grouped(list(zip(Ws, Xs, Ys)), workspace=gws), a.launches, a.warmup)
+        nb = sum(gemv_bytes(N, K, B) for _, N, K in SHAPES)
+        print(json.dumps({"case": "grouped", "B": B, "us_per_call": round(us, 2), "gbs": round(nb / (us * 1e-6) / 1e9, 1)}))
         return 0
     N, K, B = a.N, a.K, a.B
     W = P.random_weights(N, K, seed=7)
@@ -728,29 +740,41 @@ def main():
     X = {(B, i): P.fill_normal(B * K, seed=42 + B + 31 * i + 7919 * rank).view(B, K)
          for B in BATCHES for i, (_, N, K) in enumerate(SHAPES)}
     Y = {(B, i): torch.empty((B, N), dtype=torch.float32, device=dev) for B in BATCHES for i, (_, N, K) in enumerate(SHAPES)}
-    maxK = max(K for _, _, K in SHAPES)
     ws = torch.zeros(max(P.gemv_workspace_bytes(K, N, B) for B in BATCHES for _, N, K in SHAPES), dtype=torch.uint8,
                      device=dev)
+    gws = torch.zeros(max(P.gemv_grouped_workspace_bytes([(K, N) for _, N, K in SHAPES], B) for B in BATCHES),
+                      dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
 
     def step(c: int, s):
+        """The measured step: per batch size one grouped call over the six layer GEMVs."""
+        for B in BATCHES:
+            P.gemv_grouped([(weights[c][i], X[(B, i)], Y[(B, i)]) for i in range(len(SHAPES))], workspace=gws,
+                           stream=s, flags=P.FLAG_OVERLAP_PRECEDING)
+
+    def step_single(c: int, s):
+        """The same 24 GEMVs as one iq4xs_gemv_f32 call each (reported beside the headline)."""
         for B in BATCHES:
             for i, (_, N, K) in enumerate(SHAPES):
                 P.gemv(weights[c][i], X[(B, i)], N, workspace=ws, out=Y[(B, i)], stream=s, flags=P.FLAG_OVERLAP_PRECEDING)
 
-    # capture one graph per weight copy
-    graphs = []
-    with torch.cuda.stream(stream):
-        step(0, stream)
-        step(1, stream)
-        stream.synchronize()
-        for c in range(2):
-            g = torch.cuda.CUDAGraph(keep_graph=True)  # keep the cudaGraph_t: its kernel nodes are counted
-            with torch.cuda.graph(g, stream=stream):
-                step(c, stream)
-            g.instantiate()
-            graphs.append(g)
-    torch.cuda.synchronize()
+    def capture(fn):
+        gs = []
+        with torch.cuda.stream(stream):
+            fn(0, stream)
+            fn(1, stream)
+            stream.synchronize()
+            for c in range(2):
+                g = torch.cuda.CUDAGraph(keep_graph=True)  # keep the cudaGraph_t: its kernel nodes are counted
+                with torch.cuda.graph(g, stream=stream):
+                    fn(c, stream)
+                g.instantiate()
+                gs.append(g)
+        torch.cuda.synchronize()
+        return gs
+
+    # one graph per weight copy
+    graphs = capture(step)
 
     def barrier():
         if world > 1:
@@ -789,47 +813,78 @@ def main():
     value_gbs = world * sb * args.steps / (ms_max * 1e-3) / 1e9
     clocks = clk.summary()
 
-    # ---- roofline: the GEMV kernel alone (no quantizer), per launch: a CUDA graph of `reps`
-    # back-to-back launches over the two weight copies, timed with events on its stream
+    # ---- the same sweep as 24 single-matrix calls (graph-replayed; reported beside the headline)
+    graphs_single = capture(step_single)
+    with torch.cuda.stream(stream):
+        for w in range(args.warmup):
+            graphs_single[w % 2].replay()
+        a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for k in range(args.steps):
+            graphs_single[k % 2].replay()
+        b0.record(stream)
+        stream.synchronize()
+    single_ms = a0.elapsed_time(b0) / args.steps
+    single = {"what": "the same 24 GEMVs, one iq4xs_gemv_f32 call each (CUDA graph replay)",
+              "GBs": round(world * step_bytes() / (single_ms * 1e-3) / 1e9, 1), "ms_per_step": round(single_ms, 4),
+              "launches_per_step": graph_kernel_nodes(graphs_single[0])}
+    graphs_single.clear()
+
+    # ---- roofline: per grouped launch (quantiser + grouped GEMV kernel + part sums), a CUDA graph of
+    # `reps` back-to-back calls over the two weight copies, timed with events on its stream; and the
+    # single-matrix GEMV kernel per shape (Q8_1 input, part sums included) for reference
+    peak, peak_kind = hbm_peak()
+    reps = 10
+
+    def graph_time(call):
+        with torch.cuda.stream(stream):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for r in range(reps):
+                    call(r % 2)
+            g.replay()
+            stream.synchronize()
+            ts = []
+            for _ in range(3):
+                a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                g.replay()
+                b0.record(stream)
+                stream.synchronize()
+                ts.append(a0.elapsed_time(b0) / reps)
+        del g
+        return statistics.median(ts)
+
     per = []
+    tot_bytes, tot_ms = 0, 0.0
+    for B in BATCHES:
+        d = graph_time(lambda c, B=B: P.gemv_grouped([(weights[c][i], X[(B, i)], Y[(B, i)]) for i in range(len(SHAPES))],
+                                                     workspace=gws, stream=stream, flags=P.FLAG_OVERLAP_PRECEDING))
+        nb = sum(gemv_bytes(N, K, B) for _, N, K in SHAPES)
+        per.append({"B": B, "gemvs": len(SHAPES), "us": round(d * 1e3, 2), "gbs": round(nb / (d * 1e-3) / 1e9, 1),
+                    "frac": round(nb / (d * 1e-3) / 1e9 / peak, 4)})
+        tot_bytes += nb
+        tot_ms += d
+    achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
+    per_single = []
     q8s = {(B, i): P.q8_1_quantize(X[(B, i)], stream=stream) for B in BATCHES for i in range(len(SHAPES))}
     stream.synchronize()
-    reps = 10
-    tot_bytes, tot_ms = 0, 0.0
-    with torch.cuda.stream(stream):
-        for B in BATCHES:
-            for i, (name, N, K) in enumerate(SHAPES):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    for r in range(reps):
-                        P.gemv_q8(weights[r % 2][i], q8s[(B, i)], K, N, B, out=Y[(B, i)], stream=stream, workspace=ws)
-                g.replay()
-                stream.synchronize()
-                ts = []
-                for _ in range(3):
-                    a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    a0.record(stream)
-                    g.replay()
-                    b0.record(stream)
-                    stream.synchronize()
-                    ts.append(a0.elapsed_time(b0) / reps)
-                del g
-                d = statistics.median(ts)
-                nb = gemv_bytes(N, K, B)
-                per.append({"shape": name, "B": B, "us": round(d * 1e3, 2), "gbs": round(nb / (d * 1e-3) / 1e9, 1)})
-                tot_bytes += nb
-                tot_ms += d
-    achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
-    peak, peak_kind = hbm_peak()
+    for B in BATCHES:
+        for i, (name, N, K) in enumerate(SHAPES):
+            d = graph_time(lambda c, B=B, i=i, N=N, K=K: P.gemv_q8(weights[c][i], q8s[(B, i)], K, N, B, out=Y[(B, i)],
+                                                                  stream=stream, workspace=ws))
+            nb = gemv_bytes(N, K, B)
+            per_single.append({"shape": name, "B": B, "us": round(d * 1e3, 2), "gbs": round(nb / (d * 1e-3) / 1e9, 1)})
     # DRAM traffic per launch: the dominant kernel's ncu ratio (dram read+write / algorithmic bytes,
-    # captured on a 69632 x 5120 case) scaled to the mean algorithmic bytes of the sweep's launches.
+    # captured on a smaller case) scaled to the mean algorithmic bytes of the step's launches.
     traffic = ncu_traffic()
     traffic_per_launch, traffic_src = None, None
     if traffic:
-        k = traffic["kernels"]["gemv_iq4xs_q8_mma_kernel"]
+        kname, k = next(iter(traffic["kernels"].items()))
+        case = k.get("case") or f"{k.get('N')}x{k.get('K')} B={k.get('B')}"
         traffic_per_launch = round(k["traffic_ratio"] * tot_bytes / len(per))
-        traffic_src = (f"ncu dram__bytes_read+write of gemv_iq4xs_q8_mma_kernel on {k['N']}x{k['K']} B={k['B']} "
-                       f"(ratio {k['traffic_ratio']} of algorithmic), scaled to the mean launch of the sweep")
+        traffic_src = (f"ncu dram__bytes_read+write of {kname} on {case} (ratio {k['traffic_ratio']} of "
+                       f"algorithmic), scaled to the mean grouped launch of the step")
 
     # ---- e2e through the ggml hook from the C++ host loop, pinned host buffers
     e2e_steps = args.e2e_steps or args.steps
@@ -844,20 +899,29 @@ def main():
     hy = torch.empty(ny, dtype=torch.float32).pin_memory()
     dx = torch.empty(nx, dtype=torch.float32, device=dev)
     dy = torch.empty(ny, dtype=torch.float32, device=dev)
-    ems = C.c_float(0.0)
-    rc = L.iq4xs_bench_e2e_gemv(wptrs, Ks, Ns, len(SHAPES), Bs, len(BATCHES), hx.data_ptr(), hy.data_ptr(),
-                                dx.data_ptr(), dy.data_ptr(), max(args.warmup, 3), stream.cuda_stream, C.byref(ems))
-    if rc != 0:
-        raise RuntimeError(f"e2e warmup failed: cudaError {rc}")
-    barrier()
-    rc = L.iq4xs_bench_e2e_gemv(wptrs, Ks, Ns, len(SHAPES), Bs, len(BATCHES), hx.data_ptr(), hy.data_ptr(),
-                                dx.data_ptr(), dy.data_ptr(), e2e_steps, stream.cuda_stream, C.byref(ems))
-    if rc != 0:
-        raise RuntimeError(f"e2e failed: cudaError {rc}")
-    t = torch.tensor([float(ems.value)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_gbs = world * sb * e2e_steps / (float(t.item()) * 1e-3) / 1e9
+
+    def run_e2e(grouped: bool, steps: int) -> float:
+        ems = C.c_float(0.0)
+        if grouped:
+            rc = L.iq4xs_bench_e2e_gemv_grouped(wptrs, Ks, Ns, len(SHAPES), Bs, len(BATCHES), hx.data_ptr(),
+                                                hy.data_ptr(), dx.data_ptr(), dy.data_ptr(), gws.data_ptr(),
+                                                gws.numel(), steps, stream.cuda_stream, C.byref(ems))
+        else:
+            rc = L.iq4xs_bench_e2e_gemv(wptrs, Ks, Ns, len(SHAPES), Bs, len(BATCHES), hx.data_ptr(), hy.data_ptr(),
+                                        dx.data_ptr(), dy.data_ptr(), steps, stream.cuda_stream, C.byref(ems))
+        if rc != 0:
+            raise RuntimeError(f"e2e ({'grouped' if grouped else 'hook'}) failed: cudaError {rc}")
+        return float(ems.value)
+
+    e2e_val = {}
+    for grouped in (True, False):
+        run_e2e(grouped, max(args.warmup, 3))
+        barrier()
+        t = torch.tensor([run_e2e(grouped, e2e_steps)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_val[grouped] = world * sb * e2e_steps / (float(t.item()) * 1e-3) / 1e9
+    e2e_gbs, e2e_hook_gbs = e2e_val[True], e2e_val[False]
     h2d, d2h = 4 * nx, 4 * ny  # the bytes of the two copies of every step
 
     gemm_per, gemm_tops, sharded, decoder = [], None, [], None
@@ -913,19 +977,26 @@ def main():
             "config": {"workload": "decode_gemv_sweep_27b_layers", "shapes": {n: [N, K] for n, N, K in SHAPES},
                        "batches": BATCHES, "gemvs_per_step": len(SHAPES) * len(BATCHES),
                        "bytes_per_step": sb, "l2": "inputs larger than L2: 2 x 192 MB weight sets alternate, 768 MB streamed per step",
+                       "api": "iq4xs_gemv_grouped: one call per batch size over the six layer GEMVs",
                        "timing": "CUDA graph replay of the step, CUDA events on the launch stream, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic_per_launch,
                          "algorithmic_bytes_per_launch": round(tot_bytes / len(per)),
                          "traffic_source": traffic_src,
-                         "kernel": "gemv_iq4xs_q8_rows_kernel (B=1) / gemv_iq4xs_q8_mma_kernel (B=2..8)",
-                         "per_launch": per},
+                         "kernel": "gemv_rows_grouped_kernel (B=1) / gemv_mma_grouped_kernel (B=2..8), one grouped "
+                                   "launch per batch size (its quantiser and part-sum kernels included in the time)",
+                         "per_launch": per,
+                         "per_shape_single_kernel": per_single},
+            "single_calls": single,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "custom_gemv_iq4xs_dispatch_batched from a C++ host loop, pinned host x/y: each step "
-                            "uploads its activations in one copy and downloads its results in one copy, on two copy "
-                            "streams overlapping the neighbouring steps' GEMVs"},
+                    "path": "iq4xs_gemv_grouped (one call per batch size) from a C++ host loop, pinned host x/y: "
+                            "each step uploads its activations in one copy and downloads its results in one copy, "
+                            "on two copy streams overlapping the neighbouring steps' GEMVs",
+                    "hook_value": round(e2e_hook_gbs, 1),
+                    "hook_path": "the same loop through the ggml hook custom_gemv_iq4xs_dispatch_batched, one call "
+                                 "per GEMV"},
             "gemm": None if gemm_tops is None else {
                 "metric": "IQ4_XS prefill GEMM TOPS (2*M*N*K / time, Q8_1 quantisation included)",
                 "value": round(gemm_tops, 1), "unit": "TOPS", "tokens": GEMM_TOKENS,

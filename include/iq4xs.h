@@ -123,6 +123,30 @@ int iq4xs_gemv_f32_ex(const void* W, const float* X, float* Y, int64_t K, int64_
 int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, int64_t K, int64_t N, int64_t B,
                            cudaStream_t stream);
 
+/* Grouped decode GEMV: `count` (1..IQ4XS_MAX_GROUP) independent GEMVs of one batch size B in one
+ * launch sequence -- one Q8_1 quantiser for all activations, one GEMV grid whose CTAs are split over
+ * the matrices in proportion to their weight bytes, and (batch 2..8, when a matrix is split into K
+ * parts) one kernel adding the parts.  For the matrices of one decode step that a ggml graph keeps
+ * as separate tensors and feeds the same activations (attn_q / attn_k / attn_v, ffn_gate / ffn_up),
+ * or any set of independent GEMVs: the launch, ramp and tail of a GEMV are paid once per group.
+ * Each problem's output is that of iq4xs_gemv_f32 on the same inputs within the GEMV tolerance
+ * (batch 1: the same bits; batch 2..8 may split K into parts differently).  Y of one problem must not
+ * overlap any W, X or Y of the group.  Groups the grouped kernels do not take (W not 16-byte aligned,
+ * K % 512 != 0, batch 1 with K > 20480) run as one iq4xs_gemv_f32_ex per problem.
+ * workspace >= iq4xs_gemv_grouped_workspace_bytes(problems, count, B), 256-byte aligned, no zeroing.
+ * No counterpart in the reference (one GEMV per MUL_MAT node, patch:278-280). */
+#define IQ4XS_MAX_GROUP 8
+typedef struct iq4xs_gemv_problem {
+    const void* W;  /* IQ4_XS [N][K/256] (8-byte aligned) */
+    const float* X; /* fp32 [B][K] */
+    float* Y;       /* fp32 [B][N] */
+    int64_t K;
+    int64_t N;
+} iq4xs_gemv_problem;
+size_t iq4xs_gemv_grouped_workspace_bytes(const iq4xs_gemv_problem* problems, int count, int64_t B);
+int iq4xs_gemv_grouped(const iq4xs_gemv_problem* problems, int count, int64_t B, void* workspace,
+                       size_t workspace_bytes, unsigned flags, cudaStream_t stream);
+
 /* ------------------------------------------------------------------------------------------ */
 /* Prefill GEMM (tensor cores): Y[M][N] = X[M][K] (fp32, quantised per 32-block with Q8_1
  * semantics inside the call) times W^T (IQ4_XS [N][K/256]), ggml layouts.  Same per-sub-block

@@ -10,6 +10,7 @@
 #define IQ4XS_BENCH_H
 
 #include <cuda_runtime_api.h>
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -33,6 +34,14 @@ int64_t iq4xs_bench_e2e_floats(const int64_t* L, int nmat, const int64_t* batche
 int iq4xs_bench_e2e_gemv(const void* const* W, const int64_t* K, const int64_t* N, int nmat,
                          const int64_t* batches, int nbatch, const float* host_x, float* host_y,
                          float* dev_x, float* dev_y, int steps, cudaStream_t stream, float* ms);
+
+/* iq4xs_bench_e2e_gemv with one iq4xs_gemv_grouped call per batch size over the nmat matrices
+ * (nmat <= IQ4XS_MAX_GROUP) instead of one hook call per matrix; `workspace` holds at least
+ * iq4xs_gemv_grouped_workspace_bytes for the largest batch (256-byte aligned). */
+int iq4xs_bench_e2e_gemv_grouped(const void* const* W, const int64_t* K, const int64_t* N, int nmat,
+                                 const int64_t* batches, int nbatch, const float* host_x, float* host_y,
+                                 float* dev_x, float* dev_y, void* workspace, size_t workspace_bytes, int steps,
+                                 cudaStream_t stream, float* ms);
 
 #ifdef __cplusplus
 }

@@ -59,11 +59,21 @@ SIGNATURES = {
     "custom_gemv_iq4xs_dispatch_batched": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "custom_gemm_iq4xs_can_handle": (C.c_bool, [_i64, _i64, _i64, _i]),
     "custom_gemm_iq4xs_dispatch": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "iq4xs_gemv_grouped_workspace_bytes": (_sz, [_vp, _i, _i64]),
+    "iq4xs_gemv_grouped": (_i, [_vp, _i, _i64, _vp, _sz, C.c_uint, _vp]),
 }
+MAX_GROUP = 8
+
+
+class GemvProblem(C.Structure):
+    """iq4xs_gemv_problem (include/iq4xs.h)."""
+    _fields_ = [("W", _vp), ("X", _vp), ("Y", _vp), ("K", _i64), ("N", _i64)]
 # include/iq4xs_bench.h (measurement driver, not the matmul path)
 BENCH_SIGNATURES = {
     "iq4xs_bench_e2e_gemv": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _i, _vp, C.POINTER(C.c_float)]),
     "iq4xs_bench_e2e_floats": (_i64, [_vp, _i, _vp, _i]),
+    "iq4xs_bench_e2e_gemv_grouped": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _sz, _i, _vp,
+                                          C.POINTER(C.c_float)]),
 }
 
 # include/iq4xs_decoder.h (the decoder-step operations around the GEMVs)
@@ -203,6 +213,36 @@ def gemv_workspace_bytes(K: int, N: int, B: int) -> int:
 
 
 FLAG_OVERLAP_PRECEDING = 1
+
+
+def _problems(items):
+    arr = (GemvProblem * len(items))()
+    for i, (W, X, Y) in enumerate(items):
+        arr[i] = GemvProblem(_ptr(W), _ptr(X), _ptr(Y), X.shape[-1], Y.shape[-1])
+    return arr
+
+
+def gemv_grouped_workspace_bytes(shapes, B: int) -> int:
+    """Workspace bytes of iq4xs_gemv_grouped for problems of (K, N) shapes at batch B."""
+    arr = (GemvProblem * len(shapes))()
+    for i, (K, N) in enumerate(shapes):
+        arr[i] = GemvProblem(None, None, None, K, N)
+    return int(lib().iq4xs_gemv_grouped_workspace_bytes(arr, len(shapes), B))
+
+
+def gemv_grouped(items, workspace=None, stream=None, flags: int = 0):
+    """Independent GEMVs of one batch size in one launch sequence: items = [(W, X [B][K], Y [B][N])],
+    every X fp32 contiguous with the same B; each Y receives W . X^T (iq4xs_gemv_grouped)."""
+    B = items[0][1].shape[0]
+    for W, X, Y in items:
+        if X.dim() != 2 or X.shape[0] != B or not X.is_contiguous() or not Y.is_contiguous() or Y.shape[0] != B:
+            raise ValueError("every problem needs contiguous X [B][K] and Y [B][N] with the same B")
+    arr = _problems(items)
+    need = int(lib().iq4xs_gemv_grouped_workspace_bytes(arr, len(items), B))
+    ws = workspace if workspace is not None else _workspace(need, items[0][1].device)
+    _check("iq4xs_gemv_grouped", lib().iq4xs_gemv_grouped(arr, len(items), B, _ptr(ws), ws.numel() * ws.element_size(),
+                                                          flags, _stream(stream)))
+    return [Y for _, _, Y in items]
 
 
 def gemv(W, X, N: int, workspace=None, out=None, stream=None, flags: int = 0):

@@ -67,8 +67,15 @@ void pipe_destroy(Pipe& p) {
 
 // Pass `pass`: upload -> every hook call of the pass -> download.  Passes two apart share a slot and
 // are ordered by events.
+// Grouped mode: one iq4xs_gemv_grouped call per batch size over all matrices (workspace != null).
+struct Grouped {
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+};
+
 cudaError_t enqueue_pass(Pipe& p, int pass, const void* const* W, const int64_t* K, const int64_t* N, int nmat,
-                         const int64_t* batches, int nbatch, const float* host_x, float* host_y, cudaStream_t stream) {
+                         const int64_t* batches, int nbatch, const float* host_x, float* host_y, cudaStream_t stream,
+                         const Grouped& grouped) {
     const int slot = pass & 1;
     cudaError_t e = cudaSuccess;
     // upload: the slot's x is free once the compute of pass-2 has finished
@@ -80,13 +87,22 @@ cudaError_t enqueue_pass(Pipe& p, int pass, const void* const* W, const int64_t*
     if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, p.x_ready[slot], 0);
     if (e == cudaSuccess && pass >= 2) e = cudaStreamWaitEvent(stream, p.y_free[slot], 0);
     int64_t xo = 0, yo = 0;
-    for (int bi = 0; bi < nbatch && e == cudaSuccess; ++bi)
+    for (int bi = 0; bi < nbatch && e == cudaSuccess; ++bi) {
+        const int64_t b = batches[bi];
+        iq4xs_gemv_problem prob[IQ4XS_MAX_GROUP];
         for (int i = 0; i < nmat && e == cudaSuccess; ++i) {
-            const int64_t b = batches[bi];
-            e = custom_gemv_iq4xs_dispatch_batched(W[i], p.dx[slot] + xo, p.dy[slot] + yo, K[i], N[i], b, stream);
+            if (grouped.ws) {
+                prob[i] = {W[i], p.dx[slot] + xo, p.dy[slot] + yo, K[i], N[i]};
+            } else {
+                e = custom_gemv_iq4xs_dispatch_batched(W[i], p.dx[slot] + xo, p.dy[slot] + yo, K[i], N[i], b, stream);
+            }
             xo += seg_round(b * K[i]);
             yo += seg_round(b * N[i]);
         }
+        if (grouped.ws && e == cudaSuccess &&
+            iq4xs_gemv_grouped(prob, nmat, b, grouped.ws, grouped.ws_bytes, IQ4XS_FLAG_OVERLAP_PRECEDING, stream) != 0)
+            e = cudaErrorLaunchFailure;
+    }
     if (e == cudaSuccess) e = cudaEventRecord(p.done[slot], stream);
     // download
     if (e == cudaSuccess) e = cudaStreamWaitEvent(p.down, p.done[slot], 0);
@@ -101,9 +117,11 @@ extern "C" int64_t iq4xs_bench_e2e_floats(const int64_t* L, int nmat, const int6
     return pass_floats(L, nmat, batches, nbatch);
 }
 
-extern "C" int iq4xs_bench_e2e_gemv(const void* const* W, const int64_t* K, const int64_t* N, int nmat,
-                                    const int64_t* batches, int nbatch, const float* host_x, float* host_y,
-                                    float* dev_x, float* dev_y, int steps, cudaStream_t stream, float* ms) {
+namespace {
+int run_e2e(const void* const* W, const int64_t* K, const int64_t* N, int nmat, const int64_t* batches, int nbatch,
+            const float* host_x, float* host_y, float* dev_x, float* dev_y, int steps, cudaStream_t stream, float* ms,
+            const Grouped& grouped) {
+    if (grouped.ws && (nmat < 1 || nmat > IQ4XS_MAX_GROUP)) return (int)cudaErrorInvalidValue;
     Pipe p;
     cudaEvent_t e0 = nullptr, e1 = nullptr, ju = nullptr, jd = nullptr;
     cudaError_t e = pipe_create(p, K, N, nmat, batches, nbatch, dev_x, dev_y);
@@ -117,7 +135,7 @@ extern "C" int iq4xs_bench_e2e_gemv(const void* const* W, const int64_t* K, cons
         if (e == cudaSuccess) e = cudaStreamWaitEvent(p.up, e0, 0);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(p.down, e0, 0);
         for (int s = 0; s < steps && e == cudaSuccess; ++s)
-            e = enqueue_pass(p, s, W, K, N, nmat, batches, nbatch, host_x, host_y, stream);
+            e = enqueue_pass(p, s, W, K, N, nmat, batches, nbatch, host_x, host_y, stream, grouped);
         if (e == cudaSuccess) e = cudaEventRecord(ju, p.up);
         if (e == cudaSuccess) e = cudaEventRecord(jd, p.down);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ju, 0);
@@ -133,4 +151,22 @@ extern "C" int iq4xs_bench_e2e_gemv(const void* const* W, const int64_t* K, cons
     for (cudaEvent_t ev : {e0, e1, ju, jd})
         if (ev) cudaEventDestroy(ev);
     return (int)e;
+}
+}  // namespace
+
+extern "C" int iq4xs_bench_e2e_gemv(const void* const* W, const int64_t* K, const int64_t* N, int nmat,
+                                    const int64_t* batches, int nbatch, const float* host_x, float* host_y,
+                                    float* dev_x, float* dev_y, int steps, cudaStream_t stream, float* ms) {
+    return run_e2e(W, K, N, nmat, batches, nbatch, host_x, host_y, dev_x, dev_y, steps, stream, ms, Grouped{});
+}
+
+extern "C" int iq4xs_bench_e2e_gemv_grouped(const void* const* W, const int64_t* K, const int64_t* N, int nmat,
+                                            const int64_t* batches, int nbatch, const float* host_x, float* host_y,
+                                            float* dev_x, float* dev_y, void* workspace, size_t workspace_bytes,
+                                            int steps, cudaStream_t stream, float* ms) {
+    if (!workspace) return (int)cudaErrorInvalidValue;
+    Grouped g;
+    g.ws = workspace;
+    g.ws_bytes = workspace_bytes;
+    return run_e2e(W, K, N, nmat, batches, nbatch, host_x, host_y, dev_x, dev_y, steps, stream, ms, g);
 }

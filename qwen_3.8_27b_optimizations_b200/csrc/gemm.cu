@@ -36,7 +36,8 @@
 //    hundred cycles of latency here, so the single MMA-issuing thread waits on one "stage full"
 //    barrier (activation copy + four converter warps) and one "TMEM pair free" barrier per stage,
 //    and the two sub-block accumulators of a stage form a TMEM pair (two pairs, 512 columns).
-//    Waiters poll both of their barriers with one non-blocking test per round trip.
+//    Waiters sleep on their barriers in turn (try_wait with a suspend hint): a polling loop of
+//    non-blocking tests in the 16 drain warps took more issue slots than the drain arithmetic.
 //  * Every mbarrier wait is bounded (sleeping try_wait); a wait that gives up records a device
 //    error, raises the CTA's abort flag, and every role leaves its loop; in-flight TMA copies and
 //    MMAs are waited for (bounded) and TMEM is freed before the CTA exits.  No cluster multicast.
@@ -207,27 +208,11 @@ __device__ __forceinline__ uint4 expand_word(uint32_t x, const uint32_t (&lut)[4
 }
 }  // namespace
 
-// Spin (bounded) until two barrier phases have both completed; test_wait does not block, so one
-// poll of both costs one round trip.  Gives up when another role raised the abort flag.
-__device__ __forceinline__ bool gwait2(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2,
-                                       volatile uint32_t* abort_flag, uint32_t* err, uint32_t code) {
-    for (uint32_t i = 0; i < (1u << 28); ++i) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred q1, q2;\n\t"
-            "mbarrier.test_wait.parity.shared::cta.b64 q1, [%1], %2;\n\t"
-            "mbarrier.test_wait.parity.shared::cta.b64 q2, [%3], %4;\n\t"
-            "and.pred q1, q1, q2;\n\t"
-            "selp.u32 %0, 1, 0, q1;\n\t}"
-            : "=r"(ok)
-            : "r"(smem_addr(b1)), "r"(p1), "r"(smem_addr(b2)), "r"(p2)
-            : "memory");
-        if (ok) return true;
-        if ((i & 63u) == 63u && *abort_flag) return false;
-    }
-    record_error(err, code);
-    *abort_flag = 1u;
-    return false;
+// Two phases in turn, each with the sleeping wait: a waiting thread issues (almost) nothing until the
+// phase completes, so the warps that wait leave the issue slots to the warps that compute.
+__device__ __forceinline__ bool gwait_seq(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2,
+                                          volatile uint32_t* abort_flag, uint32_t* err, uint32_t code) {
+    return gwait(b1, p1, abort_flag, err, code) && gwait(b2, p2, abort_flag, err, code);
 }
 
 // Bounded wait without a suspend hint (prompt wake-up), giving up on abort.
@@ -344,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t u = it / kStages;
                     const int g = (int)(it & 1u);
                     const uint32_t ug = it >> 1;
-                    if (!(ok = gwait2(&full[s], u & 1u, &t_empty[g], (ug & 1u) ^ 1u, abort_flag, a.err, kDevErrMmaWait)))
+                    if (!(ok = gwait_seq(&full[s], u & 1u, &t_empty[g], (ug & 1u) ^ 1u, abort_flag, a.err, kDevErrMmaWait)))
                         break;
                     tc_fence_after();
                     const uint64_t ad = smem_desc_sw128(smem_addr(smem + kOffA + s * kABytes));
@@ -430,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // t_full: both sub-block MMAs of the stage are done; full[s] (complete before the MMAs were
                 // issued) makes the activation and weight scales of the stage visible to this warp.
                 if (lane == 0)
-                    go = gwait2(&t_full[g], (it >> 1) & 1u, &full[s], (it / kStages) & 1u, abort_flag, a.err, kDevErrMmaWait);
+                    go = gwait_seq(&t_full[g], (it >> 1) & 1u, &full[s], (it / kStages) & 1u, abort_flag, a.err, kDevErrMmaWait);
                 go = __shfl_sync(0xFFFFFFFFu, go ? 1 : 0, 0) != 0;
                 if (!go) break;
                 tc_fence_after();

@@ -20,6 +20,8 @@
 //  * every mbarrier wait is bounded; a timeout records a device error code and the kernel
 //    drains its in-flight copies and returns.
 #include <atomic>
+#include <cstring>
+#include <algorithm>
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -101,7 +103,7 @@ __device__ __forceinline__ float4 add4_rn(float4 a, float4 b) {
 
 template <int kAct>
 __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K, uint8_t* q8s, float* red, int cw,
-                                             int ncw, int lane, int bar_id) {
+                                             int ncw, int lane, int bar_id, bool first_cta) {
     const int nq = B * K / 128;
     const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
     if constexpr (kAct == kActNorm) {
@@ -124,7 +126,7 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
                 const int qd = base + i * ncw;
                 if (qd >= nq) continue;
                 const float4 v = act.delta ? add4_rn(xa[i], da[i]) : xa[i];
-                if (act.x_out && blockIdx.x == 0) *reinterpret_cast<float4*>(act.x_out + qd * 128 + 4 * lane) = v;
+                if (act.x_out && first_cta) *reinterpret_cast<float4*>(act.x_out + qd * 128 + 4 * lane) = v;
                 ss = fmaf(v.x, v.x, ss);
                 ss = fmaf(v.y, v.y, ss);
                 ss = fmaf(v.z, v.z, ss);
@@ -185,32 +187,31 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
     named_barrier(bar_id, ncw * 32);
 }
 
-// x >> 16 on the FMA pipe: one mul.hi.u32 by 2^16 (the integer ALU pipe is the busier one).
-__device__ __forceinline__ uint32_t hi16_fma(uint32_t x) {
-    uint32_t d;
-    asm("mul.hi.u32 %0, %1, 65536;" : "=r"(d) : "r"(x));
-    return d;
+// The upper 16 selector bits of a qs word.  A plain shift: mul.hi.u32 by 2^16 would move it to the
+// FMA pipe, but that instruction issues at a quarter of the rate and sits in the lookup's dependency
+// chain (measured on B200: the shift makes the 190 MB batch-1 GEMV 7% faster).
+__device__ __forceinline__ uint32_t sel_hi16(uint32_t x) {
+    return x >> 16;
 }
 
 // Weight side of the split codebook lookup for one qs word: hi/lo halves of both 16-bit selectors.
-// The >>16 selector shifts are done as umulhi(x, 2^16) so they issue on the FMA pipe next to the
-// dp4a instead of on the (half-rate) integer ALU pipe with the prmt lookups.
 // The table words come from the kernel parameters so prmt can read them from the constant bank.
 __device__ __forceinline__ void lut_word(const uint32_t (&tab)[4], uint32_t x, uint32_t& h0, uint32_t& l0, uint32_t& h1,
                                          uint32_t& l1) {
     const uint32_t xf = x ^ 0x88888888u;
     h0 = prmt(tab[2], tab[3], xf);
     l0 = prmt(tab[0], tab[1], x);
-    h1 = prmt(tab[2], tab[3], hi16_fma(xf));
-    l1 = prmt(tab[0], tab[1], hi16_fma(x));
+    h1 = prmt(tab[2], tab[3], sel_hi16(xf));
+    l1 = prmt(tab[0], tab[1], sel_hi16(x));
 }
 
 // kAct: where the activations come from (ActMode).  kActF32 / kActNorm build them into shared memory
 // (build_act_q8); each instance carries only its own prologue (code size costs instruction-cache
 // misses in the hot loop).
+// The kernel body, for CTA `cta` of the `ncta` CTAs that share the matrix (the single-matrix kernel
+// passes its grid; the grouped kernel a slice of it).
 template <int B, int SPL, int RPW, int NCW, bool kTail, bool kDebug, int kAct>
-__global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(const GemvArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+__device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int ncta, uint8_t* smem) {
     const int R = a.rows_per_stage, KW = a.kw;
     const int stages = a.stages;
     const int64_t stage_bytes = (int64_t)R * a.rb;
@@ -225,8 +226,8 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
     uint8_t* ring = smem + L.ring_off;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t r0 = a.N * (int64_t)blockIdx.x / gridDim.x;
-    const int64_t r1 = a.N * (int64_t)(blockIdx.x + 1) / gridDim.x;
+    const int64_t r0 = a.N * (int64_t)cta / ncta;
+    const int64_t r1 = a.N * (int64_t)(cta + 1) / ncta;
     const int ntiles = (int)((r1 - r0 + R - 1) / R);
 
     if (threadIdx.x == 0) {
@@ -286,7 +287,8 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
 
     grid_dependency_wait();
     if constexpr (smem_act)
-        build_act_q8<kAct>(a.act, B, a.K, smem + L.q8_off, reinterpret_cast<float*>(smem + L.red_off), cw, NCW, lane, 1);
+        build_act_q8<kAct>(a.act, B, a.K, smem + L.q8_off, reinterpret_cast<float*>(smem + L.red_off), cw, NCW, lane, 1,
+                           cta == 0);
     uint32_t alo[SPL][B][4], ahi[SPL][B][4];
     float dx[SPL][B];
 #pragma unroll
@@ -416,6 +418,12 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(c
     }
 }
 
+template <int B, int SPL, int RPW, int NCW, bool kTail, bool kDebug, int kAct>
+__global__ void __launch_bounds__(32 * (NCW + 1), 1) gemv_iq4xs_q8_rows_kernel(const GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    gemv_rows_body<B, SPL, RPW, NCW, kTail, kDebug, kAct>(a, (int)blockIdx.x, (int)gridDim.x, smem);
+}
+
 // --------------------------------------------------------------------------------------------
 // Generic path for shapes the bulk-copy kernel does not take (K/256 odd, unaligned W): one warp
 // per row, lane = sub-block, direct global loads.  Same per-term arithmetic.
@@ -466,7 +474,53 @@ __global__ void __launch_bounds__(256) gemv_iq4xs_q8_generic_kernel(const GemvAr
 }
 
 // --------------------------------------------------------------------------------------------
+// Grouped row kernel (batch 1): block b belongs to matrix p with cta0[p] <= b < cta0[p+1] and runs
+// the row-kernel body on that matrix's row range share.  Every instance of the body a matrix may need
+// (sub-block slots per lane, tail) is compiled in; each CTA executes one.
+constexpr int kRowGroupNCW = 12, kRowGroupRPW = 2;  // the row kernel's geometry (kRowNCW, kRowRPW below)
+struct GroupRowsParams {
+    GemvArgs args[kMaxGroup];
+    int cta0[kMaxGroup + 1];
+    int code[kMaxGroup];  // 2 * sub-block slots per lane + tail
+    int count;
+};
+
+__global__ void __launch_bounds__(32 * (kRowGroupNCW + 1), 1)
+    gemv_rows_grouped_kernel(const __grid_constant__ GroupRowsParams G) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    int p = 0;
+    while (p + 1 < G.count && (int)blockIdx.x >= G.cta0[p + 1]) ++p;
+    const int cta = (int)blockIdx.x - G.cta0[p], ncta = G.cta0[p + 1] - G.cta0[p];
+    const GemvArgs a = G.args[p];
+    switch (G.code[p]) {
+#define IQ4XS_ROWS_CASE(SPL, TAIL)                                                                           \
+    case 2 * SPL + TAIL:                                                                                     \
+        gemv_rows_body<1, SPL, kRowGroupRPW, kRowGroupNCW, TAIL != 0, false, kActQ8>(a, cta, ncta, smem); \
+        break;
+        IQ4XS_ROWS_CASE(1, 0) IQ4XS_ROWS_CASE(1, 1) IQ4XS_ROWS_CASE(2, 0) IQ4XS_ROWS_CASE(2, 1)
+        IQ4XS_ROWS_CASE(3, 0) IQ4XS_ROWS_CASE(3, 1) IQ4XS_ROWS_CASE(4, 0) IQ4XS_ROWS_CASE(4, 1)
+        IQ4XS_ROWS_CASE(5, 0) IQ4XS_ROWS_CASE(5, 1)
+#undef IQ4XS_ROWS_CASE
+        default: break;
+    }
+}
+
+// --------------------------------------------------------------------------------------------
 // Host-side launch helpers.
+// Warps per row (kw) and sub-block slots per lane (spl) of the row kernel for K at batch B; false when
+// even four warps per row would need more than the lane's register budget (the launch then takes the
+// tensor-core kernel).
+bool row_split(int64_t K, int B, int* kw_out, int* spl_out) {
+    const int64_t nsb = K / kQK8;
+    const int spl_max = (B == 1) ? 5 : 2;
+    int kw = 1;
+    while (kw < 4 && (nsb + 32 * kw - 1) / (32 * kw) > spl_max) kw *= 2;
+    const int64_t spl = (nsb + 32 * kw - 1) / (32 * kw);
+    *kw_out = kw;
+    *spl_out = (int)(spl < 1 << 20 ? spl : 1 << 20);
+    return spl <= spl_max;
+}
+
 namespace {
 
 // Per-device cache of the two attributes.  Host threads may launch on one device concurrently: the
@@ -500,24 +554,11 @@ void device_limits(int dev, int* sms, int* smem_optin) {
 
 // Row-stage kernel configuration for batch B: 16 consumer warps, one row each per stage; KW warps
 // per row so that a lane holds at most SPLMAX(B) sub-blocks of activations in registers.
-constexpr int kRowNCW = 12, kRowRPW = 2;
+constexpr int kRowNCW = kRowGroupNCW, kRowRPW = kRowGroupRPW;
 // fp32 sources are quantised inside the row kernel up to this K (every CTA quantises all of K; beyond
 // it the standalone quantizer launch is cheaper, measured on B200 at K = 8192 and 17408)
 constexpr int kRowFusedMaxK = 6144;
 
-// Warps per row (kw) and sub-block slots per lane (spl) of the row kernel for K at batch B; false when
-// even four warps per row would need more than the lane's register budget (the launch then takes the
-// tensor-core kernel).
-bool row_split(int64_t K, int B, int* kw_out, int* spl_out) {
-    const int64_t nsb = K / kQK8;
-    const int spl_max = (B == 1) ? 5 : 2;
-    int kw = 1;
-    while (kw < 4 && (nsb + 32 * kw - 1) / (32 * kw) > spl_max) kw *= 2;
-    const int64_t spl = (nsb + 32 * kw - 1) / (32 * kw);
-    *kw_out = kw;
-    *spl_out = (int)(spl < 1 << 20 ? spl : 1 << 20);
-    return spl <= spl_max;
-}
 
 template <int B, int SPL, bool kDebug, int kAct>
 void* rows_kernel_ptr_t(bool tail) {
@@ -536,23 +577,14 @@ void* rows_kernel_ptr(bool tail, int mode) {
     }
 }
 
-template <int B, bool kDebug>
-cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int smem_optin) {
+// Row-kernel geometry of `a` at batch B: warps per row, rows per stage, ring depth and prefetch
+// distance are set in `a`; *spl / *tail select the kernel instance, *smem_total its dynamic shared
+// memory.  cudaErrorNotSupported when K is too long for the row kernel.
+cudaError_t row_geometry(GemvArgs& a, int B, int smem_optin, int* spl_out, bool* tail_out, uint32_t* smem_total) {
     constexpr int NCW = kRowNCW, RPW = kRowRPW;
     const int nsb = a.K / kQK8;
     int kw = 1, spl = 1;
-    if (!row_split(a.K, B, &kw, &spl)) {  // K too long for register-resident activations: tensor-core kernel
-        if (a.act.mode == kActNorm) return cudaErrorNotSupported;
-        return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.partials, a.partial_bytes, a.K, a.N,
-                               B, stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
-    }
-    if (a.act.mode == kActF32 && a.K > kRowFusedMaxK) {
-        // every CTA would quantise all of K: the standalone quantizer (programmatic launch) is cheaper
-        cudaError_t eq = launch_q8_1_quantize(a.act.x, const_cast<uint8_t*>(a.q8), a.K, B, a.K, 1, stream, true, pdl);
-        if (eq != cudaSuccess) return eq;
-        a.act.mode = kActQ8;
-        pdl = true;
-    }
+    if (!row_split(a.K, B, &kw, &spl)) return cudaErrorNotSupported;
     const bool tail = (nsb != 32 * kw * spl);
     const int R = (NCW / kw) * RPW;
     a.kw = kw;
@@ -570,6 +602,32 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     a.prefetch = gemv_prefetch_rows();
     const RowSmem L = gemv_row_smem(B, R, kw, stages, stage_bytes, q8b);
     if ((int64_t)L.total > smem_optin || stage_bytes >= (1 << 20)) return cudaErrorInvalidConfiguration;
+    *spl_out = spl;
+    *tail_out = tail;
+    *smem_total = L.total;
+    return cudaSuccess;
+}
+
+template <int B, bool kDebug>
+cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int smem_optin) {
+    constexpr int NCW = kRowNCW;
+    int kw = 1, spl = 1;
+    if (!row_split(a.K, B, &kw, &spl)) {  // K too long for register-resident activations: tensor-core kernel
+        if (a.act.mode == kActNorm) return cudaErrorNotSupported;
+        return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.partials, a.partial_bytes, a.K, a.N,
+                               B, stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
+    }
+    if (a.act.mode == kActF32 && a.K > kRowFusedMaxK) {
+        // every CTA would quantise all of K: the standalone quantizer (programmatic launch) is cheaper
+        cudaError_t eq = launch_q8_1_quantize(a.act.x, const_cast<uint8_t*>(a.q8), a.K, B, a.K, 1, stream, true, pdl);
+        if (eq != cudaSuccess) return eq;
+        a.act.mode = kActQ8;
+        pdl = true;
+    }
+    bool tail = false;
+    uint32_t smem_total = 0;
+    cudaError_t eg = row_geometry(a, B, smem_optin, &spl, &tail, &smem_total);
+    if (eg != cudaSuccess) return eg;
     void* kern = nullptr;
     const int sa = a.act.mode;
     switch (spl) {
@@ -581,12 +639,12 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
         default: break;
     }
     if (!kern) return cudaErrorInvalidConfiguration;
-    cudaError_t e = ensure_dynamic_smem(kern, (int)L.total);
+    cudaError_t e = ensure_dynamic_smem(kern, (int)smem_total);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)imin64((int64_t)sms, a.N));
     cfg.blockDim = dim3(32 * (NCW + 1));
-    cfg.dynamicSmemBytes = L.total;
+    cfg.dynamicSmemBytes = smem_total;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -657,6 +715,63 @@ int gemv_prefetch_mma() {
 
 bool gemv_bulk_path(const uint8_t* W, int64_t K) {
     return ((K / kQK) % 2 == 0) && ((reinterpret_cast<uintptr_t>(W) & 15u) == 0);
+}
+
+void device_limits_current(int* sms, int* smem_optin) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    device_limits(dev, sms, smem_optin);
+}
+
+cudaError_t launch_gemv_rows_grouped(const GroupedProblem* p, int count, cudaStream_t stream, bool pdl, uint32_t* err,
+                                     const uint32_t lut[4]) {
+    if (count < 1 || count > kMaxGroup) return cudaErrorInvalidValue;
+    int sms = 0, smem_optin = 0;
+    device_limits_current(&sms, &smem_optin);
+    GroupRowsParams G;
+    std::memset(&G, 0, sizeof G);
+    uint32_t smem_max = 0;
+    int cta = 0;
+    for (int i = 0; i < count; ++i) {
+        if (!gemv_bulk_path(p[i].W, p[i].K)) return cudaErrorNotSupported;
+        GemvArgs a;
+        std::memset(&a, 0, sizeof a);
+        a.W = p[i].W;
+        a.q8 = p[i].q8;
+        a.y = p[i].y;
+        a.err = err;
+        a.N = p[i].N;
+        a.K = (int)p[i].K;
+        a.kb = (int)(p[i].K / kQK);
+        a.rb = (int64_t)a.kb * kBlockBytes;
+        for (int j = 0; j < 4; ++j) a.lut[j] = lut[j];
+        a.act.mode = kActQ8;
+        int spl = 1;
+        bool tail = false;
+        uint32_t sm = 0;
+        const cudaError_t e = row_geometry(a, 1, smem_optin, &spl, &tail, &sm);
+        if (e != cudaSuccess) return e;
+        G.args[i] = a;
+        G.code[i] = 2 * spl + (tail ? 1 : 0);
+        G.cta0[i] = cta;
+        cta += (int)imin64(std::max(p[i].ctas, 1), p[i].N);
+        smem_max = std::max(smem_max, sm);
+    }
+    G.cta0[count] = cta;
+    G.count = count;
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(gemv_rows_grouped_kernel), (int)smem_max);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cta);
+    cfg.blockDim = dim3(32 * (kRowNCW + 1));
+    cfg.dynamicSmemBytes = smem_max;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_rows_grouped_kernel, G);
 }
 
 bool gemv_takes_mma(const uint8_t* W, int64_t K, int B) {

@@ -28,6 +28,9 @@
 //  * Every mbarrier wait is bounded (sleeping try_wait, error word, drain before exit).
 #include <cuda.h>
 
+#include <algorithm>
+#include <cstring>
+
 #include "iq4xs_device.cuh"
 #include "iq4xs_kernels.h"
 
@@ -36,6 +39,7 @@ namespace iq4xs {
 namespace {
 constexpr int kMaxMmaStages = 16;  // stage ring depth: as many as fit, at least one per consumer warp
 constexpr int kPairs = 8;          // consumer warp pairs: one unit (tile x part) per pair at a time
+                                   // (measured on B200: 6 and 10 pairs are slower)
 constexpr int kNCW = 2 * kPairs;   // consumer warps; the two warps of a pair split the unit's super-blocks
 
 struct MmaSmem {
@@ -118,10 +122,9 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c));
 }
 
+// Upper 16 selector bits: a plain shift (mul.hi.u32 issues at a quarter of the rate, measured slower).
 __device__ __forceinline__ uint32_t hi16(uint32_t x) {
-    uint32_t d;
-    asm("mul.hi.u32 %0, %1, 65536;" : "=r"(d) : "r"(x));
-    return d;
+    return x >> 16;
 }
 
 __device__ __forceinline__ bool wait_sleep(uint64_t* bar, uint32_t parity, volatile uint32_t* flag, uint32_t* err,
@@ -138,10 +141,12 @@ __device__ __forceinline__ bool wait_sleep(uint64_t* bar, uint32_t parity, volat
 
 // kF32: the activations are quantised from fp32 while staging (batch <= 2 and small parts); the
 // Q8_1-input instances do not carry that code.
+// The kernel body for CTA `cta` of the `ncta` CTAs that share the matrix; `tmap` is a kernel-parameter
+// tensor map (the single-matrix kernel's own, or one of the grouped kernel's).
 template <int B, bool kDebug, bool kF32>
-__global__ void __launch_bounds__(32 * (kNCW + 1), 1)
-    gemv_iq4xs_q8_mma_kernel(const __grid_constant__ CUtensorMap tmap, const GemvMmaArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+__device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const GemvMmaArgs& a, int cta, int ncta,
+                                              uint8_t* smem) {
+    const CUtensorMap& tmap = *tmap_p;
     const int pk = a.pk, P = a.parts, S = a.stages;
     const MmaSmem L = mma_smem(pk, S);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
@@ -154,7 +159,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t T = (a.N + 15) / 16;
     const int64_t U = T * P;
-    const int64_t u0 = U * blockIdx.x / gridDim.x, u1 = U * (blockIdx.x + 1) / gridDim.x;
+    const int64_t u0 = U * cta / ncta, u1 = U * (cta + 1) / ncta;
     const int nunits = (int)(u1 - u0);
 
     if (threadIdx.x == 0) {
@@ -410,6 +415,31 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1)
     }
 }
 
+template <int B, bool kDebug, bool kF32>
+__global__ void __launch_bounds__(32 * (kNCW + 1), 1)
+    gemv_iq4xs_q8_mma_kernel(const __grid_constant__ CUtensorMap tmap, const GemvMmaArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    gemv_mma_body<B, kDebug, kF32>(&tmap, a, (int)blockIdx.x, (int)gridDim.x, smem);
+}
+
+// Grouped tensor-core kernel: block b belongs to matrix p with cta0[p] <= b < cta0[p+1] and runs the
+// body on that matrix (its own tensor map, part size, ring depth); Q8_1 activations from global memory.
+struct GroupMmaParams {
+    CUtensorMap maps[kMaxGroup];
+    GemvMmaArgs args[kMaxGroup];
+    int cta0[kMaxGroup + 1];
+    int count;
+};
+
+template <int B>
+__global__ void __launch_bounds__(32 * (kNCW + 1), 1) gemv_mma_grouped_kernel(const __grid_constant__ GroupMmaParams G) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    int p = 0;
+    while (p + 1 < G.count && (int)blockIdx.x >= G.cta0[p + 1]) ++p;
+    const GemvMmaArgs a = G.args[p];
+    gemv_mma_body<B, false, false>(&G.maps[p], a, (int)blockIdx.x - G.cta0[p], G.cta0[p + 1] - G.cta0[p], smem);
+}
+
 // y[b][n] = sum over parts p (in part order) of partial[p][b][n].  Launched after the GEMV with
 // programmatic serialization: griddepcontrol.wait returns once the GEMV grid has finished and its
 // stores are visible, so the GEMV needs no fences or tickets of its own.
@@ -418,8 +448,15 @@ __global__ void __launch_bounds__(256) reduce_parts_kernel(const float* __restri
     grid_dependency_wait();
     grid_launch_dependents();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < BN; i += (int64_t)gridDim.x * blockDim.x) {
+        // four parts' loads in flight before they are added (in part order)
         float sum = 0.0f;
-        for (int q = 0; q < P; ++q) sum += partial[(int64_t)q * BN + i];
+        int q = 0;
+        for (; q + 4 <= P; q += 4) {
+            const float v0 = partial[(int64_t)q * BN + i], v1 = partial[(int64_t)(q + 1) * BN + i];
+            const float v2 = partial[(int64_t)(q + 2) * BN + i], v3 = partial[(int64_t)(q + 3) * BN + i];
+            sum = (((sum + v0) + v1) + v2) + v3;
+        }
+        for (; q < P; ++q) sum += partial[(int64_t)q * BN + i];
         y[i] = sum;
     }
 }
@@ -462,6 +499,7 @@ int choose_pk(int pairs, int64_t tiles, int ctas, int smem_optin) {
     int best = 1;
     double best_cost = 1e300;
     for (int pk = 5; pk >= 1; pk -= 2) {
+        if ((int)mma_smem(pk, kPairs).total > smem_optin - 4096) continue;  // a ring of one stage per pair must fit
         const int parts = (pairs + pk - 1) / pk;
         const int64_t U = tiles * parts;
         const int64_t per = (U + (int64_t)ctas * kPairs - 1) / ((int64_t)ctas * kPairs);
@@ -600,6 +638,97 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, reduce_parts_kernel, (const float*)partials, y, parts, BN);
+}
+
+int gemv_mma_grouped_parts(int64_t K, int64_t N, int ctas, int smem_optin) {
+    if (K % 512 != 0) return 0;
+    const int pairs = (int)(K / 512);
+    const int pk = choose_pk(pairs, (N + 15) / 16, std::max(ctas, 1), smem_optin);
+    return (pairs + pk - 1) / pk;
+}
+
+cudaError_t launch_gemv_mma_grouped(const GroupedProblem* p, int count, int B, cudaStream_t stream, bool pdl,
+                                    uint32_t* err, const uint32_t lut[4]) {
+    if (count < 1 || count > kMaxGroup || B < 2 || B > 8) return cudaErrorInvalidValue;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    int sms = 0, smem_optin = 0;
+    device_limits_current(&sms, &smem_optin);
+    GroupMmaParams G;
+    std::memset(&G, 0, sizeof G);
+    uint32_t smem_max = 0;
+    int cta = 0;
+    for (int i = 0; i < count; ++i) {
+        const int64_t K = p[i].K, N = p[i].N;
+        if (K % 512 != 0 || (reinterpret_cast<uintptr_t>(p[i].W) & 15u)) return cudaErrorInvalidValue;
+        const int pairs = (int)(K / 512);
+        const int64_t T = (N + 15) / 16;
+        int ncta = std::max(p[i].ctas, 1);
+        const int pk = choose_pk(pairs, T, ncta, smem_optin);
+        const int stages = mma_stages(pk, smem_optin);
+        const int parts = (pairs + pk - 1) / pk;
+        if (parts > 1 && !p[i].partials) return cudaErrorInvalidValue;
+        const MmaSmem L = mma_smem(pk, stages);
+        if ((int)L.total > smem_optin) return cudaErrorInvalidConfiguration;
+        const cuuint64_t dims[2] = {(cuuint64_t)pairs * 34, (cuuint64_t)N};
+        const cuuint64_t strides[1] = {(cuuint64_t)pairs * 272};
+        const cuuint32_t box[2] = {(cuuint32_t)(34 * pk), 16};
+        const cuuint32_t estr[2] = {1, 1};
+        if (enc(&G.maps[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(p[i].W), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+        GemvMmaArgs& a = G.args[i];
+        a.q8 = p[i].q8;
+        a.y = p[i].y;
+        a.partial = p[i].partials;
+        a.sumi = nullptr;
+        a.err = err;
+        a.N = N;
+        a.K = (int)K;
+        a.pairs = pairs;
+        a.pk = pk;
+        a.parts = parts;
+        a.stages = stages;
+        a.prefetch = gemv_prefetch_mma();
+        for (int j = 0; j < 4; ++j) a.lut[j] = lut[j];
+        a.act.mode = kActQ8;
+        // A CTA stages the activations of at most two parts: its unit range must not exceed T units.
+        const int64_t U = T * parts;
+        int64_t n64 = std::min<int64_t>(ncta, U);
+        while ((U + n64 - 1) / n64 > T) ++n64;
+        ncta = (int)n64;
+        G.cta0[i] = cta;
+        cta += ncta;
+        smem_max = std::max(smem_max, L.total);
+    }
+    G.cta0[count] = cta;
+    G.count = count;
+    void* kern = nullptr;
+    switch (B) {
+        case 2: kern = (void*)gemv_mma_grouped_kernel<2>; break;
+        case 3: kern = (void*)gemv_mma_grouped_kernel<3>; break;
+        case 4: kern = (void*)gemv_mma_grouped_kernel<4>; break;
+        case 5: kern = (void*)gemv_mma_grouped_kernel<5>; break;
+        case 6: kern = (void*)gemv_mma_grouped_kernel<6>; break;
+        case 7: kern = (void*)gemv_mma_grouped_kernel<7>; break;
+        case 8: kern = (void*)gemv_mma_grouped_kernel<8>; break;
+        default: return cudaErrorInvalidValue;
+    }
+    cudaError_t e = ensure_dynamic_smem(kern, (int)smem_max);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cta);
+    cfg.blockDim = dim3(32 * (kNCW + 1));
+    cfg.dynamicSmemBytes = smem_max;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    void* args[] = {&G};
+    return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
 }  // namespace iq4xs

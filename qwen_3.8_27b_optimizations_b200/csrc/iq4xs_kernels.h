@@ -83,6 +83,31 @@ bool gemv_bulk_path(const uint8_t* W, int64_t K);
 // True when launch_gemv_q8 runs the tensor-core kernel (the only one that may write partial sums of
 // K parts): bulk path and batch 2..8, or batch 1 with K too long for the row kernel.
 bool gemv_takes_mma(const uint8_t* W, int64_t K, int B);
+// Row kernel: warps per row (kw) and sub-block slots per lane (spl) for K at batch B; false when K is
+// too long for register-resident activations.
+bool row_split(int64_t K, int B, int* kw_out, int* spl_out);
+
+// Grouped GEMV: several independent matrices of one batch size in one launch, each served by its own
+// slice of the grid (`ctas` CTAs, contiguous block indices), so the launch, ramp and tail are paid once
+// for the group.  Q8_1 activations are already in `q8`.
+constexpr int kMaxGroup = 8;
+struct GroupedProblem {
+    const uint8_t* W;   // IQ4_XS [N][K/256], 16-byte aligned, K % 512 == 0
+    const uint8_t* q8;  // Q8_1 [B][K/32]
+    float* y;           // [B][N]
+    float* partials;    // tensor-core kernel with more than one K part: [parts][B][N]
+    int64_t K, N;
+    int ctas;           // CTAs given to this matrix (the launchers may trim or raise it, see below)
+};
+// Batch 1 on the row kernel; cudaErrorNotSupported when a matrix's K is too long for it.
+cudaError_t launch_gemv_rows_grouped(const GroupedProblem* p, int count, cudaStream_t stream, bool pdl, uint32_t* err,
+                                     const uint32_t lut[4]);
+// K parts the grouped tensor-core launch uses for one matrix given `ctas` CTAs (partial sums when > 1).
+int gemv_mma_grouped_parts(int64_t K, int64_t N, int ctas, int smem_optin);
+// Batch 2..8 on the tensor-core kernel (partial sums left in `partials`; the caller adds the parts).
+cudaError_t launch_gemv_mma_grouped(const GroupedProblem* p, int count, int B, cudaStream_t stream, bool pdl,
+                                    uint32_t* err, const uint32_t lut[4]);
+void device_limits_current(int* sms, int* smem_optin);
 
 // Tensor-core prefill GEMM (gemm.cu).  Y[m][n] at y + m*ldy_m + n*ldy_n.
 struct GemmArgs {
