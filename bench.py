@@ -263,6 +263,7 @@ DECODER_PROMPT, DECODER_STEPS = 512, 128
 
 
 PARITY_TOKEN = 12345  # the fixed input token of the decode step compared across TP degrees
+PARITY_SEQ = [17, 4242, 99, 150001]  # fixed decode inputs from position 0 (the exact check)
 
 
 def decoder_parity_logits(m, prompt):
@@ -272,6 +273,21 @@ def decoder_parity_logits(m, prompt):
     m._tok.fill_(PARITY_TOKEN % m.cfg.vocab)
     m._step()
     return lg_pre.flatten().double(), m._last_logits.flatten().double().clone()
+
+
+def decoder_seq_logits(m):
+    """Logits of fixed decode inputs fed one per step from position 0 (no prompt): every operation is
+    one of this library's kernels, so TP-N with peer collectives (rank-order sums) and its single-GPU
+    rank emulation must agree bit for bit."""
+    import torch
+    m.reset_decode(0)
+    out = []
+    for t in PARITY_SEQ:
+        m._tok.fill_(t % m.cfg.vocab)
+        m._step()
+        out.append(m._last_logits.clone())
+    torch.cuda.synchronize()
+    return torch.cat(out)
 
 
 def decoder_run(P, dev, rank: int, world: int, barrier):
@@ -287,7 +303,7 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
     torch.cuda.synchronize()
     build_s = time.time() - t0
     prompt = torch.randint(0, cfg.vocab, (DECODER_PROMPT,), generator=torch.Generator().manual_seed(7)).to(dev)
-    logits = decoder_parity_logits(m, prompt)
+    logits = decoder_parity_logits(m, prompt) + (decoder_seq_logits(m) if world > 1 else None,)
     m.prefill(prompt)
     m.decode(4)                      # warm-up: eager steps and graph capture
     barrier()
@@ -332,12 +348,17 @@ def multi_gpu_parity(P, dev, rank: int, world: int, c5_logits) -> dict:
         batch 1 and the GEMM bit-exact against the full-matrix kernels (rows are independent, per-row
         arithmetic identical); batch 3 bit-exact against the concatenated per-shard GEMVs and within
         1e-5 (of max |y|) of the full-matrix GEMV (its K parts may be split differently);
-      * tensor-parallel decoders, prefill logits and the logits of one fused decode step on a fixed
-        token: a small 2-layer model with peer collectives against the same model with NCCL
-        all-reduces and against TP 1; the C5 dimensions at 2 layers, and the full 64-layer C5 model,
-        against TP 1 of the same weights.  Summation order differs between TP degrees (partial sums of
-        the row-parallel layers), which moves single Q8_1 roundings of the next layer's activations,
-        so decoder logits are compared by cosine (gates below), with max rel error and top-5 shown."""
+      * tensor-parallel decoders (a small 2-layer model, the C5 dimensions at 2 layers, the full
+        64-layer C5 model), two checks each:
+        - exact: four decode steps on fixed tokens from position 0 through the fused decode kernels
+          and the peer collectives, bit for bit against the single-GPU rank emulation of the same TP
+          degree (TPDecoder(emulate_ranks=N): the o_proj / down_proj GEMVs run as the ranks' K slices
+          and are added in rank order, as the peer all-reduce adds them);
+        - against TP 1: prefill logits and one decode step after the prompt, by cosine (gates below).
+          The prefill's NCCL all-reduce and TP 1's single GEMV add the K slices in another order, which
+          moves single Q8_1 roundings of the next layer's activations; 64 layers amplify that (cosine
+          ~0.995 at TP 2), a wrong shard would give a cosine near 0.  The small model also compares
+          peer collectives against NCCL all-reduces."""
     import torch
     res, ok = {}, True
     # ---- row-sharded matmuls
@@ -369,17 +390,22 @@ def multi_gpu_parity(P, dev, rank: int, world: int, c5_logits) -> dict:
     ok &= all(v for k, v in sh.items() if isinstance(v, bool))
     res["sharded_gate_up"] = sh
 
-    def build(cfg, w, rk, **kw):
-        return P.decoder.TPDecoder(cfg, rank=rk, world=w, seed=4, **kw)
-
-    def run(cfg, w, rk, prompt, **kw):
-        m = build(cfg, w, rk, **kw)
+    def run(cfg, w, rk, prompt, seed=4, **kw):
+        m = P.decoder.TPDecoder(cfg, rank=rk, world=w, seed=seed, **kw)
         out = decoder_parity_logits(m, prompt)
-        torch.cuda.synchronize()
+        seq = decoder_seq_logits(m)
         m.release()
         del m
         torch.cuda.empty_cache()
-        return out
+        return out, seq
+
+    def exact(tag, seq_tp, seq_emu):
+        nonlocal ok
+        same = bool(torch.equal(seq_tp, seq_emu))
+        d = {"bitexact": same, "steps": len(PARITY_SEQ),
+             "max_abs_diff": float((seq_tp.double() - seq_emu.double()).abs().max())}
+        ok &= same
+        res[tag] = d
 
     def agree(tag, a, b, gate):
         nonlocal ok
@@ -393,24 +419,28 @@ def multi_gpu_parity(P, dev, rank: int, world: int, c5_logits) -> dict:
     small = P.decoder.DecoderConfig(layers=2, hidden=1024, heads=4 * world, kv_heads=world, head_dim=128,
                                     ffn=1024 * world, vocab=3072, max_seq=40)
     prompt = torch.randint(0, small.vocab, (12,), generator=torch.Generator().manual_seed(3)).to(dev)
-    peer_l = run(small, world, rank, prompt, peer_collectives=True)
-    nccl_l = run(small, world, rank, prompt, peer_collectives=False)
-    tp1_l = run(small, 1, 0, prompt)
-    agree("small_2layer_peer_vs_nccl", peer_l, nccl_l, 0.9999)
-    agree("small_2layer_tp_vs_tp1", peer_l, tp1_l, 0.9999)
+    (peer_l, peer_s) = run(small, world, rank, prompt, peer_collectives=True)
+    (nccl_l, _) = run(small, world, rank, prompt, peer_collectives=False)
+    (tp1_l, _) = run(small, 1, 0, prompt)
+    (_, emu_s) = run(small, 1, 0, prompt, emulate_ranks=world)
+    agree("small_2layer_peer_vs_nccl", peer_l, nccl_l, 0.999)
+    agree("small_2layer_tp_vs_tp1", peer_l, tp1_l, 0.999)
+    exact("small_2layer_decode_vs_emulation", peer_s, emu_s)
     # ---- C5 dimensions, 2 layers
     c5_2 = P.decoder.DecoderConfig(layers=2)
     prompt = torch.randint(0, c5_2.vocab, (DECODER_PROMPT,), generator=torch.Generator().manual_seed(7)).to(dev)
-    agree("c5_2layer_tp_vs_tp1", run(c5_2, world, rank, prompt), run(c5_2, 1, 0, prompt), 0.9999)
-    # ---- full C5 (64 layers): the timed model's logits against TP 1 of the same weights (seed 1)
+    (tp_l, tp_s) = run(c5_2, world, rank, prompt)
+    (tp1_l, _) = run(c5_2, 1, 0, prompt)
+    (_, emu_s) = run(c5_2, 1, 0, prompt, emulate_ranks=world)
+    agree("c5_2layer_tp_vs_tp1", tp_l, tp1_l, 0.999)
+    exact("c5_2layer_decode_vs_emulation", tp_s, emu_s)
+    # ---- full C5 (64 layers): the timed model's logits against TP 1 of the same weights (seed 1), and
+    # its fixed-input decode steps against the rank emulation
     if c5_logits is not None:
-        m = P.decoder.TPDecoder(P.decoder.DecoderConfig(), rank=0, world=1, seed=1)
-        tp1 = decoder_parity_logits(m, prompt)
-        torch.cuda.synchronize()
-        m.release()
-        del m
-        torch.cuda.empty_cache()
-        agree("c5_64layer_tp_vs_tp1", c5_logits, tp1, 0.99)
+        (tp1_l, _) = run(P.decoder.DecoderConfig(), 1, 0, prompt, seed=1)
+        agree("c5_64layer_tp_vs_tp1", c5_logits[:2], tp1_l, 0.98)
+        (_, emu_s) = run(P.decoder.DecoderConfig(), 1, 0, prompt, seed=1, emulate_ranks=world)
+        exact("c5_64layer_decode_vs_emulation", c5_logits[2], emu_s)
     res["ok"] = bool(ok)
     return res
 

@@ -291,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int s = (int)(it % kRawStages);
                     const uint32_t u = it / kRawStages;
                     if (!(ok = gwait(&raw_empty[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
+                    fence_generic_async_smem();  // the converters' ld.shared of this stage come first
                     mbar_arrive_expect_tx(&raw_full[s], kRawBytes);
                     tma_load_3d_nohint(smem + kOffRaw + s * kRawBytes, &tmap_w, 0, p, row0, &raw_full[s]);
                 }
@@ -310,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int s = (int)(it % kStages);
                     const uint32_t u = it / kStages;
                     if (!(ok = gwait_fast(&freeb[s], (u & 1u) ^ 1u, abort_flag, a.err, kDevErrEmptyWait))) break;
+                    fence_generic_async_smem();  // the drain's ld.shared of this stage's d_x come first
                     mbar_arrive_expect_tx(&full[s], kActStageBytes);
                     bulk_g2s(smem + kOffB + s * kActStageBytes, a.act + ((size_t)mt * S + st) * kActStageBytes,
                              kActStageBytes, &full[s]);
@@ -388,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&full[s]);
                 }
+                fence_generic_async_smem();  // this warp's reads of the raw stage before its TMA refill
                 __syncwarp();
                 if (ok && lane == 0) mbar_arrive(&raw_empty[rs]);
             }
@@ -446,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
+                fence_generic_async_smem();  // this warp's reads of d_x and the weight scales before the refill
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&freeb[s]);
             }

@@ -22,7 +22,6 @@
 #include <atomic>
 #include <cstring>
 #include <algorithm>
-#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -245,13 +244,6 @@ __device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int n
         // ------------------------------------------------------------------ producer: one copy per stage
         if (lane == 0) {
             const uint64_t policy = l2_policy_evict_first();
-            // Stages beyond the ring are prefetched into L2 `a.prefetch` stages ahead of their copy.
-            auto prefetch_tile = [&](int t) {
-                const int64_t row0 = r0 + (int64_t)t * R;
-                bulk_prefetch_l2(a.W + row0 * a.rb, (uint32_t)(imin64(R, r1 - row0) * a.rb));
-            };
-            const int pf0 = min(ntiles, stages + a.prefetch);
-            for (int t = stages; t < pf0; ++t) prefetch_tile(t);
             uint32_t it = 0;
             for (int t = 0; t < ntiles; ++t, ++it) {
                 const int s = (int)(it % stages);
@@ -259,9 +251,9 @@ __device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int n
                 if (use > 0 && !wait_sleep_or_abort(&empty[s], (use - 1) & 1u, abort_flag, a.err, kDevErrEmptyWait)) break;
                 const int64_t row0 = r0 + (int64_t)t * R;
                 const uint32_t bytes = (uint32_t)(imin64(R, r1 - row0) * a.rb);
+                fence_generic_async_smem();  // the consumers' ld.shared of this stage come first
                 mbar_arrive_expect_tx(&full[s], bytes);
                 bulk_g2s_evict_first(ring + (size_t)s * stage_bytes, a.W + row0 * a.rb, bytes, &full[s], policy);
-                if (t >= stages && t + a.prefetch < ntiles) prefetch_tile(t + a.prefetch);
             }
             const uint32_t first = it > (uint32_t)stages ? it - stages : 0u;
             for (uint32_t j = first; j < it; ++j) {
@@ -413,6 +405,7 @@ __device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int n
                 }
             }
         }
+        fence_generic_async_smem();  // this warp's reads of the stage before its refill
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -577,9 +570,8 @@ void* rows_kernel_ptr(bool tail, int mode) {
     }
 }
 
-// Row-kernel geometry of `a` at batch B: warps per row, rows per stage, ring depth and prefetch
-// distance are set in `a`; *spl / *tail select the kernel instance, *smem_total its dynamic shared
-// memory.  cudaErrorNotSupported when K is too long for the row kernel.
+// Row-kernel geometry of `a` at batch B: warps per row, rows per stage and ring depth are set in
+// `a`; *spl / *tail select the kernel instance, *smem_total its dynamic shared memory.  cudaErrorNotSupported when K is too long for the row kernel.
 cudaError_t row_geometry(GemvArgs& a, int B, int smem_optin, int* spl_out, bool* tail_out, uint32_t* smem_total) {
     constexpr int NCW = kRowNCW, RPW = kRowRPW;
     const int nsb = a.K / kQK8;
@@ -599,7 +591,6 @@ cudaError_t row_geometry(GemvArgs& a, int B, int smem_optin, int* spl_out, bool*
                           (int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes, q8b).total > kRowSmemTarget + q8b))
         --stages;
     a.stages = stages;
-    a.prefetch = gemv_prefetch_rows();
     const RowSmem L = gemv_row_smem(B, R, kw, stages, stage_bytes, q8b);
     if ((int64_t)L.total > smem_optin || stage_bytes >= (1 << 20)) return cudaErrorInvalidConfiguration;
     *spl_out = spl;
@@ -693,25 +684,6 @@ cudaError_t dispatch(int B, GemvArgs a, cudaStream_t stream, bool pdl) {
                            stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
 }
 }  // namespace
-
-namespace {
-int env_int(const char* name, int dflt) {
-    const char* v = std::getenv(name);
-    if (!v || !*v) return dflt;
-    const int x = std::atoi(v);
-    return x < 0 ? 0 : (x > 64 ? 64 : x);
-}
-}  // namespace
-
-int gemv_prefetch_rows() {
-    static const int v = env_int("IQ4XS_GEMV_PREFETCH_ROWS", 0);
-    return v;
-}
-
-int gemv_prefetch_mma() {
-    static const int v = env_int("IQ4XS_GEMV_PREFETCH_MMA", 0);
-    return v;
-}
 
 bool gemv_bulk_path(const uint8_t* W, int64_t K) {
     return ((K / kQK) % 2 == 0) && ((reinterpret_cast<uintptr_t>(W) & 15u) == 0);

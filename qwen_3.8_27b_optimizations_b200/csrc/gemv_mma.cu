@@ -108,13 +108,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
-// L2 prefetch of one tensor-map box (no shared-memory destination, no completion).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, int c1) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-                 "r"(c0), "r"(c1)
-                 : "memory");
-}
-
 // d = a*b + (c, c, c, c): every accumulator starts at the same value c.
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c) {
     asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
@@ -176,15 +169,6 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
         // ------------------------------------------------------------------ producer
         if (lane == 0) {
             const uint64_t policy = l2_policy_evict_first();
-            // The ring holds S units; units beyond it are prefetched into L2 `a.prefetch` units ahead of
-            // their TMA load, so the load is served from L2 when its stage frees up.
-            auto prefetch_unit = [&](int j) {
-                const int64_t u = u0 + j;
-                const int p = (int)(u / T);
-                tma_prefetch_2d(&tmap, p * pk * 34, (int)((u - (int64_t)p * T) * 16));
-            };
-            const int pf0 = min(nunits, S + a.prefetch);
-            for (int j = S; j < pf0; ++j) prefetch_unit(j);
             int it = 0;
             for (; it < nunits; ++it) {
                 const int s = it % S;
@@ -193,9 +177,9 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
                 const int64_t u = u0 + it;
                 const int p = (int)(u / T);
                 const int64_t t = u - (int64_t)p * T;
+                fence_generic_async_smem();  // the consumers' ld.shared of this stage come first
                 mbar_arrive_expect_tx(&full[s], stage_bytes);
                 tma_load_2d(ring + (size_t)s * stage_bytes, &tmap, p * pk * 34, (int)(t * 16), &full[s], policy);
-                if (it >= S && it + a.prefetch < nunits) prefetch_unit(it + a.prefetch);
             }
             const int first = it > S ? it - S : 0;
             for (int j = first; j < it; ++j) {
@@ -394,6 +378,7 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
         acc[1] += park[1];
         acc[2] += park[2];
         acc[3] += park[3];
+        fence_generic_async_smem();  // the reads of the stage (weights, parked sums) before its refill
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
 
@@ -591,7 +576,6 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     a.pk = pk;
     a.parts = parts;
     a.stages = stages;
-    a.prefetch = gemv_prefetch_mma();
     a.partial = partials;
     for (int i = 0; i < 4; ++i) a.lut[i] = lut[i];
     a.act.mode = kActQ8;
@@ -690,8 +674,7 @@ cudaError_t launch_gemv_mma_grouped(const GroupedProblem* p, int count, int B, c
         a.pk = pk;
         a.parts = parts;
         a.stages = stages;
-        a.prefetch = gemv_prefetch_mma();
-        for (int j = 0; j < 4; ++j) a.lut[j] = lut[j];
+            for (int j = 0; j < 4; ++j) a.lut[j] = lut[j];
         a.act.mode = kActQ8;
         // A CTA stages the activations of at most two parts: its unit range must not exceed T units.
         const int64_t U = T * parts;

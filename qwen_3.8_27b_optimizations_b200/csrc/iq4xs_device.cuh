@@ -239,16 +239,19 @@ __device__ __forceinline__ void bulk_g2s_evict_first(void* dst, const void* src,
         : "memory");
 }
 
-// Prefetch `bytes` (a multiple of 16, src 16-byte aligned) of global memory into L2; no completion
-// tracking, nothing lands in shared memory.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
     return p;
+}
+
+// Orders this thread's generic-proxy shared-memory accesses before later async-proxy accesses (TMA,
+// bulk copies, tensor-core operand reads) to the same memory.  Needed on both sides of a stage
+// handed from threads that read it with ld.shared back to a copy engine that refills it: the reader
+// before it releases the stage, the producer after it acquires the stage and before it issues the
+// copy.  Without it the refill can land before the last generic read of the old contents.
+__device__ __forceinline__ void fence_generic_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ void named_barrier(int id, int threads) {

@@ -40,7 +40,6 @@ struct GemvArgs {
     int force_generic;   // test hook: take the direct-load kernel
     int kw;              // row kernel: warps per row (set by the launcher)
     int rows_per_stage;  // row kernel: rows per stage (set by the launcher)
-    int prefetch;        // row kernel: stages whose weights are prefetched into L2 ahead of the copies
     uint32_t lut[4];     // codebook prmt tables {neg_lo0, neg_lo1, pos_hi0, pos_hi1} (read from the param bank)
     float* partials;     // tensor-core kernel: cross-CTA partial sums
     size_t partial_bytes;
@@ -59,15 +58,10 @@ struct GemvMmaArgs {
     int pk;              // pairs per part (odd)
     int parts;
     int stages;
-    int prefetch;        // units whose weight boxes are prefetched into L2 ahead of the TMA loads
     uint32_t lut[4];
     ActSource act;       // kActQ8 or kActF32
 };
 
-// L2 prefetch distances of the GEMV producers (the process's IQ4XS_GEMV_PREFETCH_{ROWS,MMA} when set,
-// else the built-in defaults).
-int gemv_prefetch_rows();
-int gemv_prefetch_mma();
 
 // Tensor-core GEMV (batch 1..8).  Workspace = the partial sums of the K parts (none with one part).
 size_t gemv_mma_partial_bytes(int64_t K, int64_t N, int B);

@@ -60,10 +60,16 @@ class TPDecoder:
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, group=None, seed: int = 0,
                  device="cuda", matmul: Optional[Callable] = None, gen_weights: Optional[Callable] = None,
                  gen_normal: Optional[Callable] = None, fused_decode: Optional[bool] = None,
-                 peer_collectives: Optional[bool] = None):
+                 peer_collectives: Optional[bool] = None, emulate_ranks: int = 1):
         import torch
         from . import sharded
         self.torch = torch
+        # emulate_ranks = R > 1 (single GPU, world 1): the row-parallel GEMVs of the fused decode step
+        # run as the R per-rank K slices a tensor-parallel run over R ranks would compute, added in rank
+        # order like the peer all-reduce -- the TP-R decode step reproduced on one GPU, bit for bit.
+        if emulate_ranks > 1 and (world != 1 or matmul is not None):
+            raise ValueError("rank emulation runs on one GPU with the CUDA kernels")
+        self.emulate_ranks = int(emulate_ranks)
         self.cfg, self.rank, self.world, self.group = cfg, rank, world, group
         self.device = torch.device(device)
         if cfg.kv_heads % world or cfg.heads % world:
@@ -113,7 +119,18 @@ class TPDecoder:
             wd = kslice(self.gen_weights(D, cfg.ffn, s + 7), cfg.ffn, self.f0, self.f1)
             an = self.gen_normal(D, s + 8, 1.0, cfg.std).to(self.device)
             fn = self.gen_normal(D, s + 9, 1.0, cfg.std).to(self.device)
-            self.layers.append(dict(wqkv=wqkv, wo=wo, wgu=wgu, wd=wd, an=an, fn=fn))
+            L = dict(wqkv=wqkv, wo=wo, wgu=wgu, wd=wd, an=an, fn=fn)
+            if self.emulate_ranks > 1:
+                # the K slices of rank r of R: whole heads of o_proj, whole FFN pairs of down_proj
+                R = self.emulate_ranks
+                hqr = cfg.heads // R
+                L["wo_parts"] = [(kslice(wo, cfg.heads * hd, r * hqr * hd, (r + 1) * hqr * hd), r * hqr * hd,
+                                  (r + 1) * hqr * hd) for r in range(R)]
+                L["wd_parts"] = []
+                for r in range(R):
+                    a, b = split_units(cfg.ffn // PAIR, R, r)
+                    L["wd_parts"].append((kslice(wd, cfg.ffn, a * PAIR, b * PAIR), a * PAIR, b * PAIR))
+            self.layers.append(L)
         s = seed * 100003 + 16 * cfg.layers
         self.emb = self.gen_normal(cfg.vocab * D, s + 1, 0.0, cfg.std).view(cfg.vocab, D).to(torch.float16)
         self.final_norm = self.gen_normal(D, s + 2, 1.0, cfg.std).to(self.device)
@@ -250,24 +267,52 @@ class TPDecoder:
             norm_gemv(L["wqkv"], L["an"], self.nqkv, b["qkv"])
             api.dec_attention_decode_q8(b["qkv"], self.cache[l, 0], self.cache[l, 1], self.cos, self.sin, self._pos,
                                         self.hq, self.hkv, q8=b["q8a"], flags=PDL)
-            delta = self._reduce_gemv(L["wo"], b["q8a"], self.hq * hd, b["o"], 0)
+            delta = self._reduce_gemv(L["wo"], b["q8a"], self.hq * hd, b["o"], 0, L.get("wo_parts"))
             norm_gemv(L["wgu"], L["fn"], 2 * self.F, b["gu"])
             api.dec_swiglu_q8(b["gu"], self.F, q8=b["q8f"], flags=PDL)
-            delta = self._reduce_gemv(L["wd"], b["q8f"], self.F, b["d"], 1)
+            delta = self._reduce_gemv(L["wd"], b["q8f"], self.F, b["d"], 1, L.get("wd_parts"))
         api.dec_residual_rmsnorm_q8(cur, self.final_norm, cfg.eps, delta=delta, h_out=b["h"], want_q8=False,
                                     flags=PDL)
         return b["h"]
 
-    def _reduce_gemv(self, W, q8, K, out, area):
+    def _reduce_gemv(self, W, q8, K, out, area, parts=None):
         """out [1][hidden] = the row-parallel GEMV's partial sums, summed over the ranks: over NVLink
         peer memory (the GEMV writes into this rank's area, the pull kernel sums in rank order) or
-        with an NCCL all-reduce."""
+        with an NCCL all-reduce.  With rank emulation (`parts`: the ranks' K slices of W) the slices'
+        GEMVs run here and their outputs are added in rank order, as the peer all-reduce adds them."""
         api, D = self._api, self.cfg.hidden
+        if parts is not None:
+            torch = self.torch
+            bufs = self._emu_buffers(len(parts))
+            q8v = q8.view(-1)
+            for r, (Wr, k0, k1) in enumerate(parts):
+                api.gemv_q8_ex(Wr, q8v[k0 // 32 * 36:k1 // 32 * 36], k1 - k0, D, 1, out=bufs[r],
+                               flags=api.FLAG_OVERLAP_PRECEDING)
+            out.copy_(bufs[0])
+            for r in range(1, len(parts)):
+                out.add_(bufs[r])
+            return out
         if self.peers is None:
             return self._allreduce(api.gemv_q8_ex(W, q8, K, D, 1, out=out, flags=api.FLAG_OVERLAP_PRECEDING))
         api.gemv_q8_ex(W, q8, K, D, 1, out=self.peers.area(area, D).view(1, D), flags=api.FLAG_OVERLAP_PRECEDING)
         self.peers.allreduce(area, D, out)
         return out
+
+    def _emu_buffers(self, n):
+        if getattr(self, "_emu", None) is None or len(self._emu) != n:
+            self._emu = [self.torch.empty((1, self.cfg.hidden), dtype=self.torch.float32, device=self.device)
+                         for _ in range(n)]
+        return self._emu
+
+    def reset_decode(self, pos: int = 0):
+        """Start decoding at position `pos` without a prompt (the cache before `pos` is whatever it
+        holds); the next decode step reads the token set in self._tok."""
+        torch = self.torch
+        if self._pos is None:
+            self._pos = torch.empty((1,), dtype=torch.long, device=self.device)
+            self._tok = torch.empty((1,), dtype=torch.long, device=self.device)
+        self._pos.fill_(pos)
+        self._tok.fill_(0)
 
     def logits(self, h):
         """h [T][hidden] -> logits [T][vocab] (row-sharded lm_head + all-gather); the result may be a

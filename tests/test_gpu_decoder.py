@@ -61,3 +61,31 @@ def test_fused_decode_layers_vs_torch_ops(pkg):
     assert cos.min().item() >= 0.9999
     assert torch.max(torch.abs(a - b)) <= 2e-2 * torch.max(torch.abs(b))
     assert pkg.device_error() == 0
+
+
+@pytest.mark.parametrize("ranks", [2, 4])
+def test_rank_emulation_on_one_gpu(pkg, ranks):
+    """TPDecoder(emulate_ranks=R) on one GPU (the reference a TP-R run is compared with bit for bit on
+    several GPUs): the o_proj / down_proj GEMVs of the decode step run as R K slices added in rank
+    order.  Against the plain one-GPU model the sums of the slices differ by fp32 rounding only, so
+    the logits agree by cosine; the emulated decode is deterministic (two runs, the same bits)."""
+    dec = pkg.decoder
+    cfg = dec.DecoderConfig(layers=2, hidden=1024, heads=4 * ranks, kv_heads=ranks, head_dim=128, ffn=1024 * ranks,
+                            vocab=3072, max_seq=40)
+    seqs = {}
+    for name, emu in (("plain", 1), ("emulated", ranks), ("emulated_again", ranks)):
+        m = dec.TPDecoder(cfg, seed=4, emulate_ranks=emu)
+        m.reset_decode(0)
+        out = []
+        for t in (5, 1234, 77, 3001):
+            m._tok.fill_(t)
+            m._step()
+            out.append(m._last_logits.clone())
+        seqs[name] = torch.cat(out).double().flatten()
+        m.release()
+        del m
+    assert torch.equal(seqs["emulated"], seqs["emulated_again"])
+    a, b = seqs["emulated"], seqs["plain"]
+    assert torch.dot(a, b) / (a.norm() * b.norm()) >= 0.999
+    torch.cuda.synchronize()
+    assert pkg.device_error() == 0

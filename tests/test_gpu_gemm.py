@@ -224,3 +224,22 @@ def test_gemm_odd_superblock_count(pkg, O, K, N, M):
         Yg = pkg.gemv(W, Xd[m0:m0 + 8].contiguous(), N)
         assert torch.equal(Yg, Y[m0:m0 + 8])
     no_device_error(pkg)
+
+
+def test_gemm_deterministic_and_row_independent(pkg):
+    """The same GEMM repeated gives the same bits, in both output layouts, and a row slice of W gives
+    the same rows (each output element's sum order depends on K only): what the row-sharded GEMM
+    across GPUs relies on."""
+    N, K, M = 34816, 5120, 256
+    W = pkg.random_weights(N, K, seed=901)
+    X = pkg.fill_normal(M * K, seed=902).view(M, K)
+    ref = pkg.gemm(W, X, N)
+    for _ in range(6):
+        Y = pkg.gemm(W, X, N)
+        bad = (Y != ref).sum().item()
+        assert bad == 0, f"repeat differs in {bad} elements, max {float((Y - ref).abs().max())}"
+    h = N // 2
+    halves = torch.cat([pkg.gemm_nm(W[:h].contiguous(), X, h), pkg.gemm_nm(W[h:].contiguous(), X, N - h)])
+    bad = (halves != ref.t()).sum().item()
+    assert bad == 0, f"row halves differ in {bad} elements, max {float((halves - ref.t()).abs().max())}"
+    no_device_error(pkg)
