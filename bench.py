@@ -632,10 +632,11 @@ def run_case(argv) -> int:
       --case attention --pos 512                          the decoder's decode attention (64 / 8 heads)
       --case sweep                                        one benchmark sweep step, eager launches
       --case grouped --B 8                                one grouped call over the six layer shapes
+      --case gsweep                                       one benchmark step (a grouped call per batch), eager
     The default N (twice the gate|up projection) keeps the weights above the 126 MB L2."""
     import torch
     ap = argparse.ArgumentParser(prog="bench.py --case")
-    ap.add_argument("--case", required=True, choices=["gemv", "gemm", "attention", "sweep", "grouped"])
+    ap.add_argument("--case", required=True, choices=["gemv", "gemm", "attention", "sweep", "grouped", "gsweep"])
     ap.add_argument("--N", type=int, default=69632)
     ap.add_argument("--K", type=int, default=5120)
     ap.add_argument("--B", type=int, default=1)
@@ -688,6 +689,23 @@ def run_case(argv) -> int:
                     P.gemv(W, Xs[B][:B * K].view(B, K), N, out=Ys[B][:B * N].view(B, N), flags=P.FLAG_OVERLAP_PRECEDING)
         us = timed(step, a.launches, a.warmup)
         print(json.dumps({"case": "sweep", "us_per_step_eager": round(us, 1)}))
+        return 0
+    if a.case == "gsweep":
+        Ws = [P.random_weights(N, K, seed=i) for i, (_, N, K) in enumerate(SHAPES)]
+        items = {}
+        for B in BATCHES:
+            Xs = [P.fill_normal(B * K, seed=50 + B + i).view(B, K) for i, (_, N, K) in enumerate(SHAPES)]
+            Ys = [torch.empty((B, N), dtype=torch.float32, device="cuda") for _, N, K in SHAPES]
+            items[B] = list(zip(Ws, Xs, Ys))
+        gws = torch.zeros(max(P.gemv_grouped_workspace_bytes([(K, N) for _, N, K in SHAPES], B) for B in BATCHES),
+                          dtype=torch.uint8, device="cuda")
+
+        def gstep():
+            for B in BATCHES:
+                P.gemv_grouped(items[B], workspace=gws, flags=P.FLAG_OVERLAP_PRECEDING)
+        us = timed(gstep, a.launches, a.warmup)
+        print(json.dumps({"case": "gsweep", "us_per_step_eager": round(us, 1),
+                          "gbs": round(step_bytes() / (us * 1e-6) / 1e9, 1)}))
         return 0
     if a.case == "grouped":
         B = a.B
