@@ -132,7 +132,7 @@ int iq4xs_gemv_f32_noalloc(const void* W, const float* X, float* Y, int64_t K, i
  * Each problem's output is that of iq4xs_gemv_f32 on the same inputs within the GEMV tolerance
  * (batch 1: the same bits; batch 2..8 may split K into parts differently).  Y of one problem must not
  * overlap any W, X or Y of the group.  Groups the grouped kernels do not take (W not 16-byte aligned,
- * K % 512 != 0, batch 1 with K > 20480) run as one iq4xs_gemv_f32_ex per problem.
+ * K % 512 != 0, batch 1 with K > 24576) run as one iq4xs_gemv_f32_ex per problem.
  * workspace >= iq4xs_gemv_grouped_workspace_bytes(problems, count, B), 256-byte aligned, no zeroing.
  * No counterpart in the reference (one GEMV per MUL_MAT node, patch:278-280). */
 #define IQ4XS_MAX_GROUP 8

@@ -39,7 +39,7 @@ int iq4xs_dec_residual_rmsnorm_q8(float* x, const float* delta, const float* w, 
  * where q8(h) are the Q8_1 blocks iq4xs_q8_1_quantize would make of h (every CTA of the GEMV builds
  * them in its shared memory; the weight copies start before the kernel waits for x).  If x_out is
  * not null, v is also written there (it must not be x or delta; a decoder alternates two residual
- * buffers).  x, delta, w and x_out 16-byte aligned.  K <= 20480 and the bulk-copy GEMV (K/256 even, W 16-byte aligned), otherwise
+ * buffers).  x, delta, w and x_out 16-byte aligned.  K <= 24576 and the bulk-copy GEMV (K/256 even, W 16-byte aligned), otherwise
  * IQ4XS_ERR_NOT_SUPPORTED.  workspace >= iq4xs_gemv_q8_workspace_bytes(K, N, 1).
  * IQ4XS_FLAG_PDL: W is not written by the preceding kernel (programmatic dependent launch). */
 int iq4xs_dec_rmsnorm_gemv(const void* W, const float* x, const float* delta, const float* w, float eps, float* x_out,

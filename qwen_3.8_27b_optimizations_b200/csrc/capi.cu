@@ -491,7 +491,8 @@ int iq4xs_dec_rmsnorm_gemv(const void* W, const float* x, const float* delta, co
     if (!aligned(x, 16) || !aligned(w, 16) || !aligned(Y, 4) || (delta && !aligned(delta, 16)) ||
         (x_out && !aligned(x_out, 16)) || !aligned(workspace, 256))
         return IQ4XS_ERR_MISALIGNED;
-    if (!gemv_bulk_path(static_cast<const uint8_t*>(W), K) || K > 20480) return IQ4XS_ERR_NOT_SUPPORTED;
+    if (!gemv_bulk_path(static_cast<const uint8_t*>(W), K) || gemv_takes_mma(static_cast<const uint8_t*>(W), K, 1))
+        return IQ4XS_ERR_NOT_SUPPORTED;  // the row kernel's K range: the fused norm prologue lives there
     GemvArgs a = make_gemv_args(W, nullptr, Y, K, N);
     attach_workspace(a, workspace, 0, K, N, 1);
     a.act.mode = kActNorm;

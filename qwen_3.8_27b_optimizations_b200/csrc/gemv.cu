@@ -493,6 +493,7 @@ __global__ void __launch_bounds__(32 * (kRowGroupNCW + 1), 1)
         IQ4XS_ROWS_CASE(1, 0) IQ4XS_ROWS_CASE(1, 1) IQ4XS_ROWS_CASE(2, 0) IQ4XS_ROWS_CASE(2, 1)
         IQ4XS_ROWS_CASE(3, 0) IQ4XS_ROWS_CASE(3, 1) IQ4XS_ROWS_CASE(4, 0) IQ4XS_ROWS_CASE(4, 1)
         IQ4XS_ROWS_CASE(5, 0) IQ4XS_ROWS_CASE(5, 1)
+        IQ4XS_ROWS_CASE(6, 0) IQ4XS_ROWS_CASE(6, 1)
 #undef IQ4XS_ROWS_CASE
         default: break;
     }
@@ -505,9 +506,12 @@ __global__ void __launch_bounds__(32 * (kRowGroupNCW + 1), 1)
 // tensor-core kernel).
 bool row_split(int64_t K, int B, int* kw_out, int* spl_out) {
     const int64_t nsb = K / kQK8;
-    const int spl_max = (B == 1) ? 5 : 2;
+    // the fewest warps per row (1..4, all dividing the 12 consumer warps) that fit the lane budget;
+    // 3 warps at K = 17408 leave 5.6% of the lane slots idle where 4 warps left 15% (measured on
+    // B200: down_proj at batch 1 18.4 -> 16.4 us)
+    const int spl_max = (B == 1) ? 6 : 2;
     int kw = 1;
-    while (kw < 4 && (nsb + 32 * kw - 1) / (32 * kw) > spl_max) kw *= 2;
+    while (kw < 4 && (nsb + 32 * kw - 1) / (32 * kw) > spl_max) ++kw;
     const int64_t spl = (nsb + 32 * kw - 1) / (32 * kw);
     *kw_out = kw;
     *spl_out = (int)(spl < 1 << 20 ? spl : 1 << 20);
@@ -627,6 +631,7 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
         case 3: kern = B == 1 ? rows_kernel_ptr<1, 3, kDebug>(tail, sa) : nullptr; break;
         case 4: kern = B == 1 ? rows_kernel_ptr<1, 4, kDebug>(tail, sa) : nullptr; break;
         case 5: kern = B == 1 ? rows_kernel_ptr<1, 5, kDebug>(tail, sa) : nullptr; break;
+        case 6: kern = B == 1 ? rows_kernel_ptr<1, 6, kDebug>(tail, sa) : nullptr; break;
         default: break;
     }
     if (!kern) return cudaErrorInvalidConfiguration;

@@ -45,7 +45,7 @@ def test_noalloc_matches_workspace_entry_point(pkg, O, N, K, B):
 
 
 def test_noalloc_batch1_long_rows_need_no_partials(pkg):
-    # Batch 1 with K <= 20480 runs the row kernel, which writes no partial sums: only the 18 KiB of
+    # Batch 1 with K <= 24576 runs the row kernel, which writes no partial sums: only the 18 KiB of
     # Q8_1 activations count against the static scratch, so an lm_head-sized N is accepted.  (The
     # tensor-core path at this shape would want ~4.3 MiB of partial sums.)
     N, K, B = 152064, 16384, 1
