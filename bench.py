@@ -108,9 +108,10 @@ def bf16_peak():
     return FALLBACK_BF16_TFLOPS, "fallback"
 
 
-def gemm_sweep(P, weights, dev, stream, reps: int = 3):
+def gemm_sweep(P, weights, dev, stream, reps: int = 3, kind=None):
     """Prefill GEMM over the layer shapes at M = 512 and 2048: per shape the median of 3 timed CUDA-graph
-    replays of `reps` calls (weights alternate between the two copies)."""
+    replays of `reps` calls (weights alternate between the two copies).  kind: the tensor-core operand
+    kind ("i8", "f16"; None = the library's default)."""
     import torch
     per, tot_flops, tot_ms = [], 0.0, 0.0
     for M in GEMM_TOKENS:
@@ -119,12 +120,12 @@ def gemm_sweep(P, weights, dev, stream, reps: int = 3):
             Y = torch.empty((M, N), dtype=torch.float32, device=dev)
             ws = torch.empty(P.gemm_workspace_bytes(K, M), dtype=torch.uint8, device=dev)
             with torch.cuda.stream(stream):
-                P.gemm(weights[0][i], X, N, workspace=ws, out=Y, stream=stream)
+                P.gemm(weights[0][i], X, N, workspace=ws, out=Y, stream=stream, kind=kind)
                 stream.synchronize()
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
                     for r in range(reps):
-                        P.gemm(weights[r % 2][i], X, N, workspace=ws, out=Y, stream=stream)
+                        P.gemm(weights[r % 2][i], X, N, workspace=ws, out=Y, stream=stream, kind=kind)
                 g.replay()
                 stream.synchronize()
                 ts = []
@@ -645,6 +646,7 @@ def run_case(argv) -> int:
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--pos", type=int, default=512)
     ap.add_argument("--act", default="q8", choices=["q8", "f32"])
+    ap.add_argument("--kind", default=None, choices=["i8", "f16"], help="GEMM operand kind (default: library's)")
     a = ap.parse_args(argv)
     P = load_pkg()
     torch.cuda.set_device(0)
@@ -724,8 +726,8 @@ def run_case(argv) -> int:
         X = P.fill_normal(a.M * K, seed=11).view(a.M, K)
         ws = torch.zeros(P.gemm_workspace_bytes(K, a.M), dtype=torch.uint8, device="cuda")
         Y = torch.empty((a.M, N), dtype=torch.float32, device="cuda")
-        us = timed(lambda: P.gemm(W, X, N, workspace=ws, out=Y), a.launches, a.warmup)
-        print(json.dumps({"case": "gemm", "N": N, "K": K, "M": a.M, "us_per_call": round(us, 2),
+        us = timed(lambda: P.gemm(W, X, N, workspace=ws, out=Y, kind=a.kind), a.launches, a.warmup)
+        print(json.dumps({"case": "gemm", "kind": a.kind or "default", "N": N, "K": K, "M": a.M, "us_per_call": round(us, 2),
                           "tops": round(2.0 * a.M * N * K / (us * 1e-6) / 1e12, 1)}))
         return 0
     X = P.fill_normal(B * K, seed=11).view(B, K)
@@ -973,11 +975,13 @@ def main():
     h2d, d2h = 4 * nx, 4 * ny  # the bytes of the two copies of every step
 
     gemm_per, gemm_tops, sharded, decoder = [], None, [], None
+    gemm_per_i8, gemm_tops_i8 = [], None
     bpeak, bpeak_kind = bf16_peak()
     c1 = c1_gemv(P, dev, stream)
     if args.extras == "all":
         # ---- prefill GEMM sweep (reported beside the headline)
         gemm_per, gemm_tops = gemm_sweep(P, weights, dev, stream)
+        gemm_per_i8, gemm_tops_i8 = gemm_sweep(P, weights, dev, stream, kind="i8")
         # ---- row-sharded lm_head / gate|up across the ranks (strong scaling, output all-gather)
         sharded = sharded_sweep(P, dev, stream, rank, world, barrier)
         # ---- synthetic decoder, tensor-parallel over the ranks
@@ -1050,8 +1054,11 @@ def main():
                 "value": round(gemm_tops, 1), "unit": "TOPS", "tokens": GEMM_TOKENS,
                 "roofline": {"bound": "tensor", "achieved": round(gemm_tops, 1), "peak": bpeak,
                              "unit": "TFLOP/s", "frac": round(gemm_tops / bpeak, 4), "peak_kind": bpeak_kind,
-                             "kernel": "gemm_iq4xs_tc_kernel (tcgen05.mma kind::f16, TMEM accumulators)"},
-                "per_shape": gemm_per},
+                             "kernel": "gemm_iq4xs_tc_kernel (tcgen05.mma kind::f16, fp32 TMEM accumulators)"},
+                "per_shape": gemm_per,
+                "i8_operands": {"value": round(gemm_tops_i8, 1), "unit": "TOPS",
+                                "kernel": "gemm_iq4xs_i8_kernel (tcgen05.mma kind::i8, s32 TMEM accumulators)",
+                                "per_shape": gemm_per_i8}},
             "c1": c1,
             "parity": parity,
             "decoder": decoder,

@@ -168,6 +168,19 @@ int iq4xs_gemm(const void* W, const float* X, float* Y, int64_t K, int64_t N, in
 int iq4xs_gemm_strided(const void* W, const float* X, int64_t ldx_m, int64_t ldx_k, float* Y, int64_t ldy_m,
                        int64_t ldy_n, int64_t K, int64_t N, int64_t M, void* workspace, size_t workspace_bytes,
                        cudaStream_t stream);
+/* Operand kind of the tensor-core GEMM (iq4xs_gemm_ex flags).  IQ4XS_GEMM_KIND_I8: int8 codebook
+ * values and Q8_1 quants (tcgen05 kind::i8, s32 accumulators); IQ4XS_GEMM_KIND_F16: the same integers
+ * as fp16 (kind::f16, fp32 accumulators).  Both form the exact integer sub-block dots; the fp32 scale
+ * products are taken in a different order (i8: (sumi*sw)*d_x, f16: (sumi*d_x)*sw), so the outputs
+ * agree to fp32 rounding.  Neither flag: the default kind, fp16 (measured the faster on B200, by 2-3%
+ * at the 27B-class layer shapes).  The odd-K path ignores the kind.  No counterpart in the reference
+ * (its WMMA GEMM has one operand kind). */
+#define IQ4XS_GEMM_KIND_F16 0x10u
+#define IQ4XS_GEMM_KIND_I8 0x20u
+/* iq4xs_gemm_strided with flags (IQ4XS_GEMM_KIND_*); any other bit: IQ4XS_ERR_INVALID_ARGUMENT. */
+int iq4xs_gemm_ex(const void* W, const float* X, int64_t ldx_m, int64_t ldx_k, float* Y, int64_t ldy_m,
+                  int64_t ldy_n, int64_t K, int64_t N, int64_t M, void* workspace, size_t workspace_bytes,
+                  uint32_t flags, cudaStream_t stream);
 /* The GEMM's activation quantiser alone, into `workspace` (iq4xs_gemm_workspace_bytes(K, M)): one
  * 17,408-byte block per (128-token tile t, 64-wide K stage s) at offset (t*(K/64) + s)*17408:
  * fp16 q of the tile's tokens (exact integers) in the 128-byte-swizzled K-major layout (token r,
@@ -175,6 +188,11 @@ int iq4xs_gemm_strided(const void* W, const float* X, int64_t ldx_m, int64_t ldx
  * at position 8w+2i+j), then fp32 d [2][128] (the value of the truncated fp16 d of each Q8_1
  * block) for the stage's two 32-blocks.  Tokens past M are zeros.  For tests. */
 int iq4xs_debug_gemm_quantize(const float* X, void* workspace, int64_t K, int64_t M, cudaStream_t stream);
+/* The int8 GEMM's quantiser alone: one 18,432-byte block per (128-token tile t, 128-wide K stage s)
+ * at offset (t*(K/128) + s)*18432: int8 q in the same swizzled K-major layout (16 values per 16-byte
+ * chunk; within each 32-block element 4w+i+16j at position 8w+2i+j), then fp32 d [4][128].
+ * K % 128 == 0.  For tests. */
+int iq4xs_debug_gemm_i8_quantize(const float* X, void* workspace, int64_t K, int64_t M, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Raw int32 sub-block dot products sum_j kvalues[q_j]*q8_j (before the (ls-32) factor) through

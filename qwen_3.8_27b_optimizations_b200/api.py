@@ -42,7 +42,9 @@ SIGNATURES = {
     "iq4xs_gemm_workspace_bytes": (_sz, [_i64, _i64]),
     "iq4xs_gemm": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "iq4xs_gemm_strided": (_i, [_vp, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "iq4xs_gemm_ex": (_i, [_vp, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
     "iq4xs_debug_gemm_quantize": (_i, [_vp, _vp, _i64, _i64, _vp]),
+    "iq4xs_debug_gemm_i8_quantize": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "iq4xs_debug_subblock_dots": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_gemv_q8_generic": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "iq4xs_fill_normal": (_i, [_vp, _i64, _u64, _f, _f, _vp]),
@@ -266,16 +268,27 @@ def gemm_workspace_bytes(K: int, M: int) -> int:
     return int(lib().iq4xs_gemm_workspace_bytes(K, M))
 
 
-def gemm(W, X, N: int, workspace=None, out=None, stream=None):
-    """Y [M][N] = X [M][K] . W^T on the tensor cores (X fp32, quantised per 32-block inside)."""
+GEMM_KIND_F16 = 0x10
+GEMM_KIND_I8 = 0x20
+_GEMM_KINDS = {None: 0, "f16": GEMM_KIND_F16, "i8": GEMM_KIND_I8}
+
+
+def gemm(W, X, N: int, workspace=None, out=None, stream=None, kind=None):
+    """Y [M][N] = X [M][K] . W^T on the tensor cores (X fp32, quantised per 32-block inside).
+    kind: None (the library's default), "i8" or "f16" (tensor-core operand kind)."""
     torch = _torch()
     X = X.contiguous()
     M, K = X.shape
     need = gemm_workspace_bytes(K, M)
     ws = workspace if workspace is not None else _workspace(need, X.device, "gemm")
     Y = out if out is not None else torch.empty((M, N), dtype=torch.float32, device=X.device)
-    _check("iq4xs_gemm", lib().iq4xs_gemm(_ptr(W), _ptr(X), _ptr(Y), K, N, M, _ptr(ws),
-                                          ws.numel() * ws.element_size(), _stream(stream)))
+    if kind is None:
+        _check("iq4xs_gemm", lib().iq4xs_gemm(_ptr(W), _ptr(X), _ptr(Y), K, N, M, _ptr(ws),
+                                              ws.numel() * ws.element_size(), _stream(stream)))
+    else:
+        _check("iq4xs_gemm_ex", lib().iq4xs_gemm_ex(_ptr(W), _ptr(X), K, 1, _ptr(Y), N, 1, K, N, M, _ptr(ws),
+                                                    ws.numel() * ws.element_size(), _GEMM_KINDS[kind],
+                                                    _stream(stream)))
     return Y
 
 
@@ -309,6 +322,26 @@ def debug_gemm_quantize(X, stream=None):
     q16 = blocks[:, :, :16384].contiguous().view(torch.float16).view(T, S, 8192)
     xq = q16[:, :, idx.reshape(-1)].view(T, S, 128, 64).permute(0, 2, 1, 3).reshape(T * 128, K)[:M]
     xs = blocks[:, :, 16384:].contiguous().view(torch.float32).view(T, S, 2, 128)
+    xs = xs.permute(1, 2, 0, 3).reshape(K // 32, T * 128)[:, :M]
+    return xq, xs
+
+
+def debug_gemm_i8_quantize(X, stream=None):
+    """The int8 GEMM's activation quantiser, unpacked from its stage blocks into
+    (int8 q [M][K] in the lookup order within each 32-block, fp32 d [K/32][M])."""
+    torch = _torch()
+    X = X.contiguous()
+    M, K = X.shape
+    ws = torch.zeros(gemm_workspace_bytes(K, M), dtype=torch.uint8, device=X.device)
+    _check("iq4xs_debug_gemm_i8_quantize", lib().iq4xs_debug_gemm_i8_quantize(_ptr(X), _ptr(ws), K, M, _stream(stream)))
+    T, S = (M + 127) // 128, K // 128
+    blocks = ws[:T * S * 18432].view(T, S, 18432)
+    r = torch.arange(128, device=X.device)[:, None]
+    p = torch.arange(128, device=X.device)[None, :]
+    idx = (r // 8) * 1024 + (r % 8) * 128 + (((p // 16) ^ (r % 8)) * 16) + (p % 16)   # [128][128]
+    q8 = blocks[:, :, :16384].contiguous().view(torch.int8).view(T, S, 16384)
+    xq = q8[:, :, idx.reshape(-1)].view(T, S, 128, 128).permute(0, 2, 1, 3).reshape(T * 128, K)[:M]
+    xs = blocks[:, :, 16384:].contiguous().view(torch.float32).view(T, S, 4, 128)
     xs = xs.permute(1, 2, 0, 3).reshape(K // 32, T * 128)[:, :M]
     return xq, xs
 

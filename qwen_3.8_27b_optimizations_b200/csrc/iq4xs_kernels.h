@@ -122,6 +122,14 @@ cudaError_t launch_gemm_quantize(const float* X, void* workspace, int64_t K, int
 cudaError_t launch_gemm(const uint8_t* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M, int64_t x_stride_m,
                         int64_t x_stride_k, int64_t y_stride_m, int64_t y_stride_n, void* workspace, cudaStream_t stream,
                         uint32_t* err, const uint32_t lut[4]);
+// The int8 (kind::i8) GEMM (gemm_i8.cu): same arguments; workspace = stage blocks of 18,432 bytes,
+// [ceil(M/128)][K/128].
+size_t gemm_i8_workspace_bytes(int64_t K, int64_t M);
+cudaError_t launch_gemm_i8_quantize(const float* X, void* workspace, int64_t K, int64_t M, int64_t stride_m,
+                                    int64_t stride_k, cudaStream_t stream);
+cudaError_t launch_gemm_i8(const uint8_t* W, const float* X, float* Y, int64_t K, int64_t N, int64_t M,
+                           int64_t x_stride_m, int64_t x_stride_k, int64_t y_stride_m, int64_t y_stride_n,
+                           void* workspace, cudaStream_t stream, uint32_t* err, const uint32_t lut[4]);
 
 // Q8_1 quantizer.  Element (m, k) of X is at X[m*stride_m + k*stride_k]; output blocks [M][K/32].
 // pdl: launch with programmatic stream serialization (the kernel waits on griddepcontrol before

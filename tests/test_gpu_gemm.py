@@ -58,19 +58,53 @@ def test_gemm_quantize_bitexact(pkg, O, K, M, scale):
     assert np.array_equal(xs.cpu().numpy().T, d)
 
 
+@pytest.mark.parametrize("K,M,scale", [(512, 1, 1.0), (5120, 37, 1.0), (17408, 16, 1e-3), (1024, 130, 1e4)])
+def test_gemm_i8_quantize_bitexact(pkg, O, K, M, scale):
+    """The int8 GEMM's quantiser: the Q8_1 quants as int8 and the fp32 value of each block's fp16 d."""
+    X = (np.random.default_rng(K + M + 1).standard_normal((M, K)) * scale).astype(np.float32)
+    X[0, :32] = 0.0
+    X[-1, 64], X[-1, 65], X[-1, 66] = 127.0, 2.5, -2.5
+    xq, xs = pkg.debug_gemm_i8_quantize(dev(X))
+    Q = O.quantize_q8_1(X).reshape(M, K // 32, 36)
+    q = Q[:, :, 4:].view(np.int8)
+    d = Q[:, :, 0:2].copy().view(np.float16).astype(np.float32)[:, :, 0]
+    got = xq.cpu().numpy().reshape(M, K // 32, 32)
+    assert np.array_equal(got[:, :, lookup_positions()], q)
+    assert np.array_equal(xs.cpu().numpy().T, d)
+
+
 # ----------------------------------------------------------------------------- small shapes vs C oracle
 SMALL = [(512, 128, 128), (512, 100, 37), (1024, 256, 16), (2048, 384, 300), (5120, 200, 130),
          (17408, 130, 20), (8192, 64, 256), (512, 1, 1), (1024, 129, 129), (512, 256, 640)]
 
 
+KINDS = ["i8", "f16"]
+
+
+@pytest.mark.parametrize("kind", KINDS)
 @pytest.mark.parametrize("K,N,M", SMALL)
-def test_gemm_small_vs_oracle(pkg, O, K, N, M):
+def test_gemm_small_vs_oracle(pkg, O, K, N, M, kind):
     W = O.random_blocks(K, N, 777 + K * 31 + N)
     X = O.normal(M * K, 11 + M).reshape(M, K)
     Q = O.quantize_q8_1(X)
     Y64, A = O.matmul_q8(W, Q, K, N, M)
-    Y = pkg.gemm(dev(W), dev(X), N).cpu().numpy()
-    check_close(O, Y, Y64, A, K, f"gemm K={K} N={N} M={M}")
+    Y = pkg.gemm(dev(W), dev(X), N, kind=kind).cpu().numpy()
+    check_close(O, Y, Y64, A, K, f"gemm {kind} K={K} N={N} M={M}")
+    no_device_error(pkg)
+
+
+def test_gemm_kinds_agree_and_default(pkg, O):
+    """int8 and fp16 operands give the same integer dots; their outputs differ only by the order of
+    the fp32 scale products (a few ulp), and the default call is the fp16 kernel bit for bit."""
+    K, N, M = 5120, 768, 200
+    W = dev(O.random_blocks(K, N, 55))
+    X = dev(O.normal(M * K, 56).reshape(M, K))
+    Yi = pkg.gemm(W, X, N, kind="i8")
+    Yf = pkg.gemm(W, X, N, kind="f16")
+    assert torch.equal(pkg.gemm(W, X, N), Yf)
+    Y64, A = torch_ref.matmul_q8(W, pkg.q8_1_quantize(X), K)
+    tol = O.tolerance(Y64.cpu().numpy(), A.cpu().numpy(), K // 32, REL)
+    assert np.all(np.abs(Yi.cpu().numpy() - Yf.cpu().numpy()) <= tol)
     no_device_error(pkg)
 
 
@@ -107,12 +141,13 @@ C3 = [("q_proj", 8192, 5120), ("k_proj", 1024, 5120), ("o_proj", 5120, 8192), ("
       ("down", 5120, 17408)]
 
 
+@pytest.mark.parametrize("kind", KINDS)
 @pytest.mark.parametrize("M", [512, 2048])
 @pytest.mark.parametrize("name,N,K", C3)
-def test_gemm_full_shapes(pkg, O, name, N, K, M):
+def test_gemm_full_shapes(pkg, O, name, N, K, M, kind):
     W = pkg.random_weights(N, K, seed=4242 + N + K)
     X = pkg.fill_normal(M * K, seed=99 + M).view(M, K)
-    Y = pkg.gemm(W, X, N)
+    Y = pkg.gemm(W, X, N, kind=kind)
     q8 = pkg.q8_1_quantize(X)
     if M == 2048 and N * M > 2048 * 8192:
         # full torch check on a slab of rows, C oracle on sampled rows
@@ -200,6 +235,12 @@ def test_gemm_invalid_arguments(pkg, O):
     assert L.iq4xs_gemm(W.data_ptr(), X.data_ptr(), Y.data_ptr(), K, N, M, ws.data_ptr(), nb - 1, s) == 4
     assert L.iq4xs_gemm(W.data_ptr() + 8, X.data_ptr(), Y.data_ptr(), K, N - 1, M, ws.data_ptr(), nb, s) == 3
     assert L.iq4xs_gemm(W.data_ptr(), X.data_ptr(), Y.data_ptr(), K, N, M, ws.data_ptr(), nb, s) == 0
+    for bad_flags in (0x30, 0x1, 0x40):   # both kinds, or an unknown bit
+        assert L.iq4xs_gemm_ex(W.data_ptr(), X.data_ptr(), K, 1, Y.data_ptr(), N, 1, K, N, M, ws.data_ptr(), nb,
+                               bad_flags, s) == 1
+    for kind in (0x10, 0x20):
+        assert L.iq4xs_gemm_ex(W.data_ptr(), X.data_ptr(), K, 1, Y.data_ptr(), N, 1, K, N, M, ws.data_ptr(), nb,
+                               kind, s) == 0
     no_device_error(pkg)
 
 
@@ -226,18 +267,22 @@ def test_gemm_odd_superblock_count(pkg, O, K, N, M):
     no_device_error(pkg)
 
 
-def test_gemm_deterministic_and_row_independent(pkg):
+@pytest.mark.parametrize("kind", KINDS)
+def test_gemm_deterministic_and_row_independent(pkg, kind):
     """The same GEMM repeated gives the same bits, in both output layouts, and a row slice of W gives
     the same rows (each output element's sum order depends on K only): what the row-sharded GEMM
-    across GPUs relies on."""
+    across GPUs relies on.  The transposed-layout calls take the default kind."""
     N, K, M = 34816, 5120, 256
     W = pkg.random_weights(N, K, seed=901)
     X = pkg.fill_normal(M * K, seed=902).view(M, K)
-    ref = pkg.gemm(W, X, N)
+    ref = pkg.gemm(W, X, N, kind=kind)
     for _ in range(6):
-        Y = pkg.gemm(W, X, N)
+        Y = pkg.gemm(W, X, N, kind=kind)
         bad = (Y != ref).sum().item()
         assert bad == 0, f"repeat differs in {bad} elements, max {float((Y - ref).abs().max())}"
+    if kind != "f16":
+        no_device_error(pkg)
+        return
     h = N // 2
     halves = torch.cat([pkg.gemm_nm(W[:h].contiguous(), X, h), pkg.gemm_nm(W[h:].contiguous(), X, N - h)])
     bad = (halves != ref.t()).sum().item()
