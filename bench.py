@@ -320,6 +320,21 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     pre_ms, dec_ms = float(t[0]), float(t[1])
+    coll = None
+    if world > 1 and m.fused_allreduce:
+        # the same model with a separate peer all-reduce kernel after each o_proj / down_proj GEMV
+        m.fused_allreduce = False
+        m.graph = None
+        m.prefill(prompt)
+        m.decode(4)                  # re-capture
+        barrier()
+        ev[0].record()
+        m.decode(DECODER_STEPS)
+        ev[1].record()
+        torch.cuda.synchronize()
+        tc = torch.tensor([ev[0].elapsed_time(ev[1])], dtype=torch.float64, device=dev)
+        dist.all_reduce(tc, op=dist.ReduceOp.MAX)
+        coll = round(DECODER_STEPS / (float(tc[0]) * 1e-3), 1)
     m.release()
     del m
     torch.cuda.empty_cache()
@@ -327,6 +342,9 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
             "unit": "tok/s", "tp": world, "prompt": DECODER_PROMPT, "steps": DECODER_STEPS,
             "prefill_ms": round(pre_ms, 1), "prefill_tok_s": round(DECODER_PROMPT / (pre_ms * 1e-3), 1),
             "decode_ms": round(dec_ms, 1), "build_s": round(build_s, 1), "first_tokens": toks[:8],
+            "allreduce": "fused into the o_proj / down_proj GEMVs (push epilogue + next kernel's prologue)"
+                         if world > 1 else None,
+            "tok_s_separate_allreduce_kernel": coll,
             "model": "64 x (hidden 5120, 64x128 q heads, 8 kv heads, SwiGLU 17408), vocab 152064, IQ4_XS "
                      "linear layers, fp32 norms, f16 embeddings and KV cache, random N(0, 0.02) init"}, logits
 

@@ -46,6 +46,43 @@ int iq4xs_peer_collective(const float* const* src, uint32_t* const* rflags, uint
                           int rank, int world, int gather, int64_t n, float* out, uint32_t spin_limit,
                           cudaStream_t stream);
 
+/* Row-parallel decode GEMV with the all-reduce fused in (push model, low-latency protocol), for the
+ * tensor-parallel decoder's o_proj / down_proj.  One data area of every rank holds `world` slots of
+ * N 64-bit words; word i of slot q is rank q's partial output i (fp32 bits, low half) tagged with the
+ * epoch of the all-reduce (high half).  The producer, iq4xs_dec_gemv_q8_push, is a batch-1 GEMV whose
+ * epilogue stores each output, tagged, into slot `rank` of every rank's area (single 8-byte NVLink
+ * stores, no fence, no flag: the tag travels with the value); the last CTA to finish advances this
+ * rank's epoch counter.  There is no collective kernel.  The consumers are the next kernel of the
+ * decode step: iq4xs_dec_rmsnorm_gemv_peer and iq4xs_dec_residual_rmsnorm_q8_peer read each word until
+ * its tag is the current epoch (bounded polls) and take delta[i] = sum over q = 0..world-1, in this
+ * order, of slot q's value -- the same bits as iq4xs_peer_collective's all-reduce.  The epoch counter
+ * is the one iq4xs_peer_collective advances (the two can be mixed in one sequence; every rank runs
+ * the same sequence).  The descriptor lives in DEVICE memory (the kernels read it) and is built
+ * once per area by the caller.  A consumer must directly follow its producer's kernel on the stream
+ * (or follow its completion); two consecutive fused all-reduces must use different areas.
+ * Graph-capture safe. */
+typedef struct iq4xs_peer_slots {
+    uint64_t* dst[IQ4XS_MAX_PEERS];  /* slot `rank` of rank q's area, as mapped on this rank */
+    const uint64_t* local;           /* this rank's area: slot q at local + q*N */
+    uint32_t* counter;               /* this rank's epoch counter (2 x uint32, as for iq4xs_peer_collective) */
+    int32_t rank, world;
+    uint32_t spin_limit;             /* polls before a read gives up (device error 6); 0: a few seconds */
+    uint32_t reserved;
+} iq4xs_peer_slots;
+
+/* Y = W . q8 (batch 1, iq4xs_gemv_q8 arithmetic) into slot `rank` of every rank's area (`slots`, a
+ * device pointer), then the signal.  The row kernel's K range (K % 512 == 0, K <= 24576, W 16-byte
+ * aligned); otherwise IQ4XS_ERR_NOT_SUPPORTED.  flags: IQ4XS_FLAG_PDL. */
+int iq4xs_dec_gemv_q8_push(const void* W, const void* q8, int64_t K, int64_t N, const iq4xs_peer_slots* slots,
+                           void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream);
+/* iq4xs_dec_rmsnorm_gemv with delta = the fused all-reduce of `slots` (K = the slots' N). */
+int iq4xs_dec_rmsnorm_gemv_peer(const void* W, const float* x, const iq4xs_peer_slots* slots, const float* w, float eps,
+                                float* x_out, float* Y, int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                                unsigned flags, cudaStream_t stream);
+/* iq4xs_dec_residual_rmsnorm_q8 (one token, T = 1) with delta = the fused all-reduce of `slots`. */
+int iq4xs_dec_residual_rmsnorm_q8_peer(float* x, const iq4xs_peer_slots* slots, const float* w, int64_t D, float eps,
+                                       void* q8, float* h_out, unsigned flags, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

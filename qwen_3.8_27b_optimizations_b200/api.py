@@ -95,6 +95,9 @@ PEER_SIGNATURES = {
     "iq4xs_ipc_open": (_i, [_vp, C.POINTER(_vp)]),
     "iq4xs_ipc_close": (_i, [_vp]),
     "iq4xs_peer_collective": (_i, [C.POINTER(_vp), C.POINTER(_vp), _vp, _vp, _i, _i, _i, _i64, _vp, C.c_uint32, _vp]),
+    "iq4xs_dec_gemv_q8_push": (_i, [_vp, _vp, _i64, _i64, _vp, _vp, _sz, C.c_uint, _vp]),
+    "iq4xs_dec_rmsnorm_gemv_peer": (_i, [_vp, _vp, _vp, _vp, _f, _vp, _vp, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
+    "iq4xs_dec_residual_rmsnorm_q8_peer": (_i, [_vp, _vp, _vp, _i64, _f, _vp, _vp, C.c_uint, _vp]),
 }
 IPC_HANDLE_BYTES = 64
 MAX_PEERS = 8
@@ -495,6 +498,48 @@ def dec_rmsnorm_gemv(W, x, w, eps: float, N: int, delta=None, x_out=None, out=No
         _ptr(x_out) if x_out is not None else None, _ptr(Y), K, N, _ptr(ws), ws.numel() * ws.element_size(), flags,
         _stream(stream)))
     return Y
+
+
+def dec_gemv_q8_push(W, q8, K: int, N: int, slots, flags: int = 0, stream=None, workspace=None):
+    """Batch-1 GEMV of Q8_1 blocks whose N outputs go to slot `rank` of every rank's area of the
+    fused all-reduce described by `slots` (a device tensor holding an iq4xs_peer_slots, see
+    PeerGroup.slots); the last CTA signals the peers."""
+    need = gemv_q8_workspace_bytes(K, N, 1)
+    ws = workspace if workspace is not None else (_workspace(need, q8.device) if need else None)
+    _check("iq4xs_dec_gemv_q8_push", lib().iq4xs_dec_gemv_q8_push(
+        _ptr(W), _ptr(q8), K, N, _ptr(slots), _ptr(ws) if ws is not None else None,
+        ws.numel() * ws.element_size() if ws is not None else 0, flags, _stream(stream)))
+
+
+def dec_rmsnorm_gemv_peer(W, x, slots, w, eps: float, N: int, x_out=None, out=None, flags: int = 0, stream=None,
+                          workspace=None):
+    """dec_rmsnorm_gemv with delta = the fused all-reduce of `slots` (waits for every peer)."""
+    torch = _torch()
+    K = x.shape[-1]
+    Y = out if out is not None else torch.empty((1, N), dtype=torch.float32, device=x.device)
+    ws = workspace if workspace is not None else _workspace(gemv_q8_workspace_bytes(K, N, 1), x.device)
+    _check("iq4xs_dec_rmsnorm_gemv_peer", lib().iq4xs_dec_rmsnorm_gemv_peer(
+        _ptr(W), _ptr(x), _ptr(slots), _ptr(w), eps, _ptr(x_out) if x_out is not None else None, _ptr(Y), K, N,
+        _ptr(ws), ws.numel() * ws.element_size(), flags, _stream(stream)))
+    return Y
+
+
+def dec_residual_rmsnorm_q8_peer(x, slots, w, eps: float, q8=None, h_out=None, want_q8: bool = True, flags: int = 0,
+                                 stream=None):
+    """dec_residual_rmsnorm_q8 (one token) with delta = the fused all-reduce of `slots`."""
+    T, D = x.shape
+    if want_q8 or q8 is not None:
+        q8 = _q8_out(T, D, x.device, q8)
+    _check("iq4xs_dec_residual_rmsnorm_q8_peer", lib().iq4xs_dec_residual_rmsnorm_q8_peer(
+        _ptr(x), _ptr(slots), _ptr(w), D, eps, _ptr(q8) if q8 is not None else None,
+        _ptr(h_out) if h_out is not None else None, flags, _stream(stream)))
+    return q8, h_out
+
+
+class PeerSlots(C.Structure):
+    """iq4xs_peer_slots (include/iq4xs_peer.h)."""
+    _fields_ = [("dst", C.c_uint64 * MAX_PEERS), ("local", C.c_uint64), ("counter", C.c_uint64),
+                ("rank", C.c_int32), ("world", C.c_int32), ("spin_limit", C.c_uint32), ("reserved", C.c_uint32)]
 
 
 # ----------------------------------------------------------------------------- peer memory (iq4xs_peer.h)

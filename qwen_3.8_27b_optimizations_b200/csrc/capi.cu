@@ -530,6 +530,57 @@ int iq4xs_dec_rmsnorm_gemv(const void* W, const float* x, const float* delta, co
     return status_from(launch_gemv_q8(a, 1, stream, (flags & IQ4XS_FLAG_PDL) != 0));
 }
 
+int iq4xs_dec_gemv_q8_push(const void* W, const void* q8, int64_t K, int64_t N, const iq4xs_peer_slots* slots,
+                           void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if (!q8 || !slots) return IQ4XS_ERR_INVALID_ARGUMENT;
+    const size_t need = iq4xs_gemv_q8_workspace_bytes(K, N, 1);
+    if (need && !workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < need) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned(q8, 4) || !aligned(slots, 8) || (workspace && !aligned(workspace, 256))) return IQ4XS_ERR_MISALIGNED;
+    if (!gemv_bulk_path(static_cast<const uint8_t*>(W), K) || gemv_takes_mma(static_cast<const uint8_t*>(W), K, 1))
+        return IQ4XS_ERR_NOT_SUPPORTED;  // the row kernel carries the push epilogue
+    GemvArgs a = make_gemv_args(W, q8, nullptr, K, N);
+    attach_workspace(a, workspace, 0, K, N, 1);
+    a.push = slots;
+    return status_from(launch_gemv_q8(a, 1, stream, (flags & IQ4XS_FLAG_PDL) != 0));
+}
+
+int iq4xs_dec_rmsnorm_gemv_peer(const void* W, const float* x, const iq4xs_peer_slots* slots, const float* w, float eps,
+                                float* x_out, float* Y, int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                                unsigned flags, cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if (!x || !slots || !w || !Y || !workspace) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (x_out && x_out == x) return IQ4XS_ERR_INVALID_ARGUMENT;  // x is read by every CTA
+    if (workspace_bytes < iq4xs_gemv_q8_workspace_bytes(K, N, 1)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(Y, 4) || !aligned(slots, 8) || (x_out && !aligned(x_out, 16)) ||
+        !aligned(workspace, 256))
+        return IQ4XS_ERR_MISALIGNED;
+    if (!gemv_bulk_path(static_cast<const uint8_t*>(W), K) || gemv_takes_mma(static_cast<const uint8_t*>(W), K, 1))
+        return IQ4XS_ERR_NOT_SUPPORTED;
+    GemvArgs a = make_gemv_args(W, nullptr, Y, K, N);
+    attach_workspace(a, workspace, 0, K, N, 1);
+    a.act.mode = kActNorm;
+    a.act.x = x;
+    a.act.peer = slots;
+    a.act.w = w;
+    a.act.x_out = x_out;
+    a.act.eps = eps;
+    return status_from(launch_gemv_q8(a, 1, stream, (flags & IQ4XS_FLAG_PDL) != 0));
+}
+
+int iq4xs_dec_residual_rmsnorm_q8_peer(float* x, const iq4xs_peer_slots* slots, const float* w, int64_t D, float eps,
+                                       void* q8, float* h_out, unsigned flags, cudaStream_t stream) {
+    if (!x || !slots || !w || (!q8 && !h_out) || D <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (D % kQK8 != 0 || D > 8192) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(x, 4) || !aligned(w, 4) || !aligned(slots, 8) || (q8 && !aligned(q8, 4)) || (h_out && !aligned(h_out, 4)))
+        return IQ4XS_ERR_MISALIGNED;
+    return status_from(launch_residual_rmsnorm_q8(x, nullptr, w, (int)D, 1, eps, static_cast<uint8_t*>(q8), h_out,
+                                                  stream, (flags & IQ4XS_FLAG_PDL) != 0, slots));
+}
+
 int iq4xs_dec_swiglu_q8(const float* gu, int64_t F, int64_t T, void* q8, unsigned flags, cudaStream_t stream) {
     if (!gu || !q8 || F <= 0 || T <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
     if (F % kQK8 != 0) return IQ4XS_ERR_UNSUPPORTED_SHAPE;

@@ -44,10 +44,11 @@ constexpr int kNormMaxPer = 8;  // blocks per warp: D <= 8192
 
 __global__ void __cluster_dims__(kNormCtas, 1, 1) __launch_bounds__(kNormWarps * 32) residual_rmsnorm_q8_kernel(
     float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w, int D, float eps,
-    uint8_t* __restrict__ q8, float* __restrict__ h_out) {
+    uint8_t* __restrict__ q8, float* __restrict__ h_out, const iq4xs_peer_slots* peer, uint32_t* err) {
     namespace cg = cooperative_groups;
     grid_launch_dependents();
     grid_dependency_wait();
+    const uint32_t ep = peer ? peer_slots_epoch(peer) : 0u;  // delta = the fused all-reduce of the slots
     __shared__ float red[kNormWarps];
     __shared__ float css;
     cg::cluster_group cluster = cg::this_cluster();
@@ -67,7 +68,10 @@ __global__ void __cluster_dims__(kNormCtas, 1, 1) __launch_bounds__(kNormWarps *
             const int e = b * kQK8 + lane;
             wv[j] = w[e];
             float a = xr[e];
-            if (dr) {
+            if (peer) {
+                a = __fadd_rn(a, peer_slots_sum1(peer, D, e, ep, err));
+                xr[e] = a;
+            } else if (dr) {
                 a = __fadd_rn(a, dr[e]);
                 xr[e] = a;
             }
@@ -385,10 +389,12 @@ cudaLaunchConfig_t launch_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s
 }  // namespace
 
 cudaError_t launch_residual_rmsnorm_q8(float* x, const float* delta, const float* w, int D, int T, float eps,
-                                       uint8_t* q8, float* h_out, cudaStream_t stream, bool pdl) {
+                                       uint8_t* q8, float* h_out, cudaStream_t stream, bool pdl,
+                                       const iq4xs_peer_slots* peer) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = launch_cfg(dim3(kNormCtas, (unsigned)T), dim3(kNormWarps * 32), 0, stream, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, residual_rmsnorm_q8_kernel, x, delta, w, D, eps, q8, h_out);
+    return cudaLaunchKernelEx(&cfg, residual_rmsnorm_q8_kernel, x, delta, w, D, eps, q8, h_out, peer,
+                              device_error_word());
 }
 
 // score row length per head: the longest position range of a CTA, rounded up to 4 floats so that

@@ -102,10 +102,17 @@ __device__ __forceinline__ float4 add4_rn(float4 a, float4 b) {
 
 template <int kAct>
 __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K, uint8_t* q8s, float* red, int cw,
-                                             int ncw, int lane, int bar_id, bool first_cta) {
+                                             int ncw, int lane, int bar_id, bool first_cta, uint32_t* err) {
     const int nq = B * K / 128;
     const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
     if constexpr (kAct == kActNorm) {
+        // delta: a plain vector, or the fused all-reduce of the ranks' slots (each word read until it
+        // carries the current epoch)
+        const bool has_delta = act.delta != nullptr || act.peer != nullptr;
+        const uint32_t ep = act.peer ? peer_slots_epoch(act.peer) : 0u;
+        auto delta4 = [&](int off) -> float4 {
+            return act.peer ? peer_slots_sum4(act.peer, K, off, ep, err) : ldg4(act.delta + off);
+        };
         float4 v0[kActQ], w0[kActQ];
         float ss = 0.0f;
         for (int base = cw; base < nq; base += ncw * kActQ) {
@@ -116,7 +123,7 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
                 xa[i] = da[i] = zero4;
                 if (qd < nq) {
                     xa[i] = ldg4(act.x + qd * 128 + 4 * lane);
-                    if (act.delta) da[i] = ldg4(act.delta + qd * 128 + 4 * lane);
+                    if (has_delta) da[i] = delta4(qd * 128 + 4 * lane);
                     if (base == cw) w0[i] = ldg4(act.w + qd * 128 + 4 * lane);
                 }
             }
@@ -124,7 +131,7 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
             for (int i = 0; i < kActQ; ++i) {
                 const int qd = base + i * ncw;
                 if (qd >= nq) continue;
-                const float4 v = act.delta ? add4_rn(xa[i], da[i]) : xa[i];
+                const float4 v = has_delta ? add4_rn(xa[i], da[i]) : xa[i];
                 if (act.x_out && first_cta) *reinterpret_cast<float4*>(act.x_out + qd * 128 + 4 * lane) = v;
                 ss = fmaf(v.x, v.x, ss);
                 ss = fmaf(v.y, v.y, ss);
@@ -152,7 +159,7 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
                     wa[i] = w0[i];
                 } else {
                     va[i] = ldg4(act.x + qd * 128 + 4 * lane);
-                    if (act.delta) va[i] = add4_rn(va[i], ldg4(act.delta + qd * 128 + 4 * lane));
+                    if (has_delta) va[i] = add4_rn(va[i], delta4(qd * 128 + 4 * lane));
                     wa[i] = ldg4(act.w + qd * 128 + 4 * lane);
                 }
             }
@@ -280,7 +287,7 @@ __device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int n
     grid_dependency_wait();
     if constexpr (smem_act)
         build_act_q8<kAct>(a.act, B, a.K, smem + L.q8_off, reinterpret_cast<float*>(smem + L.red_off), cw, NCW, lane, 1,
-                           cta == 0);
+                           cta == 0, a.err);
     uint32_t alo[SPL][B][4], ahi[SPL][B][4];
     float dx[SPL][B];
 #pragma unroll
@@ -314,6 +321,7 @@ __device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int n
     }
     // Activations are in registers: a dependent kernel may now overwrite the Q8_1 workspace.
     grid_launch_dependents();
+    const uint32_t push_epoch = a.push ? peer_slots_epoch_next(a.push) : 0u;  // after the grid dependency wait
     const uint8_t* lane_h = ring + (size_t)(slot * RPW) * a.rb + off_h;  // + stage, row, sub-block offsets
 
     for (int t = 0; t < ntiles; ++t) {
@@ -380,7 +388,9 @@ __device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int n
                 if (rl >= rows) continue;
                 const int64_t row = row0 + rl;
                 if (KW == 1) {
-                    if (lane == 0 && a.y) {
+                    if (lane == 0 && a.push) {
+                        peer_slots_store(a.push, row, acc[r][0], push_epoch);
+                    } else if (lane == 0 && a.y) {
 #pragma unroll
                         for (int tt = 0; tt < B; ++tt) a.y[(int64_t)tt * a.N + row] = acc[r][tt];
                     }
@@ -393,7 +403,11 @@ __device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int n
                     if (old == (uint32_t)KW - 1) {
                         __threadfence_block();
                         cnt[s * R + rl] = 0u;
-                        if (a.y) {
+                        if (a.push) {
+                            float v = 0.0f;
+                            for (int k = 0; k < KW; ++k) v += reinterpret_cast<volatile float*>(pp)[k * B];
+                            peer_slots_store(a.push, row, v, push_epoch);
+                        } else if (a.y) {
 #pragma unroll
                             for (int tt = 0; tt < B; ++tt) {
                                 float v = 0.0f;
@@ -408,6 +422,10 @@ __device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int n
         fence_generic_async_smem();  // this warp's reads of the stage before its refill
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (a.push) {  // every consumer warp has stored: the grid's last CTA advances the epoch counter
+        named_barrier(2, NCW * 32);
+        if (cw == 0 && lane == 0) peer_slots_done(a.push, ncta, push_epoch);
     }
 }
 

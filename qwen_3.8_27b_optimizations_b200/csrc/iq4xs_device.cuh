@@ -10,6 +10,8 @@
 //   bytes 0-1 d = trunc_fp16(amax/127), bytes 2-3 s = trunc_fp16(sum), bytes 4-35 int8 q.
 #pragma once
 
+#include "../../include/iq4xs_peer.h"
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -278,6 +280,93 @@ __device__ __forceinline__ float lds_f32(uint32_t addr) {
     float v;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
     return v;
+}
+
+// ------------------------------------------------------------------------------ peer flags
+// System-scope release store / acquire load of a 32-bit flag (another GPU's memory or written by
+// another GPU).
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Fused all-reduce (low-latency protocol): a slot word is {fp32 value bits, epoch}; single 8-byte
+// relaxed system-scope accesses, so a reader sees either the old word or the new one whole.
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Producer: the epoch of this all-reduce (read by every CTA before it stores; the grid's last CTA
+// advances the counter once all CTAs have stored).
+__device__ __forceinline__ uint32_t peer_slots_epoch_next(const iq4xs_peer_slots* p) {
+    return *reinterpret_cast<const volatile uint32_t*>(p->counter) + 1u;
+}
+
+// Producer: output `row` into slot `rank` of every rank's area.
+__device__ __forceinline__ void peer_slots_store(const iq4xs_peer_slots* p, int64_t row, float v, uint32_t e) {
+    const uint64_t w = ((uint64_t)e << 32) | (uint64_t)__float_as_uint(v);
+    const int world = p->world;
+    for (int q = 0; q < world && q < IQ4XS_MAX_PEERS; ++q) st_relaxed_sys_u64(p->dst[q] + row, w);
+}
+
+// Producer, one thread per CTA after the CTA's stores: the last CTA advances the epoch counter.
+__device__ __forceinline__ void peer_slots_done(const iq4xs_peer_slots* p, int ncta, uint32_t e) {
+    uint32_t* cnt = p->counter;
+    if (atomicAdd(cnt + 1, 1u) == (uint32_t)ncta - 1u) {
+        cnt[1] = 0u;
+        reinterpret_cast<volatile uint32_t*>(cnt)[0] = e;
+    }
+}
+
+// Consumer: the epoch the producer on this rank (complete before the consumer reads) advanced to.
+__device__ __forceinline__ uint32_t peer_slots_epoch(const iq4xs_peer_slots* p) {
+    return *reinterpret_cast<const volatile uint32_t*>(p->counter);
+}
+
+// Consumer: value i of slot q once it carries epoch e (bounded: a read that gives up records
+// kDevErrPeerWait and returns the stale value).
+__device__ __forceinline__ float peer_slot_value(const iq4xs_peer_slots* p, int q, int64_t n, int64_t i, uint32_t e,
+                                                 uint32_t* err) {
+    const uint64_t* a = p->local + (int64_t)q * n + i;
+    uint64_t w = ld_relaxed_sys_u64(a);
+    if ((uint32_t)(w >> 32) != e) {
+        const uint32_t limit = p->spin_limit ? p->spin_limit : (1u << 24);
+        uint32_t k = 0;
+        do {
+            if (++k > limit) {
+                record_error(err, kDevErrPeerWait);
+                break;
+            }
+            __nanosleep(32);
+            w = ld_relaxed_sys_u64(a);
+        } while ((uint32_t)(w >> 32) != e);
+    }
+    return __uint_as_float((uint32_t)w);
+}
+
+// Consumer: delta[i] = the ranks' values added in rank order (slot 0 first), the order and rounding
+// of iq4xs_peer_collective's all-reduce.
+__device__ __forceinline__ float peer_slots_sum1(const iq4xs_peer_slots* p, int64_t n, int64_t i, uint32_t e,
+                                                 uint32_t* err) {
+    float s = peer_slot_value(p, 0, n, i, e, err);
+    const int world = p->world;
+    for (int q = 1; q < world && q < IQ4XS_MAX_PEERS; ++q) s += peer_slot_value(p, q, n, i, e, err);
+    return s;
+}
+
+__device__ __forceinline__ float4 peer_slots_sum4(const iq4xs_peer_slots* p, int64_t n, int64_t i, uint32_t e,
+                                                  uint32_t* err) {
+    return make_float4(peer_slots_sum1(p, n, i, e, err), peer_slots_sum1(p, n, i + 1, e, err),
+                       peer_slots_sum1(p, n, i + 2, e, err), peer_slots_sum1(p, n, i + 3, e, err));
 }
 
 }  // namespace iq4xs

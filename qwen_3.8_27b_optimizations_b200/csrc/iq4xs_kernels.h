@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/iq4xs_peer.h"
+
 namespace iq4xs {
 
 // Where a GEMV's Q8_1 activations come from.  The fp32 sources are quantised (and, for kActNorm,
@@ -22,6 +24,7 @@ struct ActSource {
     const float* w;      // kActNorm
     float* x_out;        // kActNorm: x + delta is written here by CTA 0 (may be null; must not alias x)
     float eps;
+    const iq4xs_peer_slots* peer;  // kActNorm: delta = the fused all-reduce of these slots (device memory)
 };
 
 struct GemvArgs {
@@ -44,6 +47,7 @@ struct GemvArgs {
     float* partials;     // tensor-core kernel: cross-CTA partial sums
     size_t partial_bytes;
     ActSource act;       // activation source (kActQ8: `q8` above)
+    const iq4xs_peer_slots* push;  // batch 1: outputs go to slot `rank` of every rank's area, then the signal
 };
 
 struct GemvMmaArgs {
@@ -153,7 +157,8 @@ cudaError_t ensure_dynamic_smem(const void* kern, int bytes);
 
 // Decoder step operations (decode_ops.cu).
 cudaError_t launch_residual_rmsnorm_q8(float* x, const float* delta, const float* w, int D, int T, float eps,
-                                       uint8_t* q8, float* h_out, cudaStream_t stream, bool pdl);
+                                       uint8_t* q8, float* h_out, cudaStream_t stream, bool pdl,
+                                       const iq4xs_peer_slots* peer = nullptr);
 cudaError_t launch_attention_decode_q8(const float* qkv, __half* kc, __half* vc, const float* cosb,
                                        const float* sinb, const int64_t* pos, int hq, int hkv, int max_seq,
                                        uint8_t* q8, float* o_out, uint32_t* err, cudaStream_t stream, bool pdl);

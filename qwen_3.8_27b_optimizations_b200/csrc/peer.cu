@@ -43,15 +43,6 @@ struct PeerArgs {
     uint32_t* err;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __global__ void __launch_bounds__(kPeerThreads) peer_collective_kernel(const PeerArgs a) {
     __shared__ uint32_t epoch;
     if (threadIdx.x == 0) epoch = a.counter[0] + 1u;

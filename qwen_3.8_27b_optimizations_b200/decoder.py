@@ -53,6 +53,14 @@ def split_units(n: int, world: int, rank: int):
     return n * rank // world, n * (rank + 1) // world
 
 
+class _PeerDelta:
+    """The o_proj / down_proj output of a fused all-reduce: still spread over the ranks' slots of a
+    peer area; the next fused kernel (norm + GEMV, or the final norm) sums it in its prologue."""
+
+    def __init__(self, slots):
+        self.slots = slots
+
+
 class TPDecoder:
     """One rank's share of the decoder.  `matmul(W, X, N) -> Y [M][N]` (fp32 X [M][K]) defaults to the
     CUDA kernels; tests on CPU ranks inject a reference."""
@@ -60,7 +68,7 @@ class TPDecoder:
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, group=None, seed: int = 0,
                  device="cuda", matmul: Optional[Callable] = None, gen_weights: Optional[Callable] = None,
                  gen_normal: Optional[Callable] = None, fused_decode: Optional[bool] = None,
-                 peer_collectives: Optional[bool] = None, emulate_ranks: int = 1):
+                 peer_collectives: Optional[bool] = None, emulate_ranks: int = 1, fused_allreduce: bool = True):
         import torch
         from . import sharded
         self.torch = torch
@@ -143,7 +151,13 @@ class TPDecoder:
         if peer_collectives and world > 1:
             from .peer import PeerGroup
             lm_pad = sharded.max_shard_rows(cfg.vocab, world)
-            self.peers = PeerGroup(max(D, 8 * lm_pad), areas=3, group=group, device=self.device)
+            self.peers = PeerGroup(max(2 * world * D, 8 * lm_pad), areas=3, group=group, device=self.device)
+        # fused all-reduce (o_proj / down_proj GEMV epilogues push their rows into every rank's slot,
+        # the next kernel's norm prologue sums the slots) instead of a collective kernel per GEMV
+        self.fused_allreduce = bool(fused_allreduce) and self.peers is not None
+        if self.fused_allreduce:  # the device descriptors exist before any graph capture
+            for area in (0, 1):
+                self.peers.slots(area, D)
         self.lm_head = sharded.RowShardedIQ4XS(lm[r0:r1].contiguous(), cfg.vocab, D, group=group, rank=rank,
                                                world=world, local_gemv=self._lm_local if matmul else None,
                                                local_gemm=self._lm_local_t if matmul else None, peers=self.peers,
@@ -258,8 +272,11 @@ class TPDecoder:
 
         def norm_gemv(W, w, N, out):
             nonlocal cur, nxt
-            api.dec_rmsnorm_gemv(W, cur, w, cfg.eps, N, delta=delta, x_out=nxt if delta is not None else None,
-                                 out=out, flags=PDL)
+            if isinstance(delta, _PeerDelta):
+                api.dec_rmsnorm_gemv_peer(W, cur, delta.slots, w, cfg.eps, N, x_out=nxt, out=out, flags=PDL)
+            else:
+                api.dec_rmsnorm_gemv(W, cur, w, cfg.eps, N, delta=delta, x_out=nxt if delta is not None else None,
+                                     out=out, flags=PDL)
             if delta is not None:
                 cur, nxt = nxt, cur
 
@@ -271,8 +288,12 @@ class TPDecoder:
             norm_gemv(L["wgu"], L["fn"], 2 * self.F, b["gu"])
             api.dec_swiglu_q8(b["gu"], self.F, q8=b["q8f"], flags=PDL)
             delta = self._reduce_gemv(L["wd"], b["q8f"], self.F, b["d"], 1, L.get("wd_parts"))
-        api.dec_residual_rmsnorm_q8(cur, self.final_norm, cfg.eps, delta=delta, h_out=b["h"], want_q8=False,
-                                    flags=PDL)
+        if isinstance(delta, _PeerDelta):
+            api.dec_residual_rmsnorm_q8_peer(cur, delta.slots, self.final_norm, cfg.eps, h_out=b["h"], want_q8=False,
+                                             flags=PDL)
+        else:
+            api.dec_residual_rmsnorm_q8(cur, self.final_norm, cfg.eps, delta=delta, h_out=b["h"], want_q8=False,
+                                        flags=PDL)
         return b["h"]
 
     def _reduce_gemv(self, W, q8, K, out, area, parts=None):
@@ -294,6 +315,10 @@ class TPDecoder:
             return out
         if self.peers is None:
             return self._allreduce(api.gemv_q8_ex(W, q8, K, D, 1, out=out, flags=api.FLAG_OVERLAP_PRECEDING))
+        if self.fused_allreduce:
+            slots = self.peers.slots(area, D)
+            api.dec_gemv_q8_push(W, q8, K, D, slots, flags=api.FLAG_PDL)
+            return _PeerDelta(slots)
         api.gemv_q8_ex(W, q8, K, D, 1, out=self.peers.area(area, D).view(1, D), flags=api.FLAG_OVERLAP_PRECEDING)
         self.peers.allreduce(area, D, out)
         return out

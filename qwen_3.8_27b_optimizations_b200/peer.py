@@ -88,6 +88,28 @@ class PeerGroup:
             raise ValueError("out: contiguous float32 with at least world*n elements")
         return self._run(i, n, out, True)
 
+    def slots(self, i: int, n: int):
+        """Device descriptor (iq4xs_peer_slots) of the fused all-reduce over area i with `world` slots
+        of n 64-bit words (value + epoch tag): slot q of every area is rank q's partial output
+        (dec_gemv_q8_push writes it, dec_rmsnorm_gemv_peer / dec_residual_rmsnorm_q8_peer sum the
+        slots in rank order)."""
+        if 2 * n * self.world > self.area_floats:
+            raise ValueError(f"{self.world} slots of {n} words do not fit an area of {self.area_floats} floats")
+        key = ("slots", i, n)
+        v = self._views.get(key)
+        if v is None:
+            api, torch = self.api, self.torch
+            d = api.PeerSlots()
+            for q in range(self.world):
+                d.dst[q] = self._area_addr(q, i) + 8 * n * self.rank
+            d.local = self._area_addr(self.rank, i)
+            d.counter = self.counter.data_ptr()
+            d.rank, d.world, d.spin_limit = self.rank, self.world, 0
+            raw = bytes(memoryview(d))
+            v = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.device)
+            self._views[key] = v
+        return v
+
     def close(self):
         """Unmap the peers' buffers, then (after every rank has unmapped ours) free this rank's."""
         import torch.distributed as dist

@@ -4,7 +4,8 @@ concatenation of the ranks' inputs (and within fp32 rounding of NCCL's all-reduc
 with alternating areas, the same collectives replayed from a CUDA graph, the row-sharded GEMV with
 the peer all-gather against the single-GPU kernel, and the tensor-parallel decoder with peer
 collectives against the same model with NCCL all-reduces and, bit for bit, against its single-GPU
-rank emulation.  NVLS is off; no multicast memory is
+rank emulation -- with the all-reduce fused into the row-parallel GEMVs (push epilogue, summed in
+the next kernel's prologue) and with the separate collective kernel.  NVLS is off; no multicast memory is
 used."""
 import os
 
@@ -120,20 +121,25 @@ def _worker(rank, world, port, q):
             res["decoder_logits"] = bool(torch.dot(a, b) / (a.norm() * b.norm()) >= 0.999)
         # exact: fixed decode inputs from position 0 with peer collectives (rank-order sums) against
         # the single-GPU emulation of the same ranks (o_proj / down_proj K slices added in rank order)
+        # (the fused all-reduce in the GEMV epilogues and the separate collective kernel alike)
         seqs = {}
-        for emu in (False, True):
+        for kind in ("fused", "collective", "emu"):
+            emu = kind == "emu"
             m = dec.TPDecoder(cfg, rank=0 if emu else rank, world=1 if emu else world, seed=4,
-                              peer_collectives=None if emu else True, emulate_ranks=world if emu else 1)
+                              peer_collectives=None if emu else True, emulate_ranks=world if emu else 1,
+                              fused_allreduce=kind == "fused")
+            assert emu or m.fused_allreduce == (kind == "fused")
             m.reset_decode(0)
             out = []
             for t in (5, 1234, 77, 3001):
                 m._tok.fill_(t)
                 m._step()
                 out.append(m._last_logits.clone())
-            seqs[emu] = torch.cat(out)
+            seqs[kind] = torch.cat(out)
             m.release()
             del m
-        res["decoder_exact_vs_emulation"] = bool(torch.equal(seqs[False], seqs[True]))
+        res["decoder_exact_vs_emulation"] = bool(torch.equal(seqs["fused"], seqs["emu"]))
+        res["decoder_collective_exact_vs_emulation"] = bool(torch.equal(seqs["collective"], seqs["emu"]))
         torch.cuda.synchronize()
         q.put((rank, res, P.device_error(), lg[True][0]))
     finally:
