@@ -562,7 +562,7 @@ int iq4xs_dec_rmsnorm_gemv_peer(const void* W, const float* x, const iq4xs_peer_
         return IQ4XS_ERR_NOT_SUPPORTED;
     GemvArgs a = make_gemv_args(W, nullptr, Y, K, N);
     attach_workspace(a, workspace, 0, K, N, 1);
-    a.act.mode = kActNorm;
+    a.act.mode = kActNormPeer;
     a.act.x = x;
     a.act.peer = slots;
     a.act.w = w;

@@ -42,13 +42,15 @@ constexpr int kNormCtas = 8;
 constexpr int kNormWarps = 4;
 constexpr int kNormMaxPer = 8;  // blocks per warp: D <= 8192
 
+// kPeer: delta is the fused all-reduce of `peer`'s slots instead of a vector (T = 1).
+template <bool kPeer>
 __global__ void __cluster_dims__(kNormCtas, 1, 1) __launch_bounds__(kNormWarps * 32) residual_rmsnorm_q8_kernel(
     float* __restrict__ x, const float* __restrict__ delta, const float* __restrict__ w, int D, float eps,
     uint8_t* __restrict__ q8, float* __restrict__ h_out, const iq4xs_peer_slots* peer, uint32_t* err) {
     namespace cg = cooperative_groups;
     grid_launch_dependents();
     grid_dependency_wait();
-    const uint32_t ep = peer ? peer_slots_epoch(peer) : 0u;  // delta = the fused all-reduce of the slots
+    const uint32_t ep = kPeer ? peer_slots_epoch(peer) : 0u;
     __shared__ float red[kNormWarps];
     __shared__ float css;
     cg::cluster_group cluster = cg::this_cluster();
@@ -58,25 +60,31 @@ __global__ void __cluster_dims__(kNormCtas, 1, 1) __launch_bounds__(kNormWarps *
     const int b0 = nb * crank / kNormCtas, b1 = nb * (crank + 1) / kNormCtas;
     float* xr = x + (int64_t)t * D;
     const float* dr = delta ? delta + (int64_t)t * D : nullptr;
-    float v[kNormMaxPer], wv[kNormMaxPer];
-    float ss = 0.f;
+    float v[kNormMaxPer], wv[kNormMaxPer], dv[kNormMaxPer];
+    int idx[kNormMaxPer];
+    bool ok[kNormMaxPer];
 #pragma unroll
     for (int j = 0; j < kNormMaxPer; ++j) {
         const int b = b0 + warp + j * kNormWarps;
-        v[j] = wv[j] = 0.f;
-        if (b < b1) {
-            const int e = b * kQK8 + lane;
-            wv[j] = w[e];
-            float a = xr[e];
-            if (peer) {
-                a = __fadd_rn(a, peer_slots_sum1(peer, D, e, ep, err));
-                xr[e] = a;
-            } else if (dr) {
-                a = __fadd_rn(a, dr[e]);
-                xr[e] = a;
+        ok[j] = b < b1;
+        idx[j] = b * kQK8 + lane;
+        v[j] = wv[j] = dv[j] = 0.f;
+        if (ok[j]) {
+            wv[j] = w[idx[j]];
+            v[j] = xr[idx[j]];
+            if (dr) dv[j] = dr[idx[j]];
+        }
+    }
+    if constexpr (kPeer) peer_slots_sum1_batch<kNormMaxPer>(peer, D, idx, ok, ep, err, dv);  // a slot's loads together
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNormMaxPer; ++j) {
+        if (ok[j]) {
+            if (kPeer || dr) {
+                v[j] = __fadd_rn(v[j], dv[j]);
+                xr[idx[j]] = v[j];
             }
-            v[j] = a;
-            ss = fmaf(a, a, ss);
+            ss = fmaf(v[j], v[j], ss);
         }
     }
 #pragma unroll
@@ -393,7 +401,10 @@ cudaError_t launch_residual_rmsnorm_q8(float* x, const float* delta, const float
                                        const iq4xs_peer_slots* peer) {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = launch_cfg(dim3(kNormCtas, (unsigned)T), dim3(kNormWarps * 32), 0, stream, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, residual_rmsnorm_q8_kernel, x, delta, w, D, eps, q8, h_out, peer,
+    if (peer)
+        return cudaLaunchKernelEx(&cfg, residual_rmsnorm_q8_kernel<true>, x, delta, w, D, eps, q8, h_out, peer,
+                                  device_error_word());
+    return cudaLaunchKernelEx(&cfg, residual_rmsnorm_q8_kernel<false>, x, delta, w, D, eps, q8, h_out, peer,
                               device_error_word());
 }
 

@@ -62,18 +62,18 @@ __device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
 }
 
 // Packed fp32 pair arithmetic (sm_100): d = a * b and d = a * b + d, two lanes per instruction.
+// (The float2 builtins let the register allocator place the pairs; inline asm that packs two
+// scalars into a .b64 operand costs register moves when the scalars are not an aligned pair.)
 __device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+    const float2 r = __fmul2_rn(make_float2(a0, a1), make_float2(b0, b1));
+    d0 = r.x;
+    d1 = r.y;
 }
 
 __device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rd, {%0, %1};\n\t"
-        "fma.rn.f32x2 rd, ra, rb, rd;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "+f"(d0), "+f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+    const float2 r = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(d0, d1));
+    d0 = r.x;
+    d1 = r.y;
 }
 
 // Bounded sleeping wait on one phase parity; gives up (error word + abort flag) after ~20 s or
@@ -98,10 +98,9 @@ __device__ __forceinline__ void gdrain(uint64_t* bar, uint32_t parity, uint32_t*
 
 // d = a * b + c, two lanes per instruction.
 __device__ __forceinline__ void fma2c(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
-    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+    const float2 r = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(c0, c1));
+    d0 = r.x;
+    d1 = r.y;
 }
 
 // Two phases in turn, each with the sleeping wait: a waiting thread issues (almost) nothing until the

@@ -105,13 +105,38 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
                                              int ncw, int lane, int bar_id, bool first_cta, uint32_t* err) {
     const int nq = B * K / 128;
     const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    if constexpr (kAct == kActNorm) {
-        // delta: a plain vector, or the fused all-reduce of the ranks' slots (each word read until it
-        // carries the current epoch)
-        const bool has_delta = act.delta != nullptr || act.peer != nullptr;
-        const uint32_t ep = act.peer ? peer_slots_epoch(act.peer) : 0u;
-        auto delta4 = [&](int off) -> float4 {
-            return act.peer ? peer_slots_sum4(act.peer, K, off, ep, err) : ldg4(act.delta + off);
+    if constexpr (kAct == kActNorm || kAct == kActNormPeer) {
+        // delta: a plain vector (kActNorm), or the fused all-reduce of the ranks' slots (kActNormPeer:
+        // each word read until it carries the current epoch)
+        constexpr bool kPeer = kAct == kActNormPeer;
+        const bool has_delta = kPeer || act.delta != nullptr;
+        const uint32_t ep = kPeer ? peer_slots_epoch(act.peer) : 0u;
+        // delta of the batch's quads; the slots' words are loaded for half the batch at a time (all
+        // of a half's loads in flight together; the whole batch at once would spill registers)
+        auto delta_batch = [&](int base, float4(&da)[kActQ]) {
+            constexpr int H = kActQ / 2;
+#pragma unroll
+            for (int h = 0; h < kActQ; h += H) {
+                int off[H];
+                bool ok[H];
+                float4 d[H];
+#pragma unroll
+                for (int i = 0; i < H; ++i) {
+                    const int qd = base + (h + i) * ncw;
+                    ok[i] = qd < nq;
+                    off[i] = qd * 128 + 4 * lane;
+                    d[i] = zero4;
+                }
+                if constexpr (kPeer) {
+                    peer_slots_sum4_batch<H>(act.peer, K, off, ok, ep, err, d);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < H; ++i)
+                        if (ok[i]) d[i] = ldg4(act.delta + off[i]);
+                }
+#pragma unroll
+                for (int i = 0; i < H; ++i) da[h + i] = d[i];
+            }
         };
         float4 v0[kActQ], w0[kActQ];
         float ss = 0.0f;
@@ -120,13 +145,13 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
 #pragma unroll
             for (int i = 0; i < kActQ; ++i) {
                 const int qd = base + i * ncw;
-                xa[i] = da[i] = zero4;
+                xa[i] = zero4;
                 if (qd < nq) {
                     xa[i] = ldg4(act.x + qd * 128 + 4 * lane);
-                    if (has_delta) da[i] = delta4(qd * 128 + 4 * lane);
                     if (base == cw) w0[i] = ldg4(act.w + qd * 128 + 4 * lane);
                 }
             }
+            if (has_delta) delta_batch(base, da);
 #pragma unroll
             for (int i = 0; i < kActQ; ++i) {
                 const int qd = base + i * ncw;
@@ -148,7 +173,7 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
         for (int i = 0; i < ncw; ++i) tot += red[i];
         const float r = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), act.eps));
         for (int base = cw; base < nq; base += ncw * kActQ) {
-            float4 va[kActQ], wa[kActQ];
+            float4 va[kActQ], wa[kActQ], da[kActQ];
 #pragma unroll
             for (int i = 0; i < kActQ; ++i) {
                 const int qd = base + i * ncw;
@@ -159,9 +184,13 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
                     wa[i] = w0[i];
                 } else {
                     va[i] = ldg4(act.x + qd * 128 + 4 * lane);
-                    if (has_delta) va[i] = add4_rn(va[i], delta4(qd * 128 + 4 * lane));
                     wa[i] = ldg4(act.w + qd * 128 + 4 * lane);
                 }
+            }
+            if (has_delta && base != cw) {
+                delta_batch(base, da);
+#pragma unroll
+                for (int i = 0; i < kActQ; ++i) va[i] = add4_rn(va[i], da[i]);
             }
 #pragma unroll
             for (int i = 0; i < kActQ; ++i) {
@@ -211,7 +240,7 @@ __device__ __forceinline__ void lut_word(const uint32_t (&tab)[4], uint32_t x, u
     l1 = prmt(tab[0], tab[1], sel_hi16(x));
 }
 
-// kAct: where the activations come from (ActMode).  kActF32 / kActNorm build them into shared memory
+// kAct: where the activations come from (ActMode).  kActF32 / kActNorm / kActNormPeer build them into shared memory
 // (build_act_q8); each instance carries only its own prologue (code size costs instruction-cache
 // misses in the hot loop).
 // The kernel body, for CTA `cta` of the `ncta` CTAs that share the matrix (the single-matrix kernel
@@ -586,6 +615,9 @@ void* rows_kernel_ptr(bool tail, int mode) {
     if constexpr (kDebug) {  // the debug path reads Q8_1 from global memory only
         return rows_kernel_ptr_t<B, SPL, true, kActQ8>(tail);
     } else {
+        if constexpr (B == 1) {
+            if (mode == kActNormPeer) return rows_kernel_ptr_t<B, SPL, false, kActNormPeer>(tail);
+        }
         if (mode == kActNorm) return rows_kernel_ptr_t<B, SPL, false, kActNorm>(tail);
         if (mode == kActF32) return rows_kernel_ptr_t<B, SPL, false, kActF32>(tail);
         return rows_kernel_ptr_t<B, SPL, false, kActQ8>(tail);
@@ -626,7 +658,7 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     constexpr int NCW = kRowNCW;
     int kw = 1, spl = 1;
     if (!row_split(a.K, B, &kw, &spl)) {  // K too long for register-resident activations: tensor-core kernel
-        if (a.act.mode == kActNorm) return cudaErrorNotSupported;
+        if (a.act.mode == kActNorm || a.act.mode == kActNormPeer) return cudaErrorNotSupported;
         return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.partials, a.partial_bytes, a.K, a.N,
                                B, stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
     }
@@ -702,7 +734,7 @@ cudaError_t dispatch(int B, GemvArgs a, cudaStream_t stream, bool pdl) {
         }
     }
     if (B == 1) return launch_rows<1, kDebug>(a, stream, pdl, sms, smem_optin);
-    if (a.act.mode == kActNorm) return cudaErrorNotSupported;
+    if (a.act.mode == kActNorm || a.act.mode == kActNormPeer) return cudaErrorNotSupported;
     return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.partials, a.partial_bytes, a.K, a.N, B,
                            stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
 }

@@ -71,20 +71,20 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Fused multiply-add on fp32 pairs: (d0, d1) += (a0, a1) * (b0, b1), one instruction on sm_100.
+// Packed fp32 pairs, one instruction each on sm_100 (float2 builtins: the register allocator places
+// the pairs, where inline asm packing two scalars into a .b64 operand costs register moves).
+// (d0, d1) += (a0, a1) * (b0, b1)
 __device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rd, {%0, %1};\n\t"
-        "fma.rn.f32x2 rd, ra, rb, rd;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "+f"(d0), "+f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+    const float2 r = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(d0, d1));
+    d0 = r.x;
+    d1 = r.y;
 }
 
-// (d0, d1) = (a0, a1) - (b0, b1), one instruction on sm_100.
+// (d0, d1) = (a0, a1) - (b0, b1)  (a - b == a + (-b) exactly)
 __device__ __forceinline__ void sub2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+    const float2 r = __fadd2_rn(make_float2(a0, a1), make_float2(-b0, -b1));
+    d0 = r.x;
+    d1 = r.y;
 }
 
 // int32 -> fp32 without conversion instructions: MMA accumulators that start at kMagicI (the bit
@@ -92,11 +92,11 @@ __device__ __forceinline__ void sub2(float& d0, float& d1, float a0, float a1, f
 // |s| < 2^22 (a half-table sub-block dot is at most 32 * 127 * 127 = 516128 in magnitude).
 constexpr int kMagicI = 0x4B400000;
 
+// (d0, d1) = (a0, a1) * (b0, b1)
 __device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+    const float2 r = __fmul2_rn(make_float2(a0, a1), make_float2(b0, b1));
+    d0 = r.x;
+    d1 = r.y;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
@@ -235,12 +235,29 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
                 }
             }
         }
-        for (int q = cw, kq = 0; q < nchunks; q += kNCW, ++kq) {
-            const int n = q % B, r = q / B;
-            const int slot = r < ch0 ? 0 : 1;
-            const int sbl0 = (r - slot * ch0) * kStageChunk;
-            const int sb = (pfirst + slot) * pk * 16 + sbl0;
-            if constexpr (kF32) {  // quantise the chunk's 8 blocks from fp32 into the scratch
+        // chunk q -> token n, staged part slot, first sub-block (local and global)
+        auto chunk_pos = [&](int q, int& n, int& slot, int& sbl0, int& sb) {
+            n = q % B;
+            const int r = q / B;
+            slot = r < ch0 ? 0 : 1;
+            sbl0 = (r - slot * ch0) * kStageChunk;
+            sb = (pfirst + slot) * pk * 16 + sbl0;
+        };
+        // the chunk in the warp's scratch -> B-fragment words and d_x of its 8 blocks
+        auto chunk_build = [&](int n, int slot, int sbl0) {
+            __syncwarp();
+            const int bq = lane >> 2, j = lane & 3;
+            const uint32_t* blk = scr + bq * (kQ8Bytes / 4);
+            const int sbl = sbl0 + bq;
+            actw[(slot * pk * 16 + sbl) * 32 + n * 4 + j] = make_uint2(act_perm_lo(blk[1 + j], blk[5 + j]), act_perm_hi(blk[1 + j], blk[5 + j]));
+            if (j == 0) dxw[(slot * pk * 16 + sbl) * 8 + n] = f16_bits_to_f32(blk[0]);
+            __syncwarp();
+        };
+        if constexpr (kF32) {
+            for (int q = cw, kq = 0; q < nchunks; q += kNCW, ++kq) {
+                int n, slot, sbl0, sb;
+                chunk_pos(q, n, slot, sbl0, sb);
+                // quantise the chunk's 8 blocks from fp32 into the scratch
                 float4 x0 = xf[0][0], x1 = xf[0][1];
 #pragma unroll
                 for (int k = 1; k < kF32Chunks; ++k)
@@ -250,21 +267,46 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
                     }
                 q8_1_quad_store(x0, reinterpret_cast<uint8_t*>(scr), lane);
                 q8_1_quad_store(x1, reinterpret_cast<uint8_t*>(scr) + 4 * kQ8Bytes, lane);
-            } else {
-                const uint32_t* src = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb) * kQ8Bytes);
-                const uint32_t v0 = __ldg(src + lane), v1 = __ldg(src + 32 + lane);
-                const uint32_t v2 = lane < kChunkWords - 64 ? __ldg(src + 64 + lane) : 0u;
-                scr[lane] = v0;
-                scr[32 + lane] = v1;
-                if (lane < kChunkWords - 64) scr[64 + lane] = v2;
+                chunk_build(n, slot, sbl0);
             }
-            __syncwarp();
-            const int bq = lane >> 2, j = lane & 3;
-            const uint32_t* blk = scr + bq * (kQ8Bytes / 4);
-            const int sbl = sbl0 + bq;
-            actw[(slot * pk * 16 + sbl) * 32 + n * 4 + j] = make_uint2(act_perm_lo(blk[1 + j], blk[5 + j]), act_perm_hi(blk[1 + j], blk[5 + j]));
-            if (j == 0) dxw[(slot * pk * 16 + sbl) * 8 + n] = f16_bits_to_f32(blk[0]);
-            __syncwarp();
+        } else {
+            // Q8_1 source: the words of all of this warp's chunks (at most kQ8Pre) are loaded before
+            // any is used, so the staging costs one global round trip instead of one per chunk.
+            constexpr int kQ8Pre = 10;  // >= 2 slots * (16 * pk / 8) * B / kNCW for pk <= 5, B <= 8
+            uint32_t pv[kQ8Pre][3];
+#pragma unroll
+            for (int k = 0; k < kQ8Pre; ++k) {
+                const int q = cw + k * kNCW;
+                pv[k][0] = pv[k][1] = pv[k][2] = 0u;
+                if (q < nchunks) {
+                    int n, slot, sbl0, sb;
+                    chunk_pos(q, n, slot, sbl0, sb);
+                    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb) * kQ8Bytes);
+                    pv[k][0] = __ldg(src + lane);
+                    pv[k][1] = __ldg(src + 32 + lane);
+                    if (lane < kChunkWords - 64) pv[k][2] = __ldg(src + 64 + lane);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kQ8Pre; ++k) {
+                const int q = cw + k * kNCW;
+                if (q >= nchunks) break;
+                int n, slot, sbl0, sb;
+                chunk_pos(q, n, slot, sbl0, sb);
+                scr[lane] = pv[k][0];
+                scr[32 + lane] = pv[k][1];
+                if (lane < kChunkWords - 64) scr[64 + lane] = pv[k][2];
+                chunk_build(n, slot, sbl0);
+            }
+            for (int q = cw + kQ8Pre * kNCW; q < nchunks; q += kNCW) {  // not reached for pk <= 5, B <= 8
+                int n, slot, sbl0, sb;
+                chunk_pos(q, n, slot, sbl0, sb);
+                const uint32_t* src = reinterpret_cast<const uint32_t*>(a.q8 + ((int64_t)n * nsb + sb) * kQ8Bytes);
+                scr[lane] = __ldg(src + lane);
+                scr[32 + lane] = __ldg(src + 32 + lane);
+                if (lane < kChunkWords - 64) scr[64 + lane] = __ldg(src + 64 + lane);
+                chunk_build(n, slot, sbl0);
+            }
         }
         if constexpr (B < 8) {
             const int zitems = (nsubs[0] + nsubs[1]) * (8 - B);

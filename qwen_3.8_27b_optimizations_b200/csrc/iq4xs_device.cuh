@@ -333,7 +333,8 @@ __device__ __forceinline__ uint32_t peer_slots_epoch(const iq4xs_peer_slots* p) 
 }
 
 // Consumer: value i of slot q once it carries epoch e (bounded: a read that gives up records
-// kDevErrPeerWait and returns the stale value).
+// kDevErrPeerWait and returns the stale value; once the device error word is set, by this wait or
+// any other, a waiting read gives up within 1024 polls, so a missing peer costs one spin limit).
 __device__ __forceinline__ float peer_slot_value(const iq4xs_peer_slots* p, int q, int64_t n, int64_t i, uint32_t e,
                                                  uint32_t* err) {
     const uint64_t* a = p->local + (int64_t)q * n + i;
@@ -346,6 +347,7 @@ __device__ __forceinline__ float peer_slot_value(const iq4xs_peer_slots* p, int 
                 record_error(err, kDevErrPeerWait);
                 break;
             }
+            if ((k & 1023u) == 0u && err && *reinterpret_cast<volatile uint32_t*>(err) != 0u) break;
             __nanosleep(32);
             w = ld_relaxed_sys_u64(a);
         } while ((uint32_t)(w >> 32) != e);
@@ -359,14 +361,73 @@ __device__ __forceinline__ float peer_slots_sum1(const iq4xs_peer_slots* p, int6
                                                  uint32_t* err) {
     float s = peer_slot_value(p, 0, n, i, e, err);
     const int world = p->world;
-    for (int q = 1; q < world && q < IQ4XS_MAX_PEERS; ++q) s += peer_slot_value(p, q, n, i, e, err);
+    for (int q = 1; q < world && q < IQ4XS_MAX_PEERS; ++q) s = __fadd_rn(s, peer_slot_value(p, q, n, i, e, err));
     return s;
 }
 
-__device__ __forceinline__ float4 peer_slots_sum4(const iq4xs_peer_slots* p, int64_t n, int64_t i, uint32_t e,
-                                                  uint32_t* err) {
-    return make_float4(peer_slots_sum1(p, n, i, e, err), peer_slots_sum1(p, n, i + 1, e, err),
-                       peer_slots_sum1(p, n, i + 2, e, err), peer_slots_sum1(p, n, i + 3, e, err));
+__device__ __forceinline__ void ld_relaxed_sys_v2u64(const uint64_t* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Consumer, batched: s[j] = delta[off[j] .. off[j]+3] for the NQ quads with ok[j] (off[j] % 4 == 0).
+// For each slot, in rank order, the words of all NQ quads are loaded before any tag is checked, so
+// a slot whose words are all current costs one round trip; a stale word is then polled on its own
+// (bounded, peer_slot_value).  Each 8-byte word of a vector load is a single-copy-atomic access.
+template <int NQ>
+__device__ __forceinline__ void peer_slots_sum4_batch(const iq4xs_peer_slots* p, int64_t n, const int (&off)[NQ],
+                                                      const bool (&ok)[NQ], uint32_t e, uint32_t* err,
+                                                      float4 (&s)[NQ]) {
+    const int world = p->world;
+    for (int q = 0; q < world && q < IQ4XS_MAX_PEERS; ++q) {
+        const uint64_t* base = p->local + (int64_t)q * n;
+        uint64_t w[NQ][4];
+#pragma unroll
+        for (int j = 0; j < NQ; ++j) {
+            w[j][0] = w[j][1] = w[j][2] = w[j][3] = (uint64_t)e << 32;
+            if (ok[j]) {
+                ld_relaxed_sys_v2u64(base + off[j], w[j][0], w[j][1]);
+                ld_relaxed_sys_v2u64(base + off[j] + 2, w[j][2], w[j][3]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NQ; ++j) {
+            float v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                v[k] = (uint32_t)(w[j][k] >> 32) == e ? __uint_as_float((uint32_t)w[j][k])
+                                                      : peer_slot_value(p, q, n, off[j] + k, e, err);
+            }
+            if (q == 0) {
+                s[j] = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+                s[j].x = __fadd_rn(s[j].x, v[0]);
+                s[j].y = __fadd_rn(s[j].y, v[1]);
+                s[j].z = __fadd_rn(s[j].z, v[2]);
+                s[j].w = __fadd_rn(s[j].w, v[3]);
+            }
+        }
+    }
+}
+
+// Consumer, batched: s[j] = delta[idx[j]] for the NB indices with ok[j] (loads of one slot issued
+// together, as in peer_slots_sum4_batch).
+template <int NB>
+__device__ __forceinline__ void peer_slots_sum1_batch(const iq4xs_peer_slots* p, int64_t n, const int (&idx)[NB],
+                                                      const bool (&ok)[NB], uint32_t e, uint32_t* err,
+                                                      float (&s)[NB]) {
+    const int world = p->world;
+    for (int q = 0; q < world && q < IQ4XS_MAX_PEERS; ++q) {
+        const uint64_t* base = p->local + (int64_t)q * n;
+        uint64_t w[NB];
+#pragma unroll
+        for (int j = 0; j < NB; ++j) w[j] = ok[j] ? ld_relaxed_sys_u64(base + idx[j]) : ((uint64_t)e << 32);
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+            const float v = (uint32_t)(w[j] >> 32) == e ? __uint_as_float((uint32_t)w[j])
+                                                        : peer_slot_value(p, q, n, idx[j], e, err);
+            s[j] = q == 0 ? v : __fadd_rn(s[j], v);
+        }
+    }
 }
 
 }  // namespace iq4xs

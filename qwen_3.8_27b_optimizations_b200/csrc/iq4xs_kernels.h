@@ -16,6 +16,7 @@ enum ActMode : int {
     kActQ8 = 0,    // q8: Q8_1 blocks [B][K/32] in global memory
     kActF32 = 1,   // x: fp32 [B][K]
     kActNorm = 2,  // batch 1: h = rmsnorm(x + delta) * w, from fp32 x [K] (+ delta [K]), weight w [K]
+    kActNormPeer = 3,  // kActNorm with delta = the fused all-reduce of `peer` (its own kernel instance)
 };
 struct ActSource {
     int mode;
@@ -24,7 +25,7 @@ struct ActSource {
     const float* w;      // kActNorm
     float* x_out;        // kActNorm: x + delta is written here by CTA 0 (may be null; must not alias x)
     float eps;
-    const iq4xs_peer_slots* peer;  // kActNorm: delta = the fused all-reduce of these slots (device memory)
+    const iq4xs_peer_slots* peer;  // kActNormPeer: delta = the fused all-reduce of these slots (device memory)
 };
 
 struct GemvArgs {
