@@ -65,6 +65,26 @@ int iq4xs_dec_attention_decode_q8(const float* qkv, void* k_cache, void* v_cache
  * Q8_1 blocks q8 [T][F/32]. */
 int iq4xs_dec_swiglu_q8(const float* gu, int64_t F, int64_t T, void* q8, unsigned flags, cudaStream_t stream);
 
+/* SwiGLU fused into the batch-1 down_proj GEMV: Y[n] = sum_k W[n][k] q8(h)[k] with h = silu(gate) * up
+ * from gu [2K] (gate = [0, K), up = [K, 2K)): the Q8_1 blocks iq4xs_dec_swiglu_q8 would write.  For
+ * K <= 6144 every CTA of the GEMV builds them in its shared memory; for longer K the standalone SwiGLU
+ * kernel writes them into the workspace first (cheaper than K/32 blocks per CTA).  gu 16-byte aligned;
+ * the row kernel's K range (K/256 even, K <= 24576, W 16-byte aligned), otherwise
+ * IQ4XS_ERR_NOT_SUPPORTED.  workspace >= iq4xs_gemv_workspace_bytes(K, N, 1). */
+int iq4xs_dec_swiglu_gemv(const void* W, const float* gu, int64_t K, int64_t N, float* Y, void* workspace,
+                          size_t workspace_bytes, unsigned flags, cudaStream_t stream);
+
+/* x [D] fp32 = row *tok of the f16 embedding table emb [vocab][D] (tok: a device int64, so a captured
+ * decode step embeds the token the previous step chose).  D % 8 == 0; emb and x 16-byte aligned.  A
+ * token outside [0, vocab) makes the kernel record device error 7 and write nothing. */
+int iq4xs_dec_embed(const void* emb, const int64_t* tok, int64_t vocab, int64_t D, float* x, unsigned flags,
+                    cudaStream_t stream);
+
+/* Greedy sampling: *tok = the index of the largest of logits [n] (the first one on ties; a NaN
+ * counts as larger than any number, as in torch.argmax), then *pos += 1 when pos is not null (the
+ * decode step's position advances in the same kernel).  tok, pos: device int64. */
+int iq4xs_dec_argmax(const float* logits, int64_t n, int64_t* tok, int64_t* pos, unsigned flags, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -75,6 +75,10 @@ typedef struct iq4xs_peer_slots {
  * aligned); otherwise IQ4XS_ERR_NOT_SUPPORTED.  flags: IQ4XS_FLAG_PDL. */
 int iq4xs_dec_gemv_q8_push(const void* W, const void* q8, int64_t K, int64_t N, const iq4xs_peer_slots* slots,
                            void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream);
+/* iq4xs_dec_swiglu_gemv with the outputs pushed into slot `rank` of every rank's area, as
+ * iq4xs_dec_gemv_q8_push does. */
+int iq4xs_dec_swiglu_gemv_push(const void* W, const float* gu, int64_t K, int64_t N, const iq4xs_peer_slots* slots,
+                               void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream);
 /* iq4xs_dec_rmsnorm_gemv with delta = the fused all-reduce of `slots` (K = the slots' N). */
 int iq4xs_dec_rmsnorm_gemv_peer(const void* W, const float* x, const iq4xs_peer_slots* slots, const float* w, float eps,
                                 float* x_out, float* Y, int64_t K, int64_t N, void* workspace, size_t workspace_bytes,

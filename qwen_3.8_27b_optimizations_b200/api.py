@@ -84,6 +84,9 @@ DECODER_SIGNATURES = {
     "iq4xs_dec_attention_decode_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp,
                                            C.c_uint, _vp]),
     "iq4xs_dec_swiglu_q8": (_i, [_vp, _i64, _i64, _vp, C.c_uint, _vp]),
+    "iq4xs_dec_embed": (_i, [_vp, _vp, _i64, _i64, _vp, C.c_uint, _vp]),
+    "iq4xs_dec_swiglu_gemv": (_i, [_vp, _vp, _i64, _i64, _vp, _vp, _sz, C.c_uint, _vp]),
+    "iq4xs_dec_argmax": (_i, [_vp, _i64, _vp, _vp, C.c_uint, _vp]),
     "iq4xs_dec_rmsnorm_gemv": (_i, [_vp, _vp, _vp, _vp, _f, _vp, _vp, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
 }
 
@@ -96,6 +99,7 @@ PEER_SIGNATURES = {
     "iq4xs_ipc_close": (_i, [_vp]),
     "iq4xs_peer_collective": (_i, [C.POINTER(_vp), C.POINTER(_vp), _vp, _vp, _i, _i, _i, _i64, _vp, C.c_uint32, _vp]),
     "iq4xs_dec_gemv_q8_push": (_i, [_vp, _vp, _i64, _i64, _vp, _vp, _sz, C.c_uint, _vp]),
+    "iq4xs_dec_swiglu_gemv_push": (_i, [_vp, _vp, _i64, _i64, _vp, _vp, _sz, C.c_uint, _vp]),
     "iq4xs_dec_rmsnorm_gemv_peer": (_i, [_vp, _vp, _vp, _vp, _f, _vp, _vp, _i64, _i64, _vp, _sz, C.c_uint, _vp]),
     "iq4xs_dec_residual_rmsnorm_q8_peer": (_i, [_vp, _vp, _vp, _i64, _f, _vp, _vp, C.c_uint, _vp]),
 }
@@ -475,6 +479,42 @@ def dec_attention_decode_q8(qkv, k_cache, v_cache, cos, sin, pos, q_heads: int, 
         _ptr(qkv), _ptr(k_cache), _ptr(v_cache), _ptr(cos), _ptr(sin), _ptr(pos), q_heads, kv_heads, hd, max_seq,
         _ptr(q8), _ptr(o_out) if o_out is not None else None, flags, _stream(stream)))
     return q8
+
+
+def dec_swiglu_gemv(W, gu, K: int, N: int, out=None, slots=None, flags: int = 0, stream=None, workspace=None):
+    """Y [1][N] = W . q8(silu(gate) * up) for gu [1][2K] (the SwiGLU fused into the down_proj GEMV);
+    with `slots` (PeerGroup.slots) the outputs are pushed into every rank's slot instead (returns None)."""
+    torch = _torch()
+    ws = workspace if workspace is not None else _workspace(gemv_workspace_bytes(K, N, 1), gu.device)
+    nbytes = ws.numel() * ws.element_size()
+    if slots is not None:
+        _check("iq4xs_dec_swiglu_gemv_push", lib().iq4xs_dec_swiglu_gemv_push(
+            _ptr(W), _ptr(gu), K, N, _ptr(slots), _ptr(ws), nbytes, flags, _stream(stream)))
+        return None
+    Y = out if out is not None else torch.empty((1, N), dtype=torch.float32, device=gu.device)
+    _check("iq4xs_dec_swiglu_gemv", lib().iq4xs_dec_swiglu_gemv(
+        _ptr(W), _ptr(gu), K, N, _ptr(Y), _ptr(ws), nbytes, flags, _stream(stream)))
+    return Y
+
+
+def dec_embed(emb, tok, out=None, flags: int = 0, stream=None):
+    """out [1][D] fp32 = emb[tok] for the f16 table emb [vocab][D] and a device int64 token tok [1]."""
+    torch = _torch()
+    vocab, D = emb.shape
+    out = out if out is not None else torch.empty((1, D), dtype=torch.float32, device=emb.device)
+    _check("iq4xs_dec_embed", lib().iq4xs_dec_embed(_ptr(emb), _ptr(tok), vocab, D, _ptr(out), flags,
+                                                    _stream(stream)))
+    return out
+
+
+def dec_argmax(logits, tok, pos=None, flags: int = 0, stream=None):
+    """tok [1] (device int64) = argmax of the fp32 logits (first index on ties); pos [1] += 1 if given."""
+    if not logits.is_contiguous():
+        raise ValueError("logits must be contiguous")
+    _check("iq4xs_dec_argmax", lib().iq4xs_dec_argmax(_ptr(logits), logits.numel(), _ptr(tok),
+                                                      _ptr(pos) if pos is not None else None, flags,
+                                                      _stream(stream)))
+    return tok
 
 
 def dec_swiglu_q8(gu, F: int, q8=None, flags: int = 0, stream=None):

@@ -547,6 +547,37 @@ int iq4xs_dec_gemv_q8_push(const void* W, const void* q8, int64_t K, int64_t N, 
     return status_from(launch_gemv_q8(a, 1, stream, (flags & IQ4XS_FLAG_PDL) != 0));
 }
 
+// The SwiGLU GEMV of both entry points below (push: outputs to the peers' slots instead of Y).
+static int swiglu_gemv(const void* W, const float* gu, int64_t K, int64_t N, float* Y, const iq4xs_peer_slots* push,
+                void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream) {
+    int s = check_matrix(W, K, N);
+    if (s) return s;
+    if (!gu || !workspace || (!Y && !push)) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < iq4xs_gemv_workspace_bytes(K, N, 1)) return IQ4XS_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned(gu, 16) || (Y && !aligned(Y, 4)) || (push && !aligned(push, 8)) || !aligned(workspace, 256))
+        return IQ4XS_ERR_MISALIGNED;
+    if (!gemv_bulk_path(static_cast<const uint8_t*>(W), K) || gemv_takes_mma(static_cast<const uint8_t*>(W), K, 1))
+        return IQ4XS_ERR_NOT_SUPPORTED;  // the row kernel's K range
+    GemvArgs a = make_gemv_args(W, workspace, push ? nullptr : Y, K, N);
+    attach_workspace(a, workspace, iq4xs_q8_1_bytes(K, 1), K, N, 1);
+    a.act.mode = kActSwiGLU;
+    a.act.x = gu;
+    a.push = push;
+    return status_from(launch_gemv_q8(a, 1, stream, (flags & IQ4XS_FLAG_PDL) != 0));
+}
+
+int iq4xs_dec_swiglu_gemv(const void* W, const float* gu, int64_t K, int64_t N, float* Y, void* workspace,
+                          size_t workspace_bytes, unsigned flags, cudaStream_t stream) {
+    if (!Y) return IQ4XS_ERR_INVALID_ARGUMENT;
+    return swiglu_gemv(W, gu, K, N, Y, nullptr, workspace, workspace_bytes, flags, stream);
+}
+
+int iq4xs_dec_swiglu_gemv_push(const void* W, const float* gu, int64_t K, int64_t N, const iq4xs_peer_slots* slots,
+                               void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream) {
+    if (!slots) return IQ4XS_ERR_INVALID_ARGUMENT;
+    return swiglu_gemv(W, gu, K, N, nullptr, slots, workspace, workspace_bytes, flags, stream);
+}
+
 int iq4xs_dec_rmsnorm_gemv_peer(const void* W, const float* x, const iq4xs_peer_slots* slots, const float* w, float eps,
                                 float* x_out, float* Y, int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
                                 unsigned flags, cudaStream_t stream) {
@@ -579,6 +610,21 @@ int iq4xs_dec_residual_rmsnorm_q8_peer(float* x, const iq4xs_peer_slots* slots, 
         return IQ4XS_ERR_MISALIGNED;
     return status_from(launch_residual_rmsnorm_q8(x, nullptr, w, (int)D, 1, eps, static_cast<uint8_t*>(q8), h_out,
                                                   stream, (flags & IQ4XS_FLAG_PDL) != 0, slots));
+}
+
+int iq4xs_dec_embed(const void* emb, const int64_t* tok, int64_t vocab, int64_t D, float* x, unsigned flags,
+                    cudaStream_t stream) {
+    if (!emb || !tok || !x || vocab <= 0 || D <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (D % 8 != 0) return IQ4XS_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(emb, 16) || !aligned(tok, 8) || !aligned(x, 16)) return IQ4XS_ERR_MISALIGNED;
+    return status_from(launch_embed_f16(static_cast<const __half*>(emb), tok, vocab, D, x, stream,
+                                        (flags & IQ4XS_FLAG_PDL) != 0));
+}
+
+int iq4xs_dec_argmax(const float* logits, int64_t n, int64_t* tok, int64_t* pos, unsigned flags, cudaStream_t stream) {
+    if (!logits || !tok || n <= 0) return IQ4XS_ERR_INVALID_ARGUMENT;
+    if (!aligned(logits, 4) || !aligned(tok, 8) || (pos && !aligned(pos, 8))) return IQ4XS_ERR_MISALIGNED;
+    return status_from(launch_argmax(logits, n, tok, pos, stream, (flags & IQ4XS_FLAG_PDL) != 0));
 }
 
 int iq4xs_dec_swiglu_q8(const float* gu, int64_t F, int64_t T, void* q8, unsigned flags, cudaStream_t stream) {

@@ -380,6 +380,138 @@ __global__ void __launch_bounds__(256) swiglu_q8_kernel(const float* __restrict_
     }
 }
 
+// x[0..D) = the fp32 value of row *tok of the f16 embedding table emb [vocab][D] (the token is a
+// device int64, so a captured decode step reads the token the previous step chose).  A token
+// outside [0, vocab) records kDevErrToken and writes nothing.  D % 8 == 0, emb 16-byte aligned:
+// one 16-byte load of 8 halves per thread.
+__global__ void __launch_bounds__(256) embed_f16_kernel(const __half* __restrict__ emb, const int64_t* tok,
+                                                        int64_t vocab, int64_t D, float* __restrict__ x,
+                                                        uint32_t* err) {
+    grid_launch_dependents();
+    grid_dependency_wait();
+    const int64_t t = *tok;
+    if (t < 0 || t >= vocab) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) record_error(err, kDevErrToken);
+        return;
+    }
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (8 * i >= D) return;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(emb + t * D) + i);
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+    float4 lo, hi;
+    float2 f = __half22float2(h[0]);
+    lo.x = f.x;
+    lo.y = f.y;
+    f = __half22float2(h[1]);
+    lo.z = f.x;
+    lo.w = f.y;
+    f = __half22float2(h[2]);
+    hi.x = f.x;
+    hi.y = f.y;
+    f = __half22float2(h[3]);
+    hi.z = f.x;
+    hi.w = f.y;
+    reinterpret_cast<float4*>(x)[2 * i] = lo;
+    reinterpret_cast<float4*>(x)[2 * i + 1] = hi;
+}
+
+// Greedy sampling of one token: *tok = the index of the largest of v[0..n) (the first one on ties,
+// NaN above every number: torch.argmax's result), then *pos += 1 when pos is not null.  One cluster
+// of kArgCtas CTAs: CTA c scans [n*c/kArgCtas, n*(c+1)/kArgCtas) with coalesced loads, the CTAs'
+// winners meet in CTA 0 through distributed shared memory.
+constexpr int kArgCtas = 8;
+constexpr int kArgThreads = 512;
+
+// (a, ia) wins over (b, ib)
+__device__ __forceinline__ bool argmax_better(float a, int64_t ia, float b, int64_t ib) {
+    const bool na = a != a, nb = b != b;
+    if (na != nb) return na;
+    if (!na && a != b) return a > b;
+    return ia < ib;
+}
+
+__global__ void __cluster_dims__(kArgCtas, 1, 1) __launch_bounds__(kArgThreads)
+    argmax_kernel(const float* __restrict__ v, int64_t n, int64_t* tok, int64_t* pos) {
+    namespace cg = cooperative_groups;
+    grid_launch_dependents();
+    grid_dependency_wait();
+    __shared__ float wv[kArgThreads / 32];
+    __shared__ int64_t wi[kArgThreads / 32];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int crank = (int)cluster.block_rank();
+    const int64_t r0 = n * crank / kArgCtas, r1 = n * (crank + 1) / kArgCtas;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // four independent running winners per thread (loads in flight together), merged in index order
+    float bv[4];
+    int64_t bi[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        bv[k] = -INFINITY;
+        bi[k] = INT64_MAX;
+    }
+    for (int64_t i0 = r0 + threadIdx.x; i0 < r1; i0 += 4 * kArgThreads) {
+        float x[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int64_t i = i0 + (int64_t)k * kArgThreads;
+            x[k] = i < r1 ? __ldg(v + i) : -INFINITY;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int64_t i = i0 + (int64_t)k * kArgThreads;
+            if (i < r1 && argmax_better(x[k], i, bv[k], bi[k])) {
+                bv[k] = x[k];
+                bi[k] = i;
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 1; k < 4; ++k)
+        if (argmax_better(bv[k], bi[k], bv[0], bi[0])) {
+            bv[0] = bv[k];
+            bi[0] = bi[k];
+        }
+    float b = bv[0];
+    int64_t ib = bi[0];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ob = __shfl_xor_sync(0xFFFFFFFFu, b, off);
+        const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, ib, off);
+        if (argmax_better(ob, oi, b, ib)) {
+            b = ob;
+            ib = oi;
+        }
+    }
+    if (lane == 0) {
+        wv[warp] = b;
+        wi[warp] = ib;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kArgThreads / 32; ++w)
+            if (argmax_better(wv[w], wi[w], wv[0], wi[0])) {
+                wv[0] = wv[w];
+                wi[0] = wi[w];
+            }
+    }
+    cluster.sync();
+    if (crank == 0 && threadIdx.x == 0) {
+        float best = wv[0];
+        int64_t bidx = wi[0];
+        for (int c = 1; c < kArgCtas; ++c) {
+            const float cv = *cluster.map_shared_rank(&wv[0], c);
+            const int64_t ci = *cluster.map_shared_rank(&wi[0], c);
+            if (argmax_better(cv, ci, best, bidx)) {
+                best = cv;
+                bidx = ci;
+            }
+        }
+        *tok = bidx;
+        if (pos) *pos += 1;
+    }
+    cluster.sync();  // keep the CTAs' winners alive until CTA 0 has read them
+}
+
 namespace {
 cudaLaunchConfig_t launch_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
                               cudaLaunchAttribute* attr) {
@@ -449,6 +581,20 @@ cudaError_t launch_swiglu_q8(const float* gu, int64_t F, int64_t T, uint8_t* q8,
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = launch_cfg(dim3((unsigned)grid), dim3(256), 0, stream, pdl, attr);
     return cudaLaunchKernelEx(&cfg, swiglu_q8_kernel, gu, F, T, q8);
+}
+
+cudaError_t launch_embed_f16(const __half* emb, const int64_t* tok, int64_t vocab, int64_t D, float* x,
+                             cudaStream_t stream, bool pdl) {
+    const int64_t grid = (D / 8 + 255) / 256;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = launch_cfg(dim3((unsigned)grid), dim3(256), 0, stream, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, embed_f16_kernel, emb, tok, vocab, D, x, device_error_word());
+}
+
+cudaError_t launch_argmax(const float* v, int64_t n, int64_t* tok, int64_t* pos, cudaStream_t stream, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = launch_cfg(dim3(kArgCtas), dim3(kArgThreads), 0, stream, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, v, n, tok, pos);
 }
 
 }  // namespace iq4xs

@@ -204,6 +204,32 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
                 q8_1_quad_store(h, q8s + (size_t)qd * 4 * kQ8Bytes, lane);
             }
         }
+    } else if constexpr (kAct == kActSwiGLU) {
+        // the values of swiglu_q8_kernel (silu(g) = g / (1 + exp(-g)), then * u, each rounded once)
+        constexpr int kQS = kActQF / 2;
+        for (int base = cw; base < nq; base += ncw * kQS) {
+            float4 ga[kQS], ua[kQS];
+#pragma unroll
+            for (int i = 0; i < kQS; ++i) {
+                const int qd = base + i * ncw;
+                ga[i] = ua[i] = zero4;
+                if (qd < nq) {
+                    ga[i] = ldg4(act.x + (int64_t)qd * 128 + 4 * lane);
+                    ua[i] = ldg4(act.x + K + (int64_t)qd * 128 + 4 * lane);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kQS; ++i) {
+                const int qd = base + i * ncw;
+                if (qd >= nq) continue;
+                float4 h;
+                h.x = __fmul_rn(__fdiv_rn(ga[i].x, __fadd_rn(1.0f, expf(-ga[i].x))), ua[i].x);
+                h.y = __fmul_rn(__fdiv_rn(ga[i].y, __fadd_rn(1.0f, expf(-ga[i].y))), ua[i].y);
+                h.z = __fmul_rn(__fdiv_rn(ga[i].z, __fadd_rn(1.0f, expf(-ga[i].z))), ua[i].z);
+                h.w = __fmul_rn(__fdiv_rn(ga[i].w, __fadd_rn(1.0f, expf(-ga[i].w))), ua[i].w);
+                q8_1_quad_store(h, q8s + (size_t)qd * 4 * kQ8Bytes, lane);
+            }
+        }
     } else {
         for (int base = cw; base < nq; base += ncw * kActQF) {
             float4 xa[kActQF];
@@ -240,7 +266,7 @@ __device__ __forceinline__ void lut_word(const uint32_t (&tab)[4], uint32_t x, u
     l1 = prmt(tab[0], tab[1], sel_hi16(x));
 }
 
-// kAct: where the activations come from (ActMode).  kActF32 / kActNorm / kActNormPeer build them into shared memory
+// kAct: where the activations come from (ActMode).  Every source but kActQ8 builds them into shared memory
 // (build_act_q8); each instance carries only its own prologue (code size costs instruction-cache
 // misses in the hot loop).
 // The kernel body, for CTA `cta` of the `ncta` CTAs that share the matrix (the single-matrix kernel
@@ -617,6 +643,7 @@ void* rows_kernel_ptr(bool tail, int mode) {
     } else {
         if constexpr (B == 1) {
             if (mode == kActNormPeer) return rows_kernel_ptr_t<B, SPL, false, kActNormPeer>(tail);
+            if (mode == kActSwiGLU) return rows_kernel_ptr_t<B, SPL, false, kActSwiGLU>(tail);
         }
         if (mode == kActNorm) return rows_kernel_ptr_t<B, SPL, false, kActNorm>(tail);
         if (mode == kActF32) return rows_kernel_ptr_t<B, SPL, false, kActF32>(tail);
@@ -658,13 +685,21 @@ cudaError_t launch_rows(GemvArgs a, cudaStream_t stream, bool pdl, int sms, int 
     constexpr int NCW = kRowNCW;
     int kw = 1, spl = 1;
     if (!row_split(a.K, B, &kw, &spl)) {  // K too long for register-resident activations: tensor-core kernel
-        if (a.act.mode == kActNorm || a.act.mode == kActNormPeer) return cudaErrorNotSupported;
+        if (a.act.mode == kActNorm || a.act.mode == kActNormPeer || a.act.mode == kActSwiGLU)
+            return cudaErrorNotSupported;
         return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.partials, a.partial_bytes, a.K, a.N,
                                B, stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
     }
     if (a.act.mode == kActF32 && a.K > kRowFusedMaxK) {
         // every CTA would quantise all of K: the standalone quantizer (programmatic launch) is cheaper
         cudaError_t eq = launch_q8_1_quantize(a.act.x, const_cast<uint8_t*>(a.q8), a.K, B, a.K, 1, stream, true, pdl);
+        if (eq != cudaSuccess) return eq;
+        a.act.mode = kActQ8;
+        pdl = true;
+    }
+    if (a.act.mode == kActSwiGLU && (B != 1 || a.K > kRowFusedMaxK)) {
+        // the same policy for the SwiGLU source: the standalone SwiGLU kernel writes the Q8_1 blocks
+        cudaError_t eq = launch_swiglu_q8(a.act.x, a.K, 1, const_cast<uint8_t*>(a.q8), stream, pdl);
         if (eq != cudaSuccess) return eq;
         a.act.mode = kActQ8;
         pdl = true;
@@ -734,7 +769,7 @@ cudaError_t dispatch(int B, GemvArgs a, cudaStream_t stream, bool pdl) {
         }
     }
     if (B == 1) return launch_rows<1, kDebug>(a, stream, pdl, sms, smem_optin);
-    if (a.act.mode == kActNorm || a.act.mode == kActNormPeer) return cudaErrorNotSupported;
+    if (a.act.mode == kActNorm || a.act.mode == kActNormPeer || a.act.mode == kActSwiGLU) return cudaErrorNotSupported;
     return launch_gemv_mma(a.W, a.q8, a.y, kDebug ? a.sumi : nullptr, a.partials, a.partial_bytes, a.K, a.N, B,
                            stream, pdl, sms, smem_optin, a.err, a.lut, &a.act);
 }

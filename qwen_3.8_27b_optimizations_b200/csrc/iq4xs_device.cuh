@@ -35,6 +35,7 @@ enum DeviceError : uint32_t {
     kDevErrMmaWait = 4,     // tensor-core pipeline barrier timed out
     kDevErrPosition = 5,    // decode attention: the device-side position is outside the KV cache
     kDevErrPeerWait = 6,    // peer collective: a peer's flag did not arrive within the spin limit
+    kDevErrToken = 7,       // decode embedding: the device-side token id is outside the vocabulary
 };
 
 // Spin limit for every mbarrier wait (each try_wait already suspends for a while in hardware);

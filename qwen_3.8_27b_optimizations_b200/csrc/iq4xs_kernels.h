@@ -17,6 +17,7 @@ enum ActMode : int {
     kActF32 = 1,   // x: fp32 [B][K]
     kActNorm = 2,  // batch 1: h = rmsnorm(x + delta) * w, from fp32 x [K] (+ delta [K]), weight w [K]
     kActNormPeer = 3,  // kActNorm with delta = the fused all-reduce of `peer` (its own kernel instance)
+    kActSwiGLU = 4,    // batch 1: h = silu(gate) * up from fp32 x = gu [2K] (gate [0, K), up [K, 2K))
 };
 struct ActSource {
     int mode;
@@ -164,5 +165,8 @@ cudaError_t launch_attention_decode_q8(const float* qkv, __half* kc, __half* vc,
                                        const float* sinb, const int64_t* pos, int hq, int hkv, int max_seq,
                                        uint8_t* q8, float* o_out, uint32_t* err, cudaStream_t stream, bool pdl);
 cudaError_t launch_swiglu_q8(const float* gu, int64_t F, int64_t T, uint8_t* q8, cudaStream_t stream, bool pdl);
+cudaError_t launch_embed_f16(const __half* emb, const int64_t* tok, int64_t vocab, int64_t D, float* x,
+                             cudaStream_t stream, bool pdl);
+cudaError_t launch_argmax(const float* v, int64_t n, int64_t* tok, int64_t* pos, cudaStream_t stream, bool pdl);
 
 }  // namespace iq4xs

@@ -261,13 +261,17 @@ class TPDecoder:
 
     def forward_decode(self, x):
         """One token through the fused decode layers: x [1][hidden] fp32 embedding at position
-        self._pos; returns the final-norm hidden state [1][hidden] (a reused buffer)."""
+        self._pos, or None to embed the token in self._tok on the device; returns the final-norm
+        hidden state [1][hidden] (a reused buffer)."""
         api, cfg = self._api, self.cfg
         b = self._decode_buffers()
         D, hd = cfg.hidden, cfg.head_dim
         OV, PDL = api.FLAG_OVERLAP_PRECEDING, api.FLAG_PDL
         cur, nxt = b["x"], b["x2"]  # the residual stream: the fused GEMVs write x + delta to the other one
-        cur.copy_(x)
+        if x is None:
+            api.dec_embed(self.emb, self._tok, out=cur, flags=PDL)
+        else:
+            cur.copy_(x)
         delta = None
 
         def norm_gemv(W, w, N, out):
@@ -286,8 +290,11 @@ class TPDecoder:
                                         self.hq, self.hkv, q8=b["q8a"], flags=PDL)
             delta = self._reduce_gemv(L["wo"], b["q8a"], self.hq * hd, b["o"], 0, L.get("wo_parts"))
             norm_gemv(L["wgu"], L["fn"], 2 * self.F, b["gu"])
-            api.dec_swiglu_q8(b["gu"], self.F, q8=b["q8f"], flags=PDL)
-            delta = self._reduce_gemv(L["wd"], b["q8f"], self.F, b["d"], 1, L.get("wd_parts"))
+            if "wd_parts" in L:
+                api.dec_swiglu_q8(b["gu"], self.F, q8=b["q8f"], flags=PDL)
+                delta = self._reduce_gemv(L["wd"], b["q8f"], self.F, b["d"], 1, L["wd_parts"])
+            else:
+                delta = self._swiglu_down(L["wd"], b["gu"], b["d"])
         if isinstance(delta, _PeerDelta):
             api.dec_residual_rmsnorm_q8_peer(cur, delta.slots, self.final_norm, cfg.eps, h_out=b["h"], want_q8=False,
                                              flags=PDL)
@@ -321,6 +328,21 @@ class TPDecoder:
             return _PeerDelta(slots)
         api.gemv_q8_ex(W, q8, K, D, 1, out=self.peers.area(area, D).view(1, D), flags=api.FLAG_OVERLAP_PRECEDING)
         self.peers.allreduce(area, D, out)
+        return out
+
+    def _swiglu_down(self, W, gu, out):
+        """The down_proj GEMV with the SwiGLU fused in (iq4xs_dec_swiglu_gemv: the Q8_1 blocks of
+        silu(gate) * up are built by the GEMV's CTAs, or by the standalone SwiGLU kernel for long K),
+        then the all-reduce as in _reduce_gemv."""
+        api, D = self._api, self.cfg.hidden
+        if self.peers is None:
+            return self._allreduce(api.dec_swiglu_gemv(W, gu, self.F, D, out=out, flags=api.FLAG_PDL))
+        if self.fused_allreduce:
+            slots = self.peers.slots(1, D)
+            api.dec_swiglu_gemv(W, gu, self.F, D, slots=slots, flags=api.FLAG_PDL)
+            return _PeerDelta(slots)
+        api.dec_swiglu_gemv(W, gu, self.F, D, out=self.peers.area(1, D).view(1, D), flags=api.FLAG_PDL)
+        self.peers.allreduce(1, D, out)
         return out
 
     def _emu_buffers(self, n):
@@ -362,9 +384,18 @@ class TPDecoder:
         return self._tok.clone(), lg
 
     def _step(self):
+        """One decode step: the token in self._tok at position self._pos -> the next token (greedy) in
+        self._tok, the position advanced.  self._last_logits: the step's logits [1][vocab] (with the
+        CUDA kernels a view of the lm_head's output buffer, valid until the next step)."""
         torch = self.torch
+        if self.fused_decode:
+            h = self.forward_decode(None)  # embeds self._tok itself
+            lg = self.logits(h)
+            self._last_logits = lg
+            self._api.dec_argmax(lg, self._tok, self._pos, flags=self._api.FLAG_PDL)
+            return self._tok
         x = self.emb[self._tok].float()
-        h = self.forward_decode(x) if self.fused_decode else self.forward(x, self._pos)
+        h = self.forward(x, self._pos)
         lg = self.logits(h)
         self._last_logits = lg.clone()
         self._tok.copy_(torch.argmax(lg, dim=-1))

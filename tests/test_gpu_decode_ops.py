@@ -168,3 +168,57 @@ def test_rmsnorm_gemv_rejects_aliased_output(pkg):
     w = torch.ones(K, device="cuda")
     with pytest.raises(pkg.IQ4XSError):
         pkg.api.dec_rmsnorm_gemv(W, x, w, 1e-6, N, delta=x.clone(), x_out=x)
+
+
+def test_embed(pkg):
+    vocab, D = 1000, 5120
+    g = _gen(7)
+    emb = (0.02 * torch.randn((vocab, D), generator=g, device="cuda")).half()
+    for t in (0, 1, 517, vocab - 1):
+        tok = torch.tensor([t], dtype=torch.long, device="cuda")
+        x = pkg.api.dec_embed(emb, tok)
+        torch.cuda.synchronize()
+        assert torch.equal(x, emb[tok].float())
+    assert pkg.device_error() == 0
+
+
+@pytest.mark.parametrize("n", [152064, 76032, 19008, 1, 4097])
+def test_argmax_matches_torch(pkg, n):
+    g = _gen(11 + n)
+    cases = [torch.randn(n, generator=g, device="cuda")]
+    tied = torch.randn(n, generator=g, device="cuda").clamp(max=1.5)  # many copies of the maximum
+    cases.append(tied)
+    if n > 3:
+        with_nan = torch.randn(n, generator=g, device="cuda")
+        with_nan[n // 3] = float("nan")
+        with_nan[n - 1] = float("nan")
+        cases.append(with_nan)
+        neg = -torch.rand(n, generator=g, device="cuda") - 1.0
+        neg[n - 2] = float("-inf")
+        cases.append(neg)
+    for v in cases:
+        tok = torch.zeros(1, dtype=torch.long, device="cuda")
+        pos = torch.tensor([41], dtype=torch.long, device="cuda")
+        pkg.api.dec_argmax(v.view(1, n), tok, pos)
+        torch.cuda.synchronize()
+        assert int(tok) == int(torch.argmax(v)), (n, int(tok), int(torch.argmax(v)))
+        assert int(pos) == 42
+    tok = torch.zeros(1, dtype=torch.long, device="cuda")
+    pkg.api.dec_argmax(cases[0], tok)  # no position
+    torch.cuda.synchronize()
+    assert int(tok) == int(torch.argmax(cases[0]))
+
+
+@pytest.mark.parametrize("F,N", [(2560, 5120), (4608, 5120), (6144, 1000), (8704, 5120), (17408, 5120)])
+def test_swiglu_gemv_matches_separate_kernels(pkg, F, N):
+    # SwiGLU inside the down_proj GEMV (every CTA builds the Q8_1 blocks for F <= 6144, the standalone
+    # SwiGLU kernel into the workspace beyond) gives the bits of swiglu_q8 followed by the Q8_1 GEMV
+    g = _gen(300 + F)
+    W = pkg.random_weights(N, F, seed=700 + F)
+    gu = torch.randn((1, 2 * F), generator=g, device="cuda") * 2.0
+    q8 = pkg.api.dec_swiglu_q8(gu, F)
+    y_ref = pkg.gemv_q8(W, q8, F, N, 1)
+    y = pkg.api.dec_swiglu_gemv(W, gu, F, N)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
+    assert pkg.device_error() == 0
