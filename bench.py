@@ -327,6 +327,7 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
         m.graph = None
         m.prefill(prompt)
         m.decode(4)                  # re-capture
+        m.prefill(prompt)            # back to position 512: 128 steps fill the 640-slot cache exactly
         barrier()
         ev[0].record()
         m.decode(DECODER_STEPS)
@@ -652,10 +653,18 @@ def run_case(argv) -> int:
       --case sweep                                        one benchmark sweep step, eager launches
       --case grouped --B 8                                one grouped call over the six layer shapes
       --case gsweep                                       one benchmark step (a grouped call per batch), eager
+      --case decode --tp 8 --layers 4 [--graph]           decode steps of the C5 decoder with one rank's
+                                                          shapes at TP 1/2/4/8 on this GPU alone (no
+                                                          communication): eager (for a launch list), or
+                                                          --graph: ms per token of the captured step
     The default N (twice the gate|up projection) keeps the weights above the 126 MB L2."""
     import torch
     ap = argparse.ArgumentParser(prog="bench.py --case")
-    ap.add_argument("--case", required=True, choices=["gemv", "gemm", "attention", "sweep", "grouped", "gsweep"])
+    ap.add_argument("--case", required=True,
+                    choices=["gemv", "gemm", "attention", "sweep", "grouped", "gsweep", "decode"])
+    ap.add_argument("--tp", type=int, default=1, choices=[1, 2, 4, 8])
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--graph", action="store_true")
     ap.add_argument("--N", type=int, default=69632)
     ap.add_argument("--K", type=int, default=5120)
     ap.add_argument("--B", type=int, default=1)
@@ -697,6 +706,32 @@ def run_case(argv) -> int:
         us = timed(lambda: P.dec_attention_decode_q8(qkv, kc, vc, cos, sin, p, hq, hkv, q8=q8), a.launches, a.warmup)
         print(json.dumps({"case": "attention", "pos": a.pos, "us_per_launch": round(us, 2),
                           "kv_bytes": 2 * hkv * (a.pos + 1) * hd * 2}))
+        return 0
+    if a.case == "decode":
+        # one rank's share of the C5 model at TP tp: tp-th of the heads, the largest rank's FFN pairs,
+        # a vocab/tp lm_head shard; the same kernels and shapes a TP rank runs, without its exchanges
+        tp = a.tp
+        cfg = P.decoder.DecoderConfig(layers=a.layers, heads=64 // tp, kv_heads=max(1, 8 // tp),
+                                      ffn=512 * (-(-34 // tp)), vocab=152064 // tp)
+        m = P.decoder.TPDecoder(cfg, rank=0, world=1, seed=1)
+        prompt = torch.randint(0, cfg.vocab, (16,), generator=torch.Generator().manual_seed(7)).to("cuda")
+        m.prefill(prompt)
+        torch.cuda.synchronize()
+        res = {"case": "decode", "tp_shapes": tp, "layers": a.layers}
+        if a.graph:
+            m.decode(4)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            m.decode(64)
+            e1.record()
+            torch.cuda.synchronize()
+            res["ms_per_token"] = round(e0.elapsed_time(e1) / 64, 4)
+        else:
+            res["tokens"] = m.decode(max(a.launches, 1), use_graph=False)
+        if P.device_error():
+            raise RuntimeError(f"device error word {P.device_error()}")
+        m.release()
+        print(json.dumps(res))
         return 0
     if a.case == "sweep":
         Ws = [P.random_weights(N, K, seed=i) for i, (_, N, K) in enumerate(SHAPES)]
