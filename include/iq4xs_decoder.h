@@ -26,6 +26,11 @@ extern "C" {
 #endif
 
 #define IQ4XS_FLAG_PDL 1u
+/* iq4xs_dec_attention_decode_q8 with IQ4XS_FLAG_PDL: the position, the cache rows before it and the
+ * RoPE tables are not written by the preceding kernel (only qkv is), so the kernel reads them, and
+ * requests the K/V rows, before it waits for that kernel.  A decode step qualifies when the position
+ * and the cache were last written by earlier tokens' kernels. */
+#define IQ4XS_FLAG_ATTN_EARLY_STATE 2u
 
 /* For each of the T rows of x [T][D] (fp32, D % 32 == 0, D <= 8192):
  *   if delta: x += delta (written back; delta [T][D] is e.g. the all-reduced o_proj output)

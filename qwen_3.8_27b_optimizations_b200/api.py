@@ -444,6 +444,7 @@ def custom_gemm_iq4xs_dispatch(W, X, Y, K: int, N: int, M: int, stream=None) -> 
 
 # ----------------------------------------------------------------------------- decoder step (iq4xs_decoder.h)
 FLAG_PDL = 1
+FLAG_ATTN_EARLY_STATE = 2  # attention: position, cache and RoPE tables not written by the preceding kernel
 
 
 def _q8_out(rows: int, D: int, device, out):

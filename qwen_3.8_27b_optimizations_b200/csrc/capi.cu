@@ -503,7 +503,8 @@ int iq4xs_dec_attention_decode_q8(const float* qkv, void* k_cache, void* v_cache
     return status_from(launch_attention_decode_q8(qkv, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache),
                                                   cos_table, sin_table, pos, (int)q_heads, (int)kv_heads,
                                                   (int)max_seq, static_cast<uint8_t*>(q8), o_out, err, stream,
-                                                  (flags & IQ4XS_FLAG_PDL) != 0));
+                                                  (flags & IQ4XS_FLAG_PDL) != 0,
+                                                  (flags & IQ4XS_FLAG_ATTN_EARLY_STATE) != 0));
 }
 
 int iq4xs_dec_rmsnorm_gemv(const void* W, const float* x, const float* delta, const float* w, float eps, float* x_out,

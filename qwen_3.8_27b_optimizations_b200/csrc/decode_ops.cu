@@ -155,10 +155,13 @@ template <int G>
 __global__ void __cluster_dims__(kChunks, 1, 1) __launch_bounds__(kAttnThreads, 1) attention_decode_q8_kernel(
     const float* __restrict__ qkv, __half* __restrict__ kc, __half* __restrict__ vc,
     const float* __restrict__ cosb, const float* __restrict__ sinb, const int64_t* __restrict__ pos_p, int hq,
-    int hkv, int max_seq, int lmax, uint8_t* __restrict__ q8, float* __restrict__ o_out, uint32_t* err) {
+    int hkv, int max_seq, int lmax, uint8_t* __restrict__ q8, float* __restrict__ o_out, uint32_t* err,
+    bool early_state) {
     namespace cg = cooperative_groups;
     grid_launch_dependents();
-    grid_dependency_wait();
+    // early_state: the position, the cache rows before it and the RoPE tables are not written by the
+    // preceding kernel, so they are read (and the K/V rows requested) before waiting for it; only qkv is
+    if (!early_state) grid_dependency_wait();
     extern __shared__ __align__(16) float dyn[];
     float* sc = dyn;                                   // [G][lmax] scores, then exp(s - m_c)
     float* stage = dyn + G * lmax;                     // [kAttnWarps][G][128] per-warp partial outputs
@@ -194,6 +197,7 @@ __global__ void __cluster_dims__(kChunks, 1, 1) __launch_bounds__(kAttnThreads, 
             vraw[u] = *reinterpret_cast<const uint2*>(vbase + (int64_t)t * kHeadDim);
         }
     }
+    if (early_state) grid_dependency_wait();  // qkv comes from the preceding kernel
     // RoPE (rotate-half) of the group's q heads and the new k; the new k and v rounded to f16
     for (int it = tid; it < G * kHalf + kHalf + kHeadDim; it += kAttnThreads) {
         if (it < G * kHalf) {
@@ -551,7 +555,7 @@ size_t attention_decode_smem(int max_seq, int g) {
 template <int G>
 cudaError_t launch_attention_g(const float* qkv, __half* kc, __half* vc, const float* cosb, const float* sinb,
                                const int64_t* pos, int hq, int hkv, int max_seq, uint8_t* q8, float* o_out,
-                               uint32_t* err, cudaStream_t stream, bool pdl) {
+                               uint32_t* err, cudaStream_t stream, bool pdl, bool early_state) {
     const size_t smem = attention_decode_smem(max_seq, G);
     if (smem > 48 * 1024) {
         cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(attention_decode_q8_kernel<G>), (int)smem);
@@ -560,17 +564,18 @@ cudaError_t launch_attention_g(const float* qkv, __half* kc, __half* vc, const f
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = launch_cfg(dim3(kChunks, (unsigned)hkv), dim3(kAttnThreads), smem, stream, pdl, attr);
     return cudaLaunchKernelEx(&cfg, attention_decode_q8_kernel<G>, qkv, kc, vc, cosb, sinb, pos, hq, hkv, max_seq,
-                              attention_lmax(max_seq), q8, o_out, err);
+                              attention_lmax(max_seq), q8, o_out, err, early_state && pdl);
 }
 
 cudaError_t launch_attention_decode_q8(const float* qkv, __half* kc, __half* vc, const float* cosb,
                                        const float* sinb, const int64_t* pos, int hq, int hkv, int max_seq,
-                                       uint8_t* q8, float* o_out, uint32_t* err, cudaStream_t stream, bool pdl) {
+                                       uint8_t* q8, float* o_out, uint32_t* err, cudaStream_t stream, bool pdl,
+                                       bool early_state) {
     switch (hq / hkv) {
-        case 1: return launch_attention_g<1>(qkv, kc, vc, cosb, sinb, pos, hq, hkv, max_seq, q8, o_out, err, stream, pdl);
-        case 2: return launch_attention_g<2>(qkv, kc, vc, cosb, sinb, pos, hq, hkv, max_seq, q8, o_out, err, stream, pdl);
-        case 4: return launch_attention_g<4>(qkv, kc, vc, cosb, sinb, pos, hq, hkv, max_seq, q8, o_out, err, stream, pdl);
-        case 8: return launch_attention_g<8>(qkv, kc, vc, cosb, sinb, pos, hq, hkv, max_seq, q8, o_out, err, stream, pdl);
+        case 1: return launch_attention_g<1>(qkv, kc, vc, cosb, sinb, pos, hq, hkv, max_seq, q8, o_out, err, stream, pdl, early_state);
+        case 2: return launch_attention_g<2>(qkv, kc, vc, cosb, sinb, pos, hq, hkv, max_seq, q8, o_out, err, stream, pdl, early_state);
+        case 4: return launch_attention_g<4>(qkv, kc, vc, cosb, sinb, pos, hq, hkv, max_seq, q8, o_out, err, stream, pdl, early_state);
+        case 8: return launch_attention_g<8>(qkv, kc, vc, cosb, sinb, pos, hq, hkv, max_seq, q8, o_out, err, stream, pdl, early_state);
         default: return cudaErrorInvalidValue;
     }
 }

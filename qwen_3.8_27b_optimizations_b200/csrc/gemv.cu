@@ -83,6 +83,15 @@ __host__ __device__ inline RowSmem gemv_row_smem(int B, int R, int KW, int stage
     return L;
 }
 
+// Shared memory of an activation source: the Q8_1 blocks [B][K/32] (every source but kActQ8), then
+// for kActNormPeer the all-reduced delta [K] fp32 (16-byte aligned).
+__host__ __device__ inline uint32_t act_q8_bytes(int B, int K) { return (uint32_t)(B * (K / kQK8) * kQ8Bytes); }
+__host__ __device__ inline uint32_t act_smem_bytes(int mode, int B, int K) {
+    if (mode == kActQ8) return 0u;
+    const uint32_t q8 = act_q8_bytes(B, K);
+    return mode == kActNormPeer ? ((q8 + 15u) & ~15u) + (uint32_t)K * 4u : q8;
+}
+
 // Consumer warps (warp index cw of ncw) build the Q8_1 activations of an fp32 source in shared
 // memory, four blocks (128 values, one float4 per lane) at a time with q8_1_quad_store; each warp
 // issues the loads of a batch of quads (kActQ / kActQF) before using any (one round trip per batch).
@@ -110,9 +119,17 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
         // each word read until it carries the current epoch)
         constexpr bool kPeer = kAct == kActNormPeer;
         const bool has_delta = kPeer || act.delta != nullptr;
-        const uint32_t ep = kPeer ? peer_slots_epoch(act.peer) : 0u;
-        // delta of the batch's quads; the slots' words are loaded for half the batch at a time (all
-        // of a half's loads in flight together; the whole batch at once would spill registers)
+        // kPeer: the all-reduced delta of this warp's quads is summed first into shared memory (after
+        // the Q8_1 blocks), with up to eight (quad, rank) slot reads in flight at a time; the warp
+        // reads back only its own quads
+        float* dsm = reinterpret_cast<float*>(q8s + ((act_q8_bytes(B, K) + 15u) & ~15u));
+        if constexpr (kPeer) {
+            const uint32_t ep = peer_slots_epoch(act.peer);
+            peer_slots_sum_to_smem(act.peer, K, nq, cw, ncw, lane, ep, err, dsm);
+            __syncwarp();
+        }
+        // delta of the batch's quads (global memory, or the peer pre-pass's shared memory), in halves
+        // of the batch
         auto delta_batch = [&](int base, float4(&da)[kActQ]) {
             constexpr int H = kActQ / 2;
 #pragma unroll
@@ -128,7 +145,9 @@ __device__ __forceinline__ void build_act_q8(const ActSource& act, int B, int K,
                     d[i] = zero4;
                 }
                 if constexpr (kPeer) {
-                    peer_slots_sum4_batch<H>(act.peer, K, off, ok, ep, err, d);
+#pragma unroll
+                    for (int i = 0; i < H; ++i)
+                        if (ok[i]) d[i] = *reinterpret_cast<const float4*>(dsm + off[i]);
                 } else {
 #pragma unroll
                     for (int i = 0; i < H; ++i)
@@ -277,8 +296,7 @@ __device__ __forceinline__ void gemv_rows_body(const GemvArgs& a, int cta, int n
     const int stages = a.stages;
     const int64_t stage_bytes = (int64_t)R * a.rb;
     constexpr bool smem_act = kAct != kActQ8;
-    const RowSmem L = gemv_row_smem(B, R, KW, stages, stage_bytes,
-                                    smem_act ? (uint32_t)(B * (a.K / kQK8) * kQ8Bytes) : 0u);
+    const RowSmem L = gemv_row_smem(B, R, KW, stages, stage_bytes, act_smem_bytes(kAct, B, a.K));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     uint64_t* empty = full + kMaxStages;
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L.abort_off);
@@ -666,7 +684,7 @@ cudaError_t row_geometry(GemvArgs& a, int B, int smem_optin, int* spl_out, bool*
     // At most ~110 KB of stages (two of them always): deeper rings did not stream faster, and a CTA
     // that leaves half the shared memory free lets the next kernel's CTA start on the same SM.
     constexpr int64_t kRowSmemTarget = 110000;
-    const uint32_t q8b = a.act.mode != kActQ8 ? (uint32_t)(B * nsb * kQ8Bytes) : 0u;
+    const uint32_t q8b = act_smem_bytes(a.act.mode, B, a.K);
     int stages = kMaxStages;
     while (stages > 2 && ((int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes, q8b).total > smem_optin ||
                           (int64_t)gemv_row_smem(B, R, kw, stages, stage_bytes, q8b).total > kRowSmemTarget + q8b))

@@ -370,42 +370,51 @@ __device__ __forceinline__ void ld_relaxed_sys_v2u64(const uint64_t* p, uint64_t
     asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-// Consumer, batched: s[j] = delta[off[j] .. off[j]+3] for the NQ quads with ok[j] (off[j] % 4 == 0).
-// For each slot, in rank order, the words of all NQ quads are loaded before any tag is checked, so
-// a slot whose words are all current costs one round trip; a stale word is then polled on its own
-// (bounded, peer_slot_value).  Each 8-byte word of a vector load is a single-copy-atomic access.
-template <int NQ>
-__device__ __forceinline__ void peer_slots_sum4_batch(const iq4xs_peer_slots* p, int64_t n, const int (&off)[NQ],
-                                                      const bool (&ok)[NQ], uint32_t e, uint32_t* err,
-                                                      float4 (&s)[NQ]) {
-    const int world = p->world;
-    for (int q = 0; q < world && q < IQ4XS_MAX_PEERS; ++q) {
-        const uint64_t* base = p->local + (int64_t)q * n;
-        uint64_t w[NQ][4];
+// Consumer, one warp: dsm[i] = delta[i] (the ranks' values added in rank order) for every i in this
+// warp's quads qd = cw, cw + ncw, ... < nq (128 values each, 4 per lane).  (quad, rank) pairs go eight
+// at a time: every word of a round is loaded before any tag is checked, so a round whose tags are all
+// current costs one round trip (1, 2 or 4 rounds for this warp's four quads at 2, 4 or 8 ranks); a
+// stale word is then polled on its own (bounded, peer_slot_value).  Each 8-byte word of a vector load
+// is a single-copy-atomic access.
+__device__ __forceinline__ void peer_slots_sum_to_smem(const iq4xs_peer_slots* p, int64_t n, int nq, int cw, int ncw,
+                                                       int lane, uint32_t e, uint32_t* err, float* dsm) {
+    constexpr int kRound = 8;
+    const int world = p->world < kRound ? (p->world > 0 ? p->world : 1) : kRound;
+    const int qpr = kRound / world;  // quads per round
+    for (int first = cw; first < nq; first += ncw * qpr) {
+        uint64_t w[kRound][4];
 #pragma unroll
-        for (int j = 0; j < NQ; ++j) {
-            w[j][0] = w[j][1] = w[j][2] = w[j][3] = (uint64_t)e << 32;
-            if (ok[j]) {
-                ld_relaxed_sys_v2u64(base + off[j], w[j][0], w[j][1]);
-                ld_relaxed_sys_v2u64(base + off[j] + 2, w[j][2], w[j][3]);
+        for (int u = 0; u < kRound; ++u) {
+            const int j = u / world, q = u - j * world;
+            const int qd = first + j * ncw;
+            if (j < qpr && qd < nq) {
+                const uint64_t* a = p->local + (int64_t)q * n + qd * 128 + 4 * lane;
+                ld_relaxed_sys_v2u64(a, w[u][0], w[u][1]);
+                ld_relaxed_sys_v2u64(a + 2, w[u][2], w[u][3]);
             }
         }
+        float4 cur = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int j = 0; j < NQ; ++j) {
+        for (int u = 0; u < kRound; ++u) {
+            const int j = u / world, q = u - j * world;
+            const int qd = first + j * ncw;
+            if (j >= qpr || qd >= nq) continue;
+            const int off = qd * 128 + 4 * lane;
             float v[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                v[k] = (uint32_t)(w[j][k] >> 32) == e ? __uint_as_float((uint32_t)w[j][k])
-                                                      : peer_slot_value(p, q, n, off[j] + k, e, err);
+                v[k] = (uint32_t)(w[u][k] >> 32) == e ? __uint_as_float((uint32_t)w[u][k])
+                                                      : peer_slot_value(p, q, n, off + k, e, err);
             }
             if (q == 0) {
-                s[j] = make_float4(v[0], v[1], v[2], v[3]);
+                cur = make_float4(v[0], v[1], v[2], v[3]);
             } else {
-                s[j].x = __fadd_rn(s[j].x, v[0]);
-                s[j].y = __fadd_rn(s[j].y, v[1]);
-                s[j].z = __fadd_rn(s[j].z, v[2]);
-                s[j].w = __fadd_rn(s[j].w, v[3]);
+                cur.x = __fadd_rn(cur.x, v[0]);
+                cur.y = __fadd_rn(cur.y, v[1]);
+                cur.z = __fadd_rn(cur.z, v[2]);
+                cur.w = __fadd_rn(cur.w, v[3]);
             }
+            if (q == world - 1) *reinterpret_cast<float4*>(dsm + off) = cur;
         }
     }
 }

@@ -163,7 +163,8 @@ cudaError_t launch_residual_rmsnorm_q8(float* x, const float* delta, const float
                                        const iq4xs_peer_slots* peer = nullptr);
 cudaError_t launch_attention_decode_q8(const float* qkv, __half* kc, __half* vc, const float* cosb,
                                        const float* sinb, const int64_t* pos, int hq, int hkv, int max_seq,
-                                       uint8_t* q8, float* o_out, uint32_t* err, cudaStream_t stream, bool pdl);
+                                       uint8_t* q8, float* o_out, uint32_t* err, cudaStream_t stream, bool pdl,
+                                       bool early_state = false);
 cudaError_t launch_swiglu_q8(const float* gu, int64_t F, int64_t T, uint8_t* q8, cudaStream_t stream, bool pdl);
 cudaError_t launch_embed_f16(const __half* emb, const int64_t* tok, int64_t vocab, int64_t D, float* x,
                              cudaStream_t stream, bool pdl);

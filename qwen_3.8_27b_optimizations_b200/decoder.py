@@ -286,8 +286,9 @@ class TPDecoder:
 
         for l, L in enumerate(self.layers):
             norm_gemv(L["wqkv"], L["an"], self.nqkv, b["qkv"])
+            # the position and the cache rows before it were written by earlier tokens' kernels
             api.dec_attention_decode_q8(b["qkv"], self.cache[l, 0], self.cache[l, 1], self.cos, self.sin, self._pos,
-                                        self.hq, self.hkv, q8=b["q8a"], flags=PDL)
+                                        self.hq, self.hkv, q8=b["q8a"], flags=PDL | api.FLAG_ATTN_EARLY_STATE)
             delta = self._reduce_gemv(L["wo"], b["q8a"], self.hq * hd, b["o"], 0, L.get("wo_parts"))
             norm_gemv(L["wgu"], L["fn"], 2 * self.F, b["gu"])
             if "wd_parts" in L:

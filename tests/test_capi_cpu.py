@@ -75,6 +75,22 @@ def test_decoder_op_validation(pkg):
     assert L.iq4xs_dec_rmsnorm_gemv(FAKE + 4, FAKE, None, FAKE, 1e-6, None, FAKE, 5120, 64, FAKE, 1 << 30, 0, None) == 3
     # gemv_q8_ex shares gemv_q8's checks
     assert L.iq4xs_gemv_q8_ex(FAKE, FAKE, FAKE, 500, 64, 1, FAKE, 1 << 30, 1, None) == 2
+    # embedding: D % 8, null token, misaligned table
+    assert L.iq4xs_dec_embed(FAKE, FAKE, 1000, 100, FAKE, 0, None) == 2
+    assert L.iq4xs_dec_embed(FAKE, None, 1000, 128, FAKE, 0, None) == 1
+    assert L.iq4xs_dec_embed(FAKE + 8, FAKE, 1000, 128, FAKE, 0, None) == 3
+    # argmax: empty input, null token, misaligned position
+    assert L.iq4xs_dec_argmax(FAKE, 0, FAKE, None, 0, None) == 1
+    assert L.iq4xs_dec_argmax(FAKE, 100, None, None, 0, None) == 1
+    assert L.iq4xs_dec_argmax(FAKE, 100, FAKE, FAKE + 4, 0, None) == 3
+    # SwiGLU GEMV: K % 256, no output, workspace too small, misaligned gu, K past the row kernel
+    need = L.iq4xs_gemv_workspace_bytes(5120, 64, 1)
+    assert L.iq4xs_dec_swiglu_gemv(FAKE, FAKE, 500, 64, FAKE, FAKE, 1 << 30, 0, None) == 2
+    assert L.iq4xs_dec_swiglu_gemv(FAKE, FAKE, 5120, 64, None, FAKE, 1 << 30, 0, None) == 1
+    assert L.iq4xs_dec_swiglu_gemv(FAKE, FAKE, 5120, 64, FAKE, FAKE, need - 1, 0, None) == 4
+    assert L.iq4xs_dec_swiglu_gemv(FAKE, FAKE + 4, 5120, 64, FAKE, FAKE, 1 << 30, 0, None) == 3
+    assert L.iq4xs_dec_swiglu_gemv(FAKE, FAKE, 25600, 64, FAKE, FAKE, 1 << 30, 0, None) == 7
+    assert L.iq4xs_dec_swiglu_gemv_push(FAKE, FAKE, 5120, 64, None, FAKE, 1 << 30, 0, None) == 1
 
 
 def test_status_strings(pkg):

@@ -222,3 +222,28 @@ def test_swiglu_gemv_matches_separate_kernels(pkg, F, N):
     torch.cuda.synchronize()
     assert torch.equal(y, y_ref)
     assert pkg.device_error() == 0
+
+
+@pytest.mark.parametrize("hq,hkv,p", [(64, 8, 512), (8, 1, 77)])
+def test_attention_early_state_same_bits(pkg, hq, hkv, p):
+    # IQ4XS_FLAG_ATTN_EARLY_STATE (position, cache and RoPE tables read before waiting for the
+    # preceding kernel, as a programmatic dependent): the same cache and outputs as the plain launch
+    hd, max_seq = 128, 640
+    g = _gen(500 + p)
+    qkv = torch.randn((1, (hq + 2 * hkv) * hd), generator=g, device="cuda")
+    kc = torch.randn((hkv, max_seq, hd), generator=g, device="cuda").half()
+    vc = torch.randn((hkv, max_seq, hd), generator=g, device="cuda").half()
+    cos = torch.randn((max_seq, hd // 2), generator=g, device="cuda")
+    sin = torch.randn((max_seq, hd // 2), generator=g, device="cuda")
+    pos = torch.tensor([p], dtype=torch.long, device="cuda")
+    outs = []
+    for flags in (0, pkg.api.FLAG_PDL | pkg.api.FLAG_ATTN_EARLY_STATE):
+        k1, v1 = kc.clone(), vc.clone()
+        qkv2 = qkv * 1.0  # a kernel right before the launch (its programmatic predecessor)
+        o = torch.empty((hq * hd,), dtype=torch.float32, device="cuda")
+        q8 = pkg.api.dec_attention_decode_q8(qkv2, k1, v1, cos, sin, pos, hq, hkv, o_out=o, flags=flags)
+        torch.cuda.synchronize()
+        outs.append((k1, v1, o, q8))
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a, b)
+    assert pkg.device_error() == 0
