@@ -54,7 +54,10 @@ const char* iq4xs_status_string(int status);
 int iq4xs_version(void); /* major*10000 + minor*100 + patch */
 
 /* Reads the current device's error word set by bounded device waits and clears it.
- * *code = 0 when no kernel gave up since the last call.  The read and the clear are two
+ * *code = 0 when no kernel gave up since the last call; otherwise the first code recorded:
+ * 1-4 a copy or tensor-core pipeline wait gave up, 5 a decode position outside the KV cache,
+ * 6 a peer's data or flag did not arrive (multi-GPU), 7 a decode token id outside the vocabulary
+ * (iq4xs_decoder.h, iq4xs_peer.h).  The read and the clear are two
  * synchronous copies, not one atomic exchange: call it between steps, with no kernel of this
  * library running on the device, or an error recorded between the two copies is lost. */
 int iq4xs_device_error(uint32_t* code);

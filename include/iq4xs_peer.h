@@ -71,8 +71,9 @@ typedef struct iq4xs_peer_slots {
 } iq4xs_peer_slots;
 
 /* Y = W . q8 (batch 1, iq4xs_gemv_q8 arithmetic) into slot `rank` of every rank's area (`slots`, a
- * device pointer), then the signal.  The row kernel's K range (K % 512 == 0, K <= 24576, W 16-byte
- * aligned); otherwise IQ4XS_ERR_NOT_SUPPORTED.  flags: IQ4XS_FLAG_PDL. */
+ * device pointer), each output tagged with the all-reduce's epoch; the grid's last CTA advances this
+ * rank's epoch counter.  The row kernel's K range (K % 512 == 0, K <= 24576, W 16-byte aligned);
+ * otherwise IQ4XS_ERR_NOT_SUPPORTED.  flags: IQ4XS_FLAG_PDL. */
 int iq4xs_dec_gemv_q8_push(const void* W, const void* q8, int64_t K, int64_t N, const iq4xs_peer_slots* slots,
                            void* workspace, size_t workspace_bytes, unsigned flags, cudaStream_t stream);
 /* iq4xs_dec_swiglu_gemv with the outputs pushed into slot `rank` of every rank's area, as
