@@ -67,6 +67,14 @@ __host__ __device__ inline MmaSmem mma_smem(int pk, int stages) {
     return L;
 }
 
+// Staged activations of sub-block sb (counted over both part slots) in shared memory, by pairs of
+// sub-blocks: lane L's B-fragment words of sub-blocks 2m and 2m+1 are adjacent (one 16-byte load),
+// and so are the d_x of tokens 2c, 2c+1 of both (one 16-byte load for lane column c).
+__device__ __forceinline__ int act_index(int sb, int L) { return ((sb >> 1) * 32 + L) * 2 + (sb & 1); }  // uint2
+__device__ __forceinline__ int dx_index(int sb, int n) {                                                // float
+    return ((sb >> 1) * 4 + (n >> 1)) * 4 + (sb & 1) * 2 + (n & 1);
+}
+
 __device__ __forceinline__ void fence_proxy_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -249,8 +257,9 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
             const int bq = lane >> 2, j = lane & 3;
             const uint32_t* blk = scr + bq * (kQ8Bytes / 4);
             const int sbl = sbl0 + bq;
-            actw[(slot * pk * 16 + sbl) * 32 + n * 4 + j] = make_uint2(act_perm_lo(blk[1 + j], blk[5 + j]), act_perm_hi(blk[1 + j], blk[5 + j]));
-            if (j == 0) dxw[(slot * pk * 16 + sbl) * 8 + n] = f16_bits_to_f32(blk[0]);
+            actw[act_index(slot * pk * 16 + sbl, n * 4 + j)] =
+                make_uint2(act_perm_lo(blk[1 + j], blk[5 + j]), act_perm_hi(blk[1 + j], blk[5 + j]));
+            if (j == 0) dxw[dx_index(slot * pk * 16 + sbl, n)] = f16_bits_to_f32(blk[0]);
             __syncwarp();
         };
         if constexpr (kF32) {
@@ -314,10 +323,9 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
                 const int n = B + e % (8 - B), sbg = e / (8 - B);
                 const int slot = sbg < nsubs[0] ? 0 : 1;
                 const int sbl = sbg - slot * nsubs[0];
-                uint2* dst = actw + (slot * pk * 16 + sbl) * 32 + n * 4;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) dst[j] = make_uint2(0u, 0u);
-                dxw[(slot * pk * 16 + sbl) * 8 + n] = 0.0f;
+                for (int j = 0; j < 4; ++j) actw[act_index(slot * pk * 16 + sbl, n * 4 + j)] = make_uint2(0u, 0u);
+                dxw[dx_index(slot * pk * 16 + sbl, n)] = 0.0f;
             }
         }
     }
@@ -341,8 +349,7 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
         if (ready) {
             const uint8_t* rg = ring + (size_t)s * stage_bytes + (size_t)g * row_pitch;
             const uint8_t* rg8 = rg + 8 * row_pitch;
-            const uint2* actp = act + (size_t)slot * pk * 16 * 32 + lane;
-            const float* dxp = dxs + (size_t)slot * pk * 16 * 8 + 2 * c;
+            const int sbs = slot * pk * 16;  // this part's first staged sub-block (even)
             for (int j = hf; j < nsup; j += 2) {
                 const uint8_t* b0p = rg + j * kBlockBytes;
                 const uint8_t* b8p = rg8 + j * kBlockBytes;
@@ -351,6 +358,8 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
                 // Lane (g, c) computes the weight scale d*(ls-32) of rows g and g+8 for sub-blocks 2c
                 // and 2c+1; the sub-block loop fetches the one it needs from lane 4g + ib/2.
                 float fq0[2], fq8[2];
+                uint4 bf2 = make_uint4(0u, 0u, 0u, 0u);
+                float4 dx2 = make_float4(0.f, 0.f, 0.f, 0.f);
                 {
                     const float dw0 = f16_bits_to_f32(h0.x), dw8 = f16_bits_to_f32(h8.x);
 #pragma unroll
@@ -367,8 +376,12 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
                     const int sbl = j * 8 + ib;
                     const uint32_t x0 = *reinterpret_cast<const uint32_t*>(b0p + 8 + 16 * ib + 4 * c);
                     const uint32_t x8 = *reinterpret_cast<const uint32_t*>(b8p + 8 + 16 * ib + 4 * c);
-                    const uint2 bf = actp[sbl * 32];
-                    const float2 dx = *reinterpret_cast<const float2*>(dxp + sbl * 8);
+                    if ((ib & 1) == 0) {  // the B fragments and d_x of sub-blocks ib, ib+1: two 16-byte loads
+                        bf2 = *reinterpret_cast<const uint4*>(act + act_index(sbs + sbl, lane));
+                        dx2 = *reinterpret_cast<const float4*>(dxs + dx_index(sbs + sbl, 2 * c));
+                    }
+                    const uint2 bf = (ib & 1) ? make_uint2(bf2.z, bf2.w) : make_uint2(bf2.x, bf2.y);
+                    const float2 dx = (ib & 1) ? make_float2(dx2.z, dx2.w) : make_float2(dx2.x, dx2.y);
                     const uint32_t xf0 = x0 ^ 0x88888888u, xf8 = x8 ^ 0x88888888u;
                     // Codebook bytes of the two table halves: ah = kv (codes >= 8, else 0), al = -kv (codes
                     // < 8, else 0), so kv = ah - al.  Two s8 x s8 MMAs (both accumulators starting at
