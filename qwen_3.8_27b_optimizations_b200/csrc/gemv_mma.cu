@@ -226,7 +226,7 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
         const int ch0 = nsubs[0] / kStageChunk, ch1 = nsubs[1] / kStageChunk;  // chunks per token
         const int nchunks = (ch0 + ch1) * B;
         // fp32 source (batch <= 2): the fp32 values of all of this warp's chunks are requested first
-        constexpr int kF32Chunks = 3;  // >= 2 slots * (16 * pk / 8) * B / kNCW for pk * B <= kF32MaxPkB
+        constexpr int kF32Chunks = (4 * kF32MaxPkB + kNCW - 1) / kNCW;  // 2 slots * (16 pk / 8) * B / kNCW
         float4 xf[kF32Chunks][2];
         if constexpr (kF32) {
 #pragma unroll
@@ -281,7 +281,7 @@ __device__ __forceinline__ void gemv_mma_body(const CUtensorMap* tmap_p, const G
         } else {
             // Q8_1 source: the words of all of this warp's chunks (at most kQ8Pre) are loaded before
             // any is used, so the staging costs one global round trip instead of one per chunk.
-            constexpr int kQ8Pre = 10;  // >= 2 slots * (16 * pk / 8) * B / kNCW for pk <= 5, B <= 8
+            constexpr int kQ8Pre = (4 * 5 * 8 + kNCW - 1) / kNCW;  // 2 slots * (16 pk / 8) * B / kNCW, pk <= 5, B <= 8
             uint32_t pv[kQ8Pre][3];
 #pragma unroll
             for (int k = 0; k < kQ8Pre; ++k) {
