@@ -118,8 +118,9 @@ __global__ void __cluster_dims__(kNormCtas, 1, 1) __launch_bounds__(kNormWarps *
 // Decode attention for one token at position p = *pos.  One cluster of kChunks CTAs per kv head;
 // CTA c of the cluster takes the positions [c0, c1) = [(p+1)*c/kChunks, (p+1)*(c+1)/kChunks) for all
 // G = q_heads/kv_heads query heads of the group, so every K/V row is read once per group.  Each CTA
-// keeps its own softmax max m_c and sum l_c per head and an unnormalised output o_c; CTA r of the
-// cluster then merges head r over the cluster through distributed shared memory:
+// keeps its own softmax max m_c and sum l_c per head and an unnormalised output o_c, and pushes those
+// of head r into CTA r's shared memory (distributed shared memory stores); after one cluster barrier
+// CTA r merges head r from its own shared memory:
 //   M = max_c m_c,  o = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c.
 // qkv: fp32 [hq + 2*hkv][128] (q heads, then k heads, then v heads) of this token;
 // k_cache / v_cache: f16 [hkv][max_seq][128]; cos/sin: fp32 [max_seq][64].
@@ -168,8 +169,10 @@ __global__ void __cluster_dims__(kChunks, 1, 1) __launch_bounds__(kAttnThreads, 
     __shared__ __align__(16) float qs[G][kHeadDim];
     __shared__ __align__(16) float kn[kHeadDim];
     __shared__ __align__(16) float vn[kHeadDim];
-    __shared__ __align__(16) float oc[G][kHeadDim];     // this CTA's unnormalised output
-    __shared__ float mc[G], lc[G];
+    __shared__ float mc[G], lc[G];                      // this CTA's softmax max and sum per head
+    // CTA r < G owns head r of the group: every CTA c pushes its (m_c, l_c, o_c) of head r here
+    __shared__ float rm[kChunks], rl[kChunks];
+    __shared__ __align__(16) float ro[kChunks][kHeadDim];
     cg::cluster_group cluster = cg::this_cluster();
     const int crank = (int)cluster.block_rank();
     const int kvh = blockIdx.y;
@@ -180,6 +183,9 @@ __global__ void __cluster_dims__(kChunks, 1, 1) __launch_bounds__(kAttnThreads, 
         return;
     }
     const int p = (int)p64;
+    // first phase of a cluster barrier: this CTA has started (its shared memory may receive the other
+    // CTAs' pushes once every CTA has arrived; the wait comes just before the first push)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     const int c0 = (int)((int64_t)(p + 1) * crank / kChunks), c1 = (int)((int64_t)(p + 1) * (crank + 1) / kChunks);
     constexpr int kHalf = kHeadDim / 2;
     // warp w takes positions c0 + w + 8k, kU at a time; lane holds dims 4*lane .. 4*lane+3.  The
@@ -338,32 +344,38 @@ __global__ void __cluster_dims__(kChunks, 1, 1) __launch_bounds__(kAttnThreads, 
         *reinterpret_cast<float4*>(stage + ((size_t)warp * G + j) * kHeadDim + 4 * lane) =
             make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
     __syncthreads();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA of the cluster has started
+    // push this CTA's unnormalised output of head j, and its m_c / l_c, into the owner CTA j
     for (int it = tid; it < G * kHeadDim; it += kAttnThreads) {
         float o = 0.f;
 #pragma unroll
         for (int w2 = 0; w2 < kAttnWarps; ++w2) o += stage[(size_t)w2 * G * kHeadDim + it];
-        oc[it / kHeadDim][it % kHeadDim] = o;
+        const int j = it / kHeadDim;
+        cluster.map_shared_rank(&ro[0][0], j)[crank * kHeadDim + it % kHeadDim] = o;
     }
-    cluster.sync();  // every CTA's m_c, l_c, o_c visible to the cluster
+    if (tid < G) {
+        cluster.map_shared_rank(&rm[0], tid)[crank] = mc[tid];
+        cluster.map_shared_rank(&rl[0], tid)[crank] = lc[tid];
+    }
+    cluster.sync();  // every push has landed; from here on each CTA reads only its own shared memory
     if (crank < G && tid < kHeadDim) {
         float M = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kChunks; ++c) M = fmaxf(M, cluster.map_shared_rank(&mc[0], c)[crank]);
+        for (int c = 0; c < kChunks; ++c) M = fmaxf(M, rm[c]);
         float L = 0.f, o = 0.f;
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
-            const float m = cluster.map_shared_rank(&mc[0], c)[crank];
+            const float m = rm[c];
             if (m == -INFINITY) continue;  // an empty range
             const float w = expf(__fsub_rn(m, M));
-            L = fmaf(w, cluster.map_shared_rank(&lc[0], c)[crank], L);
-            o = fmaf(w, cluster.map_shared_rank(&oc[0][0], c)[crank * kHeadDim + tid], o);
+            L = fmaf(w, rl[c], L);
+            o = fmaf(w, ro[c][tid], o);
         }
         o = __fdiv_rn(o, L);
         const int h = kvh * G + crank;
         if (o_out) o_out[(int64_t)h * kHeadDim + tid] = o;
         q8_1_block_store(o, q8 + ((int64_t)h * (kHeadDim / kQK8) + warp) * kQ8Bytes, lane);
     }
-    cluster.sync();  // keep this CTA's shared memory alive until the cluster has read it
 }
 
 // act = silu(gate) * up for gu [T][2F] (gate columns [0, F), up columns [F, 2F)); Q8_1 blocks
