@@ -140,6 +140,27 @@ void split_ctas(const iq4xs_gemv_problem* p, int count, int64_t B, int total, in
     }
 }
 
+// Batch 2..8: CTAs handed out one at a time to the matrix whose busiest CTA the tensor-core
+// kernel's cost model (gemv_mma_cta_cost) estimates slowest, starting from one each, so that the
+// matrices' last CTAs finish together at the granularity of whole units per warp pair.
+void split_ctas_mma(const iq4xs_gemv_problem* p, int count, int total, int smem_optin, int* out) {
+    double cost[kMaxGroup];
+    int used = 0;
+    for (int i = 0; i < count; ++i) {
+        out[i] = 1;
+        cost[i] = gemv_mma_cta_cost(p[i].K, p[i].N, 1, smem_optin);
+        ++used;
+    }
+    while (used < total) {
+        int best = 0;
+        for (int i = 1; i < count; ++i)
+            if (cost[i] > cost[best]) best = i;
+        ++out[best];
+        cost[best] = gemv_mma_cta_cost(p[best].K, p[best].N, out[best], smem_optin);
+        ++used;
+    }
+}
+
 bool grouped_kernels_take(const iq4xs_gemv_problem* p, int count, int64_t B) {
     for (int i = 0; i < count; ++i) {
         const uint8_t* W = static_cast<const uint8_t*>(p[i].W);
@@ -212,7 +233,10 @@ extern "C" int iq4xs_gemv_grouped(const iq4xs_gemv_problem* problems, int count,
     uint32_t* err = device_error_word();
     const uint32_t lut[4] = {kNegLo0, kNegLo1, kPosHi0, kPosHi1};
     int ctas[kMaxGroup];
-    split_ctas(problems, count, B, std::max(sms, count), ctas);
+    if (B > 1)
+        split_ctas_mma(problems, count, std::max(sms, count), smem_optin, ctas);
+    else
+        split_ctas(problems, count, B, std::max(sms, count), ctas);
 
     // 1. activations -> Q8_1 (one launch for the group)
     GroupQuantParams Q;

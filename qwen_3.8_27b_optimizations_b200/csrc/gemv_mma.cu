@@ -679,6 +679,20 @@ cudaError_t launch_gemv_mma(const uint8_t* W, const uint8_t* q8, float* y, int32
     return cudaLaunchKernelEx(&cfg, reduce_parts_kernel, (const float*)partials, y, parts, BN);
 }
 
+double gemv_mma_cta_cost(int64_t K, int64_t N, int ctas, int smem_optin) {
+    if (K % 512 != 0 || ctas < 1) return 1e300;
+    const int pairs = (int)(K / 512);
+    const int64_t T = (N + 15) / 16;
+    const int pk = choose_pk(pairs, T, ctas, smem_optin);
+    const int parts = (pairs + pk - 1) / pk;
+    const int64_t U = T * parts;
+    int64_t n = std::min<int64_t>(ctas, U);
+    while ((U + n - 1) / n > T) ++n;  // the launcher's bound: a CTA's units span at most two parts
+    const int64_t rounds = ((U + n - 1) / n + kPairs - 1) / kPairs;
+    const double ovh = mma_stages(pk, smem_optin) >= 12 ? 0.35 : 0.75;
+    return (double)rounds * ((double)pk + ovh) + (parts > 1 ? 0.25 : 0.0);
+}
+
 int gemv_mma_grouped_parts(int64_t K, int64_t N, int ctas, int smem_optin) {
     if (K % 512 != 0) return 0;
     const int pairs = (int)(K / 512);

@@ -104,6 +104,10 @@ cudaError_t launch_gemv_rows_grouped(const GroupedProblem* p, int count, cudaStr
                                      const uint32_t lut[4]);
 // K parts the grouped tensor-core launch uses for one matrix given `ctas` CTAs (partial sums when > 1).
 int gemv_mma_grouped_parts(int64_t K, int64_t N, int ctas, int smem_optin);
+// The busiest CTA's estimated time when the tensor-core GEMV runs (K, N) on `ctas` CTAs, in units of
+// one warp pair's super-block pair (choose_pk's cost model: rounds of units per pair x (pk + per-unit
+// overhead)); the grouped planner balances the matrices with it.
+double gemv_mma_cta_cost(int64_t K, int64_t N, int ctas, int smem_optin);
 // Batch 2..8 on the tensor-core kernel (partial sums left in `partials`; the caller adds the parts).
 cudaError_t launch_gemv_mma_grouped(const GroupedProblem* p, int count, int B, cudaStream_t stream, bool pdl,
                                     uint32_t* err, const uint32_t lut[4]);
