@@ -595,6 +595,12 @@ __global__ void __launch_bounds__(32 * (kRowGroupNCW + 1), 1)
 // Warps per row (kw) and sub-block slots per lane (spl) of the row kernel for K at batch B; false when
 // even four warps per row would need more than the lane's register budget (the launch then takes the
 // tensor-core kernel).
+int gemv_rows_per_stage(int64_t K) {
+    int kw = 1, spl = 1;
+    row_split(K, 1, &kw, &spl);
+    return (kRowGroupNCW / kw) * kRowGroupRPW;
+}
+
 bool row_split(int64_t K, int B, int* kw_out, int* spl_out) {
     const int64_t nsb = K / kQK8;
     // the fewest warps per row (1..4, all dividing the 12 consumer warps) that fit the lane budget;

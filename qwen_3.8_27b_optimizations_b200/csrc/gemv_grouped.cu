@@ -7,7 +7,8 @@
 // GEMV launch pays a fixed cost of a few microseconds (launch, the first weight bytes, the tail of
 // the last CTAs) that a 2.8 MB k_proj cannot hide.  Here the matrices share one grid: matrix i gets a
 // contiguous slice of the CTAs in proportion to its estimated time (weight bytes times a measured
-// cost per byte of its shape), so that the whole group ends together.
+// cost of its busiest CTA, as the kernels' own work granularity sees it), so that the whole group
+// ends together.
 //
 //  1. q8_1_grouped_kernel quantises every problem's activations into its slice of the workspace
 //     (q8_1_block_store: the bytes of iq4xs_q8_1_quantize);
@@ -105,50 +106,28 @@ double cost_per_byte(int64_t K, int64_t B) {
     return 1.0 + 0.25 * x;
 }
 
-// CTAs per problem in proportion to its estimated time (weight bytes x cost per byte; largest
-// remainder), at least one each, so that the matrices of the group finish together.
-void split_ctas(const iq4xs_gemv_problem* p, int count, int64_t B, int total, int* out) {
-    double sum = 0.0;
-    double w[kMaxGroup];
-    for (int i = 0; i < count; ++i) {
-        w[i] = (double)p[i].N * (double)p[i].K * cost_per_byte(p[i].K, B);
-        sum += w[i];
-    }
-    int used = 0;
-    double frac[kMaxGroup];
-    for (int i = 0; i < count; ++i) {
-        const double share = sum > 0 ? total * w[i] / sum : 1.0;
-        out[i] = std::max(1, (int)share);
-        frac[i] = share - (int)share;
-        used += out[i];
-    }
-    while (used < total) {  // hand the rest out by largest remainder
-        int best = 0;
-        for (int i = 1; i < count; ++i)
-            if (frac[i] > frac[best]) best = i;
-        ++out[best];
-        frac[best] -= 1.0;
-        ++used;
-    }
-    while (used > total) {  // the minimum of one CTA each overshot: take from the largest
-        int best = 0;
-        for (int i = 1; i < count; ++i)
-            if (out[i] > out[best]) best = i;
-        if (out[best] <= 1) break;
-        --out[best];
-        --used;
-    }
+// Estimated time of the busiest CTA of matrix q on `ctas` CTAs.  Batch 2..8: the tensor-core
+// kernel's own cost model (gemv_mma_cta_cost: whole units per warp pair).  Batch 1: the row kernel
+// streams whole stages of R rows, and a partly filled last stage takes as long as a full one (a
+// warp's rows are computed together), so a CTA costs its stage count x R rows x the matrix's cost
+// per byte.
+double cta_cost(const iq4xs_gemv_problem& q, int64_t B, int ctas, int smem_optin) {
+    if (B > 1) return gemv_mma_cta_cost(q.K, q.N, ctas, smem_optin);
+    const int64_t R = gemv_rows_per_stage(q.K);
+    const int64_t rows = (q.N + ctas - 1) / ctas;
+    const int64_t stages = (rows + R - 1) / R;
+    return (double)(stages * R) * (double)q.K * cost_per_byte(q.K, 1);
 }
 
-// Batch 2..8: CTAs handed out one at a time to the matrix whose busiest CTA the tensor-core
-// kernel's cost model (gemv_mma_cta_cost) estimates slowest, starting from one each, so that the
-// matrices' last CTAs finish together at the granularity of whole units per warp pair.
-void split_ctas_mma(const iq4xs_gemv_problem* p, int count, int total, int smem_optin, int* out) {
+// CTAs handed out one at a time to the matrix whose busiest CTA is estimated slowest (cta_cost),
+// starting from one each, so that the matrices' last CTAs finish together at the granularity the
+// kernels work in.
+void split_ctas_balanced(const iq4xs_gemv_problem* p, int count, int64_t B, int total, int smem_optin, int* out) {
     double cost[kMaxGroup];
     int used = 0;
     for (int i = 0; i < count; ++i) {
         out[i] = 1;
-        cost[i] = gemv_mma_cta_cost(p[i].K, p[i].N, 1, smem_optin);
+        cost[i] = cta_cost(p[i], B, 1, smem_optin);
         ++used;
     }
     while (used < total) {
@@ -156,7 +135,7 @@ void split_ctas_mma(const iq4xs_gemv_problem* p, int count, int total, int smem_
         for (int i = 1; i < count; ++i)
             if (cost[i] > cost[best]) best = i;
         ++out[best];
-        cost[best] = gemv_mma_cta_cost(p[best].K, p[best].N, out[best], smem_optin);
+        cost[best] = cta_cost(p[best], B, out[best], smem_optin);
         ++used;
     }
 }
@@ -233,10 +212,7 @@ extern "C" int iq4xs_gemv_grouped(const iq4xs_gemv_problem* problems, int count,
     uint32_t* err = device_error_word();
     const uint32_t lut[4] = {kNegLo0, kNegLo1, kPosHi0, kPosHi1};
     int ctas[kMaxGroup];
-    if (B > 1)
-        split_ctas_mma(problems, count, std::max(sms, count), smem_optin, ctas);
-    else
-        split_ctas(problems, count, B, std::max(sms, count), ctas);
+    split_ctas_balanced(problems, count, B, std::max(sms, count), smem_optin, ctas);
 
     // 1. activations -> Q8_1 (one launch for the group)
     GroupQuantParams Q;

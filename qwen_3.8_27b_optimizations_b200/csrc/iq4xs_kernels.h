@@ -86,6 +86,8 @@ bool gemv_takes_mma(const uint8_t* W, int64_t K, int B);
 // Row kernel: warps per row (kw) and sub-block slots per lane (spl) for K at batch B; false when K is
 // too long for register-resident activations.
 bool row_split(int64_t K, int B, int* kw_out, int* spl_out);
+// Rows per stage of the batch-1 row kernel at this K.
+int gemv_rows_per_stage(int64_t K);
 
 // Grouped GEMV: several independent matrices of one batch size in one launch, each served by its own
 // slice of the grid (`ctas` CTAs, contiguous block indices), so the launch, ramp and tail are paid once
