@@ -6,9 +6,8 @@
 // own GEMV (patches/0001-gfx1100-mul-mat-custom.patch:278-280, one call per MUL_MAT node).  On B200 a
 // GEMV launch pays a fixed cost of a few microseconds (launch, the first weight bytes, the tail of
 // the last CTAs) that a 2.8 MB k_proj cannot hide.  Here the matrices share one grid: matrix i gets a
-// contiguous slice of the CTAs in proportion to its estimated time (weight bytes times a measured
-// cost of its busiest CTA, as the kernels' own work granularity sees it), so that the whole group
-// ends together.
+// contiguous slice of the CTAs, handed out one at a time to the matrix whose busiest CTA is estimated
+// slowest at the kernels' own work granularity (cta_cost), so that the whole group ends together.
 //
 //  1. q8_1_grouped_kernel quantises every problem's activations into its slice of the workspace
 //     (q8_1_block_store: the bytes of iq4xs_q8_1_quantize);
