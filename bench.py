@@ -320,10 +320,13 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     pre_ms, dec_ms = float(t[0]), float(t[1])
-    coll = None
-    if world > 1 and m.fused_allreduce:
-        # the same model with a separate peer all-reduce kernel after each o_proj / down_proj GEMV
-        m.fused_allreduce = False
+    alt = None
+    form = None
+    if world > 1 and m.peers is not None:
+        form = "fused" if m.fused_allreduce else "collective"
+        # the same model with the other all-reduce form (fused into the GEMVs <-> a separate peer
+        # collective kernel after each o_proj / down_proj GEMV)
+        m.fused_allreduce = not m.fused_allreduce
         m.graph = None
         m.prefill(prompt)
         m.decode(4)                  # re-capture
@@ -335,7 +338,7 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
         torch.cuda.synchronize()
         tc = torch.tensor([ev[0].elapsed_time(ev[1])], dtype=torch.float64, device=dev)
         dist.all_reduce(tc, op=dist.ReduceOp.MAX)
-        coll = round(DECODER_STEPS / (float(tc[0]) * 1e-3), 1)
+        alt = round(DECODER_STEPS / (float(tc[0]) * 1e-3), 1)
     m.release()
     del m
     torch.cuda.empty_cache()
@@ -343,9 +346,10 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
             "unit": "tok/s", "tp": world, "prompt": DECODER_PROMPT, "steps": DECODER_STEPS,
             "prefill_ms": round(pre_ms, 1), "prefill_tok_s": round(DECODER_PROMPT / (pre_ms * 1e-3), 1),
             "decode_ms": round(dec_ms, 1), "build_s": round(build_s, 1), "first_tokens": toks[:8],
-            "allreduce": "fused into the o_proj / down_proj GEMVs (push epilogue + next kernel's prologue)"
-                         if world > 1 else None,
-            "tok_s_separate_allreduce_kernel": coll,
+            "allreduce": {"fused": "fused into the o_proj / down_proj GEMVs (push epilogue + next kernel's prologue)",
+                          "collective": "a peer collective kernel after each o_proj / down_proj GEMV"}.get(form),
+            "tok_s_other_allreduce": ({"form": "collective" if form == "fused" else "fused", "value": alt}
+                                      if alt is not None else None),
             "model": "64 x (hidden 5120, 64x128 q heads, 8 kv heads, SwiGLU 17408), vocab 152064, IQ4_XS "
                      "linear layers, fp32 norms, f16 embeddings and KV cache, random N(0, 0.02) init"}, logits
 

@@ -65,10 +65,13 @@ class TPDecoder:
     """One rank's share of the decoder.  `matmul(W, X, N) -> Y [M][N]` (fp32 X [M][K]) defaults to the
     CUDA kernels; tests on CPU ranks inject a reference."""
 
+    SLOT_AREAS = (3, 4)  # peer areas of the fused all-reduce's slots for o_proj (0) and down_proj (1)
+
     def __init__(self, cfg: DecoderConfig, rank: int = 0, world: int = 1, group=None, seed: int = 0,
                  device="cuda", matmul: Optional[Callable] = None, gen_weights: Optional[Callable] = None,
                  gen_normal: Optional[Callable] = None, fused_decode: Optional[bool] = None,
-                 peer_collectives: Optional[bool] = None, emulate_ranks: int = 1, fused_allreduce: bool = True):
+                 peer_collectives: Optional[bool] = None, emulate_ranks: int = 1,
+                 fused_allreduce: Optional[bool] = None):
         import torch
         from . import sharded
         self.torch = torch
@@ -151,12 +154,20 @@ class TPDecoder:
         if peer_collectives and world > 1:
             from .peer import PeerGroup
             lm_pad = sharded.max_shard_rows(cfg.vocab, world)
-            self.peers = PeerGroup(max(2 * world * D, 8 * lm_pad), areas=3, group=group, device=self.device)
+            # areas: 0 / 1 the collective kernel's o_proj / down_proj, 2 the lm_head all-gather,
+            # 3 / 4 the fused all-reduce's slots (their own areas, so that the two forms can alternate
+            # on one model without a slot word left by the other being read as current)
+            self.peers = PeerGroup(max(2 * world * D, 8 * lm_pad), areas=5, group=group, device=self.device)
         # fused all-reduce (o_proj / down_proj GEMV epilogues push their rows into every rank's slot,
-        # the next kernel's norm prologue sums the slots) instead of a collective kernel per GEMV
+        # the next kernel's norm prologue sums the slots) instead of a collective kernel per GEMV.
+        # Default: fused at 2 ranks, the collective kernel from 4 (measured on B200s, 64-layer C5
+        # decoder: TP2 238 vs 220 tok/s, TP4 197 vs 237 -- every consumer CTA reads world x hidden x 8
+        # bytes of slots, which outgrows the collective kernel's cost as the rank count grows).
+        if fused_allreduce is None:
+            fused_allreduce = world <= 2
         self.fused_allreduce = bool(fused_allreduce) and self.peers is not None
-        if self.fused_allreduce:  # the device descriptors exist before any graph capture
-            for area in (0, 1):
+        if self.peers is not None:  # the device descriptors exist before any graph capture
+            for area in self.SLOT_AREAS:
                 self.peers.slots(area, D)
         self.lm_head = sharded.RowShardedIQ4XS(lm[r0:r1].contiguous(), cfg.vocab, D, group=group, rank=rank,
                                                world=world, local_gemv=self._lm_local if matmul else None,
@@ -324,7 +335,7 @@ class TPDecoder:
         if self.peers is None:
             return self._allreduce(api.gemv_q8_ex(W, q8, K, D, 1, out=out, flags=api.FLAG_OVERLAP_PRECEDING))
         if self.fused_allreduce:
-            slots = self.peers.slots(area, D)
+            slots = self.peers.slots(self.SLOT_AREAS[area], D)
             api.dec_gemv_q8_push(W, q8, K, D, slots, flags=api.FLAG_PDL)
             return _PeerDelta(slots)
         api.gemv_q8_ex(W, q8, K, D, 1, out=self.peers.area(area, D).view(1, D), flags=api.FLAG_OVERLAP_PRECEDING)
@@ -339,7 +350,7 @@ class TPDecoder:
         if self.peers is None:
             return self._allreduce(api.dec_swiglu_gemv(W, gu, self.F, D, out=out, flags=api.FLAG_PDL))
         if self.fused_allreduce:
-            slots = self.peers.slots(1, D)
+            slots = self.peers.slots(self.SLOT_AREAS[1], D)
             api.dec_swiglu_gemv(W, gu, self.F, D, slots=slots, flags=api.FLAG_PDL)
             return _PeerDelta(slots)
         api.dec_swiglu_gemv(W, gu, self.F, D, out=self.peers.area(1, D).view(1, D), flags=api.FLAG_PDL)
