@@ -15,6 +15,9 @@
 //    fresh TMEM accumulator; drain warps load it (tcgen05.ld) and fold the scale in:
 //    acc[row][token] += (sumi * d_x[token]) * (d_w*(ls-32))[row] in fp32 registers.  Four TMEM
 //    accumulators (4 x 128 columns) let the MMA run up to four sub-blocks ahead of the drain.
+//    A drain warp reads its 32 columns of a stage's two accumulators in four 16-column chunks and
+//    issues each chunk's load before the arithmetic of the previous one, so the TMEM load latency
+//    hides behind the scale folding (+4-5% over load-all-then-compute, measured on B200).
 //  * Weights: the IQ4_XS rows as stored, viewed as uint64 [N][K/512 pairs][34] and loaded by TMA
 //    128 rows x one super-block pair (34,816 bytes) at a time.  Converter warps (one thread per row)
 //    expand each 64-wide K chunk to fp16 in the canonical K-major 128-byte-swizzled layout that
@@ -121,6 +124,28 @@ __device__ __forceinline__ uint4 expand_word(uint32_t x, const uint32_t (&lut)[4
     r.z = hadd2_bits(prmt(bhi, 0x64646464u, 0x4140u), kBias);
     r.w = hadd2_bits(prmt(bhi, 0x64646464u, 0x4342u), kBias);
     return r;
+}
+
+// The loaded registers are redefined after the wait, so no use can be scheduled before it.
+__device__ __forceinline__ void regs_after_wait(uint32_t (&v)[16]) {
+    asm volatile("" : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]));
+}
+
+// acc[c0 + j] += (v[j] * d_x[32 cg + c0 + j]) * sw for the 16 columns of one chunk of sub-block h.
+__device__ __forceinline__ void drain_chunk(float (&acc)[32], const uint32_t (&v)[16], int c0, uint32_t sw_base,
+                                            uint32_t sx_base, int s, int h) {
+    const float wsc = lds_f32(sw_base + (uint32_t)(s * kSwBytes + h * kBM * 4));
+    const uint32_t sxa = sx_base + (uint32_t)(s * kActStageBytes + h * kBN * 4 + 4 * c0);
+#pragma unroll
+    for (int c4 = 0; c4 < 4; ++c4) {
+        const uint4 x = lds_u4(sxa + 16u * c4);
+        float t0, t1, t2, t3;
+        mul2(t0, t1, __uint_as_float(v[4 * c4 + 0]), __uint_as_float(v[4 * c4 + 1]), __uint_as_float(x.x), __uint_as_float(x.y));
+        mul2(t2, t3, __uint_as_float(v[4 * c4 + 2]), __uint_as_float(v[4 * c4 + 3]), __uint_as_float(x.z), __uint_as_float(x.w));
+        fma2(acc[c0 + 4 * c4 + 0], acc[c0 + 4 * c4 + 1], t0, t1, wsc, wsc);
+        fma2(acc[c0 + 4 * c4 + 2], acc[c0 + 4 * c4 + 3], t2, t3, wsc, wsc);
+    }
 }
 }  // namespace
 
@@ -319,32 +344,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 go = __shfl_sync(0xFFFFFFFFu, go ? 1 : 0, 0) != 0;
                 if (!go) break;
                 tc_fence_after();
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t v[32];
-                    tmem_ld16(lane_base + (uint32_t)(g * 2 * kBN + h * kBN), *reinterpret_cast<uint32_t(*)[16]>(v));
-                    tmem_ld16(lane_base + (uint32_t)(g * 2 * kBN + h * kBN + 16), *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+                {
+                    // 16-column chunks q = 0..3 (sub-block q >> 1, columns 16*(q & 1)), each load issued
+                    // before the arithmetic of the previous chunk; the pair is released after the last load.
+                    uint32_t va[16], vb[16];
+                    const uint32_t tb = lane_base + (uint32_t)(g * 2 * kBN);
+                    tmem_ld16(tb, va);
                     tmem_wait_ld();
-                    if (h == 1) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&t_empty[g]);
-                    }
-                    {
-                        const float wsc = lds_f32(sw_base + (uint32_t)(s * kSwBytes + h * kBM * 4));
-                        const uint32_t sxa = sx_base + (uint32_t)(s * kActStageBytes + h * kBN * 4);
-#pragma unroll
-                        for (int c4 = 0; c4 < 8; ++c4) {
-                            const uint4 x = lds_u4(sxa + 16u * c4);
-                            float t0, t1, t2, t3;
-                            mul2(t0, t1, __uint_as_float(v[4 * c4 + 0]), __uint_as_float(v[4 * c4 + 1]), __uint_as_float(x.x),
-                                 __uint_as_float(x.y));
-                            mul2(t2, t3, __uint_as_float(v[4 * c4 + 2]), __uint_as_float(v[4 * c4 + 3]), __uint_as_float(x.z),
-                                 __uint_as_float(x.w));
-                            fma2(acc[4 * c4 + 0], acc[4 * c4 + 1], t0, t1, wsc, wsc);
-                            fma2(acc[4 * c4 + 2], acc[4 * c4 + 3], t2, t3, wsc, wsc);
-                        }
-                    }
+                    regs_after_wait(va);
+                    tmem_ld16(tb + 16u, vb);
+                    drain_chunk(acc, va, 0, sw_base, sx_base, s, 0);
+                    tmem_wait_ld();
+                    regs_after_wait(vb);
+                    tmem_ld16(tb + (uint32_t)kBN, va);
+                    drain_chunk(acc, vb, 16, sw_base, sx_base, s, 0);
+                    tmem_wait_ld();
+                    regs_after_wait(va);
+                    tmem_ld16(tb + (uint32_t)kBN + 16u, vb);
+                    drain_chunk(acc, va, 0, sw_base, sx_base, s, 1);
+                    tmem_wait_ld();
+                    regs_after_wait(vb);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&t_empty[g]);
+                    drain_chunk(acc, vb, 16, sw_base, sx_base, s, 1);
                 }
                 fence_generic_async_smem();  // this warp's reads of d_x and the weight scales before the refill
                 __syncwarp();
