@@ -321,9 +321,10 @@ def decoder_run(P, dev, rank: int, world: int, barrier):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     pre_ms, dec_ms = float(t[0]), float(t[1])
     alt = None
-    form = None
-    if world > 1 and m.peers is not None:
-        form = "fused" if m.fused_allreduce else "collective"
+    form = ("fused" if m.fused_allreduce else "collective") if world > 1 and m.peers is not None else None
+    # the other form is timed at 2 and 4 ranks; at 8 only the default (the collective kernel: every
+    # consumer CTA of the fused form reads world x hidden x 8 bytes of slots, already slower at 4)
+    if form is not None and world <= 4:
         # the same model with the other all-reduce form (fused into the GEMVs <-> a separate peer
         # collective kernel after each o_proj / down_proj GEMV)
         m.fused_allreduce = not m.fused_allreduce
