@@ -125,6 +125,48 @@ def test_validation_before_any_launch(pkg):
     assert L.iq4xs_quantize_weights(FAKE, FAKE, 4, 300, None) == 2
 
 
+def test_grouped_validation_and_workspace(pkg):
+    """iq4xs_gemv_grouped on the host: the workspace covers every problem's Q8_1 activations (each
+    slice 256-byte aligned), an invalid group sizes to 0, and bad arguments are rejected before any
+    launch (nothing here reaches the device)."""
+    L = pkg.lib()
+    Prob = pkg.api.GemvProblem
+
+    def group(items):
+        a = (Prob * max(len(items), 9))()
+        for i, it in enumerate(items):
+            a[i] = Prob(*it)
+        return C.cast(a, C.c_void_p), a
+
+    layer = [(5120, 8192), (5120, 1024), (5120, 1024), (8192, 5120), (5120, 34816), (17408, 5120)]
+    ok, keep = group([(FAKE, FAKE, FAKE, K, N) for K, N in layer])
+    for B in range(1, 9):
+        need = L.iq4xs_gemv_grouped_workspace_bytes(ok, 6, B)
+        q8 = sum((L.iq4xs_q8_1_bytes(K, B) + 255) // 256 * 256 for K, _ in layer)
+        assert need >= q8 and need % 256 == 0
+    assert L.iq4xs_gemv_grouped_workspace_bytes(ok, 0, 1) == 0
+    assert L.iq4xs_gemv_grouped_workspace_bytes(ok, 9, 1) == 0     # more than IQ4XS_MAX_GROUP
+    assert L.iq4xs_gemv_grouped_workspace_bytes(ok, 6, 0) == 0
+    assert L.iq4xs_gemv_grouped_workspace_bytes(ok, 6, 9) == 0
+    odd, k1 = group([(FAKE, FAKE, FAKE, 500, 64)])
+    assert L.iq4xs_gemv_grouped_workspace_bytes(odd, 1, 1) == 0
+
+    big = 1 << 40
+    need = L.iq4xs_gemv_grouped_workspace_bytes(ok, 6, 2)
+    assert L.iq4xs_gemv_grouped(None, 1, 1, FAKE, big, 0, None) == 1
+    assert L.iq4xs_gemv_grouped(ok, 0, 1, FAKE, big, 0, None) == 1
+    assert L.iq4xs_gemv_grouped(ok, 9, 1, FAKE, big, 0, None) == 2      # more than IQ4XS_MAX_GROUP
+    assert L.iq4xs_gemv_grouped(ok, 6, 9, FAKE, big, 0, None) == 2      # batch > 8
+    assert L.iq4xs_gemv_grouped(odd, 1, 1, FAKE, big, 0, None) == 2     # K % 256
+    null_w, k2 = group([(None, FAKE, FAKE, 5120, 64)])
+    assert L.iq4xs_gemv_grouped(null_w, 1, 1, FAKE, big, 0, None) == 1
+    mis_w, k3 = group([(FAKE + 4, FAKE, FAKE, 5120, 64)])
+    assert L.iq4xs_gemv_grouped(mis_w, 1, 1, FAKE, big, 0, None) == 3   # W not 8-byte aligned
+    assert L.iq4xs_gemv_grouped(ok, 6, 2, None, need, 0, None) == 1     # no workspace
+    assert L.iq4xs_gemv_grouped(ok, 6, 2, FAKE, need - 1, 0, None) == 4
+    assert L.iq4xs_gemv_grouped(ok, 6, 2, FAKE + 16, need, 0, None) == 3  # workspace not 256-byte aligned
+
+
 def test_ggml_can_handle(pkg):
     assert pkg.custom_gemv_iq4xs_can_handle(5120, 17408, 1)
     assert pkg.custom_gemv_iq4xs_can_handle(4096, 4096, 8)
