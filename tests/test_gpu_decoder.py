@@ -63,7 +63,7 @@ def test_fused_decode_layers_vs_torch_ops(pkg):
     assert pkg.device_error() == 0
 
 
-@pytest.mark.parametrize("ranks", [2, 4])
+@pytest.mark.parametrize("ranks", [2, 4, 8])
 def test_rank_emulation_on_one_gpu(pkg, ranks):
     """TPDecoder(emulate_ranks=R) on one GPU (the reference a TP-R run is compared with bit for bit on
     several GPUs): the o_proj / down_proj GEMVs of the decode step run as R K slices added in rank
